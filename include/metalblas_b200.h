@@ -1,0 +1,151 @@
+/*
+ * metalblas_b200 — C ABI of the B200 (sm_100a) matmul / addmm / bmm hot path.
+ *
+ * Every entry point takes plain device pointers, element strides and a CUDA
+ * stream (passed as void* so no CUDA header is needed to bind it).  The library
+ * never allocates or frees caller memory; scratch space for split-K partials is
+ * passed in by the caller (see mb_gemm_workspace_size).  All launches are
+ * asynchronous on the given stream.
+ *
+ * The reference (Isalia20/metalBLAS) has no C ABI: its "FFI" is the set of
+ * launchable Metal pipelines returned by metalblas/kernels.py, called as
+ *   fn(*buffers, packed_dims, [bias, int2 bstride, float beta, float alpha],
+ *      [int4 batch], threads=..., group_size=...)
+ * from metalblas/float_dispatch.py:770-775, :945-947, :1087,
+ * metalblas/integer_dispatch.py:108-117, :135-146 and
+ * metalblas/complex_dispatch.py:60-66, :114.  Each entry point below names the
+ * reference interface it replaces.
+ */
+#ifndef METALBLAS_B200_H
+#define METALBLAS_B200_H
+
+#include <stdint.h>
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MB_ABI_VERSION 1
+
+/* Element types.  Output dtype == input dtype (torch semantics, reference
+ * metalblas/dispatch.py:106-114 and integer_dispatch.py:13-19). */
+typedef enum mb_dtype {
+    MB_F32 = 0, MB_F16 = 1, MB_BF16 = 2,
+    MB_C64 = 3,            /* interleaved float2 (torch.complex64)            */
+    MB_C32 = 4,            /* interleaved half2  (torch.complex32 / chalf)    */
+    MB_I8 = 5, MB_U8 = 6, MB_I16 = 7, MB_I32 = 8, MB_I64 = 9
+} mb_dtype;
+
+/* Backend selection; names follow the reference's backend= strings
+ * (metalblas/float_dispatch.py:802-852). */
+typedef enum mb_backend {
+    MB_BACKEND_AUTO = 0,   /* tile table picks                                  */
+    MB_BACKEND_GEMV = 1,   /* "gemv": bandwidth kernels, needs M==1 or N==1     */
+    MB_BACKEND_TC   = 2,   /* "mpp_tensor": tcgen05/TMEM tensor-core GEMM       */
+    MB_BACKEND_SIMT = 3    /* "simd" (and "mpp" fallback): CUDA-core FFMA/IMAD  */
+} mb_backend;
+
+/* Status codes; the Python layer maps them onto the reference's exception types
+ * (AssertionError / ValueError / NotImplementedError / RuntimeError). */
+typedef enum mb_status {
+    MB_OK = 0,
+    MB_ERR_INVALID = 1,        /* bad shape / stride / pointer / tile      -> ValueError/AssertionError */
+    MB_ERR_UNSUPPORTED = 2,    /* dtype or layout not handled by the forced backend -> NotImplementedError */
+    MB_ERR_LAUNCH = 3,         /* CUDA launch or driver error               -> RuntimeError */
+    MB_ERR_DEVICE_TIMEOUT = 4, /* a bounded device-side wait ran out        -> RuntimeError */
+    MB_ERR_WORKSPACE = 5       /* workspace missing or too small            -> ValueError */
+} mb_status;
+
+/*
+ * One (batched) GEMM with optional fused epilogue:
+ *   C[b] = alpha * (op(A[b]) @ op(B[b])) + beta * bias[b]          (epilogue)
+ *   C[b] = A[b] @ B[b]                                            (no epilogue)
+ * Element (m,k) of A[b] is A[b*sA + m*a_rs + k*a_cs]; B(k,n) is
+ * B[b*sB + k*b_rs + n*b_cs]; C(m,n) is C[b*sC + m*c_rs + n*c_cs]; bias(m,n) is
+ * bias[b*bias_bs + m*bias_rs + n*bias_cs].  All strides are in ELEMENTS and
+ * 64-bit (the reference packs int32 offsets, metalblas/dispatch.py:12-16).
+ * A batch stride of 0 broadcasts that operand (reference keeps stride 0,
+ * metalblas/dispatch.py:96-103, float_dispatch.py:1071-1087).
+ * Row-major A is a_cs==1, a_rs==lda; column-major ("trans_a") is a_rs==1,
+ * a_cs==lda (reference _unit_lead, metalblas/dispatch.py:23-30).  Other stride
+ * pairs are accepted and read in place by the CUDA-core kernel.
+ * conj_a / conj_b conjugate a complex operand on load (the reference
+ * materialises it, metalblas/complex_dispatch.py:25-30).
+ * Epilogue semantics follow metalblas/shaders/mb_epi.h:16-26: with
+ * alpha_nz==0 the product is not used, with beta_nz==0 bias is never read
+ * (so NaN in bias cannot leak).  Float/complex epilogues compute in fp32
+ * (complex: complex multiply, shaders/complex_pack.h:43-55); integer epilogues
+ * compute in the accumulator type with two's-complement wrap using ialpha/ibeta.
+ */
+typedef struct mb_gemm_desc {
+    int32_t dtype;          /* mb_dtype */
+    int32_t backend;        /* mb_backend */
+    int64_t M, N, K, batch;
+    const void *A;
+    const void *B;
+    void *C;
+    int64_t a_rs, a_cs, sA;
+    int64_t b_rs, b_cs, sB;
+    int64_t c_rs, c_cs, sC;
+    int32_t conj_a, conj_b;
+    /* epilogue */
+    int32_t epilogue;       /* 0: plain product; 1: alpha/beta/bias epilogue */
+    int32_t alpha_nz, beta_nz;
+    int32_t _pad0;
+    const void *bias;       /* same dtype as C */
+    int64_t bias_rs, bias_cs, bias_bs;
+    double alpha_re, alpha_im, beta_re, beta_im;   /* float / complex scalars */
+    int64_t ialpha, ibeta;                         /* integer scalars         */
+    /* plan overrides (0 = planner decides) */
+    int32_t tile_n;         /* TC: N-tile of the tcgen05 kernel (16..256)     */
+    int32_t split_k;        /* TC/GEMV: number of K splits                    */
+    int32_t swap_ab;        /* TC: -1 never, 0 planner decides, 1 force Cᵀ=BᵀAᵀ */
+    int32_t _pad1;
+    /* caller-owned scratch for split-K partials; must be zero-filled before
+     * its first use; kernels leave the counter region zeroed again. */
+    void *workspace;
+    int64_t workspace_bytes;
+} mb_gemm_desc;
+
+/* Fill *d with defaults (backend AUTO, alpha=beta=1, no epilogue, batch=1). */
+void mb_gemm_desc_init(mb_gemm_desc *d);
+
+/* Launch one (batched) GEMM on `stream` (a cudaStream_t; NULL = legacy default).
+ * Replaces the mpp_tensor / mpp / simd / int_gemm / gemv_t / gemv_nt / gemv_bt /
+ * splitk_gemm+splitk_reduce / complex split+combine launches of
+ * metalblas/float_dispatch.py:745-852, 897-956, 1049-1091,
+ * metalblas/integer_dispatch.py:92-150 and metalblas/complex_dispatch.py:33-129. */
+int mb_gemm(const mb_gemm_desc *d, void *stream);
+
+/* Bytes of workspace mb_gemm needs for this descriptor's plan (0 if none).
+ * Replaces the split-K partial pool of metalblas/float_dispatch.py:183-192. */
+int64_t mb_gemm_workspace_size(const mb_gemm_desc *d);
+
+/* Describe the plan mb_gemm would run, as text ("tc bn=256 split=1 swap=0 ...").
+ * Replaces the plan/tile lookups of metalblas/float_dispatch.py:484-505 (the
+ * tile that _gemm_plan returns). Returns the string length written. */
+int mb_plan_query(const mb_gemm_desc *d, char *buf, int buflen);
+
+/* Text of the last error raised on this thread. */
+const char *mb_last_error_string(void);
+
+/* Device status word of the current device: 0, or MB_ERR_DEVICE_TIMEOUT if a
+ * bounded device-side wait ran out since the last mb_device_status_clear.
+ * Synchronises the current device.  The reference has no device-side waits. */
+int mb_device_status(void);
+void mb_device_status_clear(void);
+
+/* Testing hook for the bounded-wait path: launches a kernel that waits on an
+ * mbarrier nothing will complete, with the given limit in microseconds; the
+ * kernel must give up, record MB_ERR_DEVICE_TIMEOUT and return. */
+int mb_debug_wait_timeout(int64_t limit_us, void *stream);
+
+/* Library ABI version (MB_ABI_VERSION) and the SM arch it was built for (100). */
+int mb_abi_version(void);
+int mb_built_sm(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* METALBLAS_B200_H */

@@ -1,0 +1,247 @@
+// Bandwidth-bound matrix-vector kernels (the M==1 / N==1 products).
+//
+// Two orientations cover every unit-stride layout, as in the reference:
+//  * gemv_cols: y[r] = sum_k x[k] * W[k*ld + r]   (vector times a matrix whose
+//    output index is contiguous) — the B200 form of gemv_t
+//    (metalblas/shaders/gemv_t.h:15-99): lanes own 16-byte column vectors, the
+//    warps of a CTA split K, partial sums meet in shared memory, and, when the
+//    column count alone cannot fill 148 SMs, K is also split across CTAs with
+//    fp32 partials in a caller-provided workspace reduced by the last CTA to
+//    arrive (an atomic ticket, no waiting).
+//  * gemv_rows: y[r] = sum_k W[r*ld + k] * x[k]   (rows contiguous along K) —
+//    the B200 form of gemv_nt (metalblas/shaders/gemv_nt.h:16-101): one warp
+//    per row, 16-byte loads, a warp-shuffle reduction.
+// Orientation is chosen by the host like the reference's _dispatch_gemv
+// (metalblas/dispatch.py:49-70).  Loads of W use ld.global.nc with L1
+// no-allocate (W is streamed once); x is small and re-read from L1/L2.
+#pragma once
+#include "mb_common.cuh"
+
+namespace mb {
+
+struct GemvParams {
+  const void *W, *X, *bias;
+  void *Y;
+  int64_t R, K;          // outputs, reduction length
+  int64_t w_ld;          // cols: W(k,r) = W[k*w_ld + r];  rows: W(r,k) = W[r*w_ld + k]
+  int64_t x_s;           // x(k) = X[k*x_s]
+  int64_t y_s;           // y(r) = Y[r*y_s]
+  int64_t bias_s;        // bias(r) = bias[r*bias_s]
+  int64_t batch, sW, sX, sY, sBias;
+  int conj_w, conj_x;
+  int x_vec;             // rows kernel: x is unit-stride and 16-byte aligned in every batch
+  EpiScalars epi;
+  int ksplit;            // cols kernel: CTAs along K
+  int64_t kchunk;        // cols kernel: rows of W per CTA
+  void *ws;              // ksplit*batch*R accumulators
+  unsigned *tickets;     // batch * ceil(R / cols_per_cta) counters, zero on entry and exit
+};
+
+template <class T, int VEC>
+struct VecLoad {
+  union U { uint4 u; T v[VEC]; };
+  static_assert(sizeof(T) * VEC == 16, "16-byte vectors");
+  __device__ static __forceinline__ void load(const T *p, T (&out)[VEC]) {
+    U x;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(x.u.x), "=r"(x.u.y), "=r"(x.u.z), "=r"(x.u.w) : "l"(p));
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) out[i] = x.v[i];
+  }
+};
+
+template <class Acc> __device__ __forceinline__ void acc_add(Acc &a, const Acc &b) { a += b; }
+template <> __device__ __forceinline__ void acc_add<cf32>(cf32 &a, const cf32 &b) { a.re += b.re; a.im += b.im; }
+
+template <class Acc> __device__ __forceinline__ Acc shfl_xor(Acc v, int m) { return __shfl_xor_sync(0xffffffffu, v, m); }
+template <> __device__ __forceinline__ cf32 shfl_xor<cf32>(cf32 v, int m) {
+  return cf32{__shfl_xor_sync(0xffffffffu, v.re, m), __shfl_xor_sync(0xffffffffu, v.im, m)};
+}
+
+template <class T>
+__device__ __forceinline__ void gemv_store(const GemvParams &p, int64_t b, int64_t r, typename Elem<T>::acc v) {
+  if (p.epi.enabled) {
+    const T *bias = (const T *)p.bias + b * p.sBias + r * p.bias_s;
+    v = EpiOps<T>::apply(v, bias, p.epi);
+  }
+  ((T *)p.Y)[b * p.sY + r * p.y_s] = Elem<T>::store(v);
+}
+
+// ---------------------------------------------------------------------------
+// gemv_cols: grid (ceil(R / (32*VEC)), ksplit, batch), NW warps per CTA.
+// VEC == 1 is the unaligned fallback (scalar loads).
+template <class T, int VEC, int NW>
+__global__ void __launch_bounds__(NW * 32) gemv_cols_kernel(const GemvParams p) {
+  using E = Elem<T>;
+  using Acc = typename E::acc;
+  constexpr int COLS = 32 * VEC;
+  __shared__ Acc red[NW][COLS];
+  __shared__ unsigned s_ticket;
+
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t b = blockIdx.z;
+  const int64_t c0 = (int64_t)blockIdx.x * COLS + lane * VEC;
+  const int64_t kbeg = (int64_t)blockIdx.y * p.kchunk;
+  const int64_t kend = min(p.K, kbeg + p.kchunk);
+  const T *W = (const T *)p.W + b * p.sW;
+  const T *X = (const T *)p.X + b * p.sX;
+
+  Acc acc[VEC];
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) acc[i] = E::zero();
+
+  const bool full = (c0 + VEC <= p.R);
+  constexpr int U = 4;  // independent 16-byte loads in flight per thread
+  int64_t k = kbeg + warp;
+  bool done = false;
+  if constexpr (VEC > 1) {
+    if (full) {
+      done = true;
+    for (; k + (U - 1) * NW < kend; k += U * NW) {
+      T w[U][VEC];
+      Acc xv[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) VecLoad<T, VEC>::load(W + (k + u * NW) * p.w_ld + c0, w[u]);
+#pragma unroll
+      for (int u = 0; u < U; ++u) xv[u] = E::load(X[(k + u * NW) * p.x_s], p.conj_x);
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) E::mad(acc[i], xv[u], E::load(w[u][i], p.conj_w));
+    }
+    for (; k < kend; k += NW) {
+      T w[VEC];
+      VecLoad<T, VEC>::load(W + k * p.w_ld + c0, w);
+      const Acc xv = E::load(X[k * p.x_s], p.conj_x);
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) E::mad(acc[i], xv, E::load(w[i], p.conj_w));
+    }
+    }
+  }
+  if (!done) {
+    for (; k < kend; k += NW) {
+      const Acc xv = E::load(X[k * p.x_s], p.conj_x);
+#pragma unroll
+      for (int i = 0; i < VEC; ++i)
+        if (c0 + i < p.R) E::mad(acc[i], xv, E::load(W[k * p.w_ld + c0 + i], p.conj_w));
+    }
+  }
+
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) red[warp][lane * VEC + i] = acc[i];
+  __syncthreads();
+
+  const int64_t cbase = (int64_t)blockIdx.x * COLS;
+  if (p.ksplit == 1) {
+    for (int c = threadIdx.x; c < COLS; c += NW * 32) {
+      if (cbase + c >= p.R) continue;
+      Acc s = red[0][c];
+#pragma unroll
+      for (int w = 1; w < NW; ++w) acc_add(s, red[w][c]);
+      gemv_store<T>(p, b, cbase + c, s);
+    }
+    return;
+  }
+
+  // Split K across CTAs: publish this CTA's partial, take a ticket; the CTA
+  // that draws the last ticket sums all partials in split order (deterministic)
+  // and resets the ticket for the next launch.
+  Acc *ws = (Acc *)p.ws + (b * p.ksplit + blockIdx.y) * p.R;
+  for (int c = threadIdx.x; c < COLS; c += NW * 32) {
+    if (cbase + c >= p.R) continue;
+    Acc s = red[0][c];
+#pragma unroll
+    for (int w = 1; w < NW; ++w) acc_add(s, red[w][c]);
+    ws[cbase + c] = s;
+  }
+  __threadfence();
+  __syncthreads();
+  unsigned *ticket = p.tickets + b * gridDim.x + blockIdx.x;
+  if (threadIdx.x == 0) s_ticket = atomicAdd(ticket, 1u);
+  __syncthreads();
+  if (s_ticket != (unsigned)(p.ksplit - 1)) return;
+  __threadfence();
+  const Acc *ws0 = (const Acc *)p.ws + b * p.ksplit * p.R;
+  for (int c = threadIdx.x; c < COLS; c += NW * 32) {
+    const int64_t r = cbase + c;
+    if (r >= p.R) continue;
+    Acc s = E::zero();
+    for (int sp = 0; sp < p.ksplit; ++sp) {
+      Acc v;
+      if constexpr (sizeof(Acc) == 8 && !E::is_int) {
+        float2 f = __ldcg((const float2 *)(ws0 + sp * p.R + r));
+        v = *reinterpret_cast<Acc *>(&f);
+      } else {
+        v = __ldcg(ws0 + sp * p.R + r);
+      }
+      acc_add(s, v);
+    }
+    gemv_store<T>(p, b, r, s);
+  }
+  if (threadIdx.x == 0) *ticket = 0u;
+}
+
+// ---------------------------------------------------------------------------
+// gemv_rows: one warp per output row, grid (ceil(R / NW), 1, batch).
+// VEC == 1 is the unaligned fallback.
+template <class T, int VEC, int NW>
+__global__ void __launch_bounds__(NW * 32) gemv_rows_kernel(const GemvParams p) {
+  using E = Elem<T>;
+  using Acc = typename E::acc;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t b = blockIdx.z;
+  const int64_t r = (int64_t)blockIdx.x * NW + warp;
+  if (r >= p.R) return;
+  const T *W = (const T *)p.W + b * p.sW + r * p.w_ld;
+  const T *X = (const T *)p.X + b * p.sX;
+
+  Acc acc = E::zero();
+  int64_t k = (int64_t)lane * VEC;
+  if constexpr (VEC > 1) {
+    constexpr int U = 4;
+    constexpr int64_t STEP = 32 * VEC;
+    const int64_t kvec_end = (p.K / VEC) * VEC;  // vector part
+    const bool x_vec = p.x_vec != 0;
+    for (; k + (U - 1) * STEP + VEC <= kvec_end; k += U * STEP) {
+      T w[U][VEC];
+#pragma unroll
+      for (int u = 0; u < U; ++u) VecLoad<T, VEC>::load(W + k + u * STEP, w[u]);
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int64_t kk = k + u * STEP;
+        if (x_vec) {
+          T xv[VEC];
+          const T *xp = X + kk;
+          union { uint4 q; T v[VEC]; } xu;
+          xu.q = __ldg(reinterpret_cast<const uint4 *>(xp));
+#pragma unroll
+          for (int i = 0; i < VEC; ++i) xv[i] = xu.v[i];
+#pragma unroll
+          for (int i = 0; i < VEC; ++i) E::mad(acc, E::load(w[u][i], p.conj_w), E::load(xv[i], p.conj_x));
+        } else {
+#pragma unroll
+          for (int i = 0; i < VEC; ++i)
+            E::mad(acc, E::load(w[u][i], p.conj_w), E::load(X[(kk + i) * p.x_s], p.conj_x));
+        }
+      }
+    }
+    for (; k + VEC <= kvec_end; k += STEP) {
+      T w[VEC];
+      VecLoad<T, VEC>::load(W + k, w);
+#pragma unroll
+      for (int i = 0; i < VEC; ++i)
+        E::mad(acc, E::load(w[i], p.conj_w), E::load(X[(k + i) * p.x_s], p.conj_x));
+    }
+    // scalar tail beyond the last full vector
+    for (int64_t kk = kvec_end + lane; kk < p.K; kk += 32)
+      E::mad(acc, E::load(W[kk], p.conj_w), E::load(X[kk * p.x_s], p.conj_x));
+  } else {
+    for (int64_t kk = lane; kk < p.K; kk += 32)
+      E::mad(acc, E::load(W[kk], p.conj_w), E::load(X[kk * p.x_s], p.conj_x));
+  }
+#pragma unroll
+  for (int m = 16; m >= 1; m >>= 1) acc_add(acc, shfl_xor(acc, m));
+  if (lane == 0) gemv_store<T>(p, b, r, acc);
+}
+
+}  // namespace mb

@@ -1,0 +1,644 @@
+// C ABI of metalblas_b200: validation, the sm_100a plan (tile table), TMA
+// descriptor construction and kernel launches.  One translation unit so that
+// the device status word has a single definition.
+//
+// Plan rules (B200 replacement of the reference's planners):
+//  * M==1 or N==1 with a unit-stride matrix -> GEMV kernels, oriented like
+//    _dispatch_gemv (metalblas/dispatch.py:49-70) and the fast paths of
+//    metalblas/float_dispatch.py:745-764;
+//  * bf16/fp16/int8/uint8 whose operands TMA can address -> tcgen05 kernel
+//    (mpp_tensor_gemm / splitk / gemv_bt / int_gemm-for-8-bit replacement);
+//    thin M runs as Cᵀ = Bᵀ·Aᵀ (the reference's flipt/sgpipe/gemv_bt ideas,
+//    metalblas/float_dispatch.py:249-366, folded into one kernel);
+//    N-tile and split-K come from a wave-quantisation cost model instead of
+//    the Apple tile heuristics (metalblas/float_dispatch.py:613-655);
+//  * everything else -> CUDA-core kernel (simd_gemm / int_gemm / complex
+//    products replacement).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <type_traits>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/metalblas_b200.h"
+#include "mb_common.cuh"
+#include "simt_gemm.cuh"
+#include "gemv.cuh"
+#include "tc_gemm.cuh"
+
+using namespace mb;
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char *fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+
+int cuda_check(cudaError_t e, const char *what) {
+  if (e == cudaSuccess) return MB_OK;
+  return fail(MB_ERR_LAUNCH, "%s: %s", what, cudaGetErrorString(e));
+}
+
+int elem_size(int dt) {
+  switch (dt) {
+    case MB_F32: return 4;
+    case MB_F16: case MB_BF16: return 2;
+    case MB_C64: return 8;
+    case MB_C32: return 4;
+    case MB_I8: case MB_U8: return 1;
+    case MB_I16: return 2;
+    case MB_I32: return 4;
+    case MB_I64: return 8;
+  }
+  return 0;
+}
+bool acc_is_8byte(int dt) { return dt == MB_C64 || dt == MB_C32 || dt == MB_I64; }
+bool is_tc_dtype(int dt) { return dt == MB_BF16 || dt == MB_F16 || dt == MB_I8 || dt == MB_U8; }
+
+int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+int64_t round_up(int64_t a, int64_t b) { return ceil_div(a, b) * b; }
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+struct DevInfo {
+  int sms = 148;
+  bool ok = false;
+};
+DevInfo g_dev[64];
+std::mutex g_dev_mu;
+
+int current_device(int *dev) {
+  return cuda_check(cudaGetDevice(dev), "cudaGetDevice");
+}
+int num_sms(int dev) {
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  if (dev < 0 || dev >= 64) return 148;
+  if (!g_dev[dev].ok) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && n > 0) g_dev[dev].sms = n;
+    g_dev[dev].ok = true;
+  }
+  return g_dev[dev].sms;
+}
+
+unsigned long long wait_timeout_ns() {
+  static unsigned long long v = [] {
+    const char *s = getenv("METALBLAS_WAIT_TIMEOUT_MS");
+    long long ms = s ? atoll(s) : 2000;
+    if (ms <= 0) ms = 2000;
+    return (unsigned long long)ms * 1000000ull;
+  }();
+  return v;
+}
+
+// A strided 2-D operand: element (r, c) at base[r*rs + c*cs].  Extent-1
+// dimensions get a stride that makes the operand look unit-stride / aligned,
+// since that stride never moves the address.
+void normalize(int64_t rows, int64_t cols, int64_t &rs, int64_t &cs) {
+  if (rows <= 1 && cols <= 1) { rs = std::max<int64_t>(cols, 1); cs = 1; return; }
+  if (rows <= 1) { if (cs == 1) rs = round_up(cols, 16); else rs = 1; }
+  if (cols <= 1) { if (rs == 1) cs = round_up(rows, 16); else cs = 1; }
+}
+
+// --------------------------------------------------------------------------- plan
+enum PlanKind { PK_EMPTY = 0, PK_GEMV_COLS, PK_GEMV_ROWS, PK_TC, PK_SIMT };
+
+struct Plan {
+  int kind = PK_EMPTY;
+  // GEMV
+  GemvParams g{};
+  int vec = 1;
+  int64_t gemv_ctas_x = 0;
+  // TC (operands already swapped when swap == 1)
+  int swap = 0, bn = 0, splits = 1;
+  int64_t tiles_m = 0, tiles_n = 0, kb_total = 0, kb_per_split = 0;
+  int a_mn = 0, b_mn = 0;
+  // shared
+  int64_t ws_bytes = 0, ws_tickets_off = 0;
+  std::string why;
+};
+
+// Working copy of the descriptor with normalised strides.
+struct Op {
+  int dt;
+  int64_t M, N, K, batch;
+  const void *A, *B;
+  void *C;
+  int64_t a_rs, a_cs, sA, b_rs, b_cs, sB, c_rs, c_cs, sC;
+  int conj_a, conj_b;
+  const void *bias;
+  int64_t bias_rs, bias_cs, bias_bs;
+};
+
+Op make_op(const mb_gemm_desc *d) {
+  Op o{};
+  o.dt = d->dtype; o.M = d->M; o.N = d->N; o.K = d->K; o.batch = d->batch;
+  o.A = d->A; o.B = d->B; o.C = d->C;
+  o.a_rs = d->a_rs; o.a_cs = d->a_cs; o.sA = d->sA;
+  o.b_rs = d->b_rs; o.b_cs = d->b_cs; o.sB = d->sB;
+  o.c_rs = d->c_rs; o.c_cs = d->c_cs; o.sC = d->sC;
+  o.conj_a = d->conj_a; o.conj_b = d->conj_b;
+  o.bias = d->bias; o.bias_rs = d->bias_rs; o.bias_cs = d->bias_cs; o.bias_bs = d->bias_bs;
+  if (o.batch <= 1) { o.sA = o.sB = o.sC = 0; o.bias_bs = 0; }
+  normalize(o.M, o.K, o.a_rs, o.a_cs);
+  normalize(o.K, o.N, o.b_rs, o.b_cs);
+  return o;
+}
+
+Op swapped(const Op &o) {
+  Op s = o;
+  s.M = o.N; s.N = o.M;
+  s.A = o.B; s.B = o.A;
+  s.a_rs = o.b_cs; s.a_cs = o.b_rs; s.sA = o.sB;
+  s.b_rs = o.a_cs; s.b_cs = o.a_rs; s.sB = o.sA;
+  s.c_rs = o.c_cs; s.c_cs = o.c_rs;
+  s.bias_rs = o.bias_cs; s.bias_cs = o.bias_rs;
+  s.conj_a = o.conj_b; s.conj_b = o.conj_a;
+  return s;
+}
+
+// Can TMA feed this operand pair?  Sets a_mn / b_mn.
+bool tc_layout_ok(const Op &o, int bn, int &a_mn, int &b_mn, std::string *why) {
+  const int esz = elem_size(o.dt);
+  auto bad = [&](const char *w) { if (why) *why = w; return false; };
+  if (o.M >= (1ll << 31) || o.N >= (1ll << 31) || o.K >= (1ll << 31) || o.K < 1) return bad("extent");
+  if (!aligned16(o.A) || !aligned16(o.B)) return bad("base not 16B aligned");
+  if (o.batch > 1) {
+    if ((o.sA * esz) % 16 || (o.sB * esz) % 16) return bad("batch stride not 16B multiple");
+    if (o.sA < 0 || o.sB < 0) return bad("negative batch stride");
+  }
+  if (o.a_cs == 1 && o.a_rs >= o.K && (o.a_rs * esz) % 16 == 0) a_mn = 0;
+  else if (o.a_rs == 1 && o.a_cs >= o.M && (o.a_cs * esz) % 16 == 0) a_mn = 1;
+  else return bad("A layout");
+  if (o.b_rs == 1 && o.b_cs >= o.K && (o.b_cs * esz) % 16 == 0) b_mn = 0;
+  else if (o.b_cs == 1 && o.b_rs >= o.N && (o.b_rs * esz) % 16 == 0 && bn * esz >= 128) b_mn = 1;
+  else return bad("B layout");
+  return true;
+}
+
+// Cycles per K-block of a 128 x BN tile: tensor time vs. shared-memory operand
+// bandwidth (128 B/clk/SM), four UMMA K-steps per block.
+double kblock_cycles(int bn) { return 4.0 * std::max(bn / 2.0, 32.0 + bn / 4.0); }
+
+void choose_tc_tile(const Op &o, int sms, int force_bn, int force_split, bool have_ws, Plan &pl) {
+  const int esz = elem_size(o.dt);
+  const int64_t BK = 128 / esz;
+  const int64_t kb_total = ceil_div(o.K, BK);
+  static const int bns[] = {16, 32, 64, 128, 256};
+  double best = 1e300;
+  for (int bn : bns) {
+    if (force_bn && bn != force_bn) continue;
+    int am, bm;
+    if (!tc_layout_ok(o, bn, am, bm, nullptr)) continue;
+    if (!force_bn && bn > 16 && round_up(o.N, 16) <= bn / 2) continue;  // a smaller tile already covers N
+    const int64_t tiles = o.batch * ceil_div(o.M, 128) * ceil_div(o.N, bn);
+    int max_split = have_ws ? (int)std::min<int64_t>(kb_total, 32) : 1;
+    for (int s = 1; s <= max_split; ++s) {
+      if (force_split && s != force_split) continue;
+      const int64_t kbp = ceil_div(kb_total, s);
+      const int64_t seff = ceil_div(kb_total, kbp);
+      if (seff != s && !force_split) continue;
+      const int64_t units = tiles * seff;
+      const int64_t waves = ceil_div(units, sms);
+      double unit = kbp * kblock_cycles(bn) + 2.0 * bn + (seff > 1 ? 12.0 * seff * bn : 0.0);
+      // memory floor: operands streamed at ~22 B/clk per active SM
+      const double active = (double)std::min<int64_t>(units, sms);
+      const double bytes = (double)(o.M * o.K * (o.sA ? o.batch : 1) + o.N * o.K * (o.sB ? o.batch : 1)) * esz;
+      const double mem = bytes / (22.0 * active * (units > sms ? 1.0 : 1.0));
+      const double t = std::max(waves * unit, mem) * (1.0 + 0.002 * seff);
+      if (t < best) {
+        best = t;
+        pl.bn = bn; pl.splits = (int)seff; pl.a_mn = am; pl.b_mn = bm;
+        pl.tiles_m = ceil_div(o.M, 128); pl.tiles_n = ceil_div(o.N, bn);
+        pl.kb_total = kb_total; pl.kb_per_split = kbp;
+      }
+    }
+  }
+}
+
+// Fill pl for the TC path on operands o (possibly swapped); false if TMA can't.
+bool plan_tc(const Op &o, int sms, const mb_gemm_desc *d, bool have_ws, Plan &pl) {
+  pl.bn = 0;
+  choose_tc_tile(o, sms, d->tile_n, d->split_k, have_ws, pl);
+  if (!pl.bn) return false;
+  pl.kind = PK_TC;
+  const int64_t tiles = o.batch * pl.tiles_m * pl.tiles_n;
+  if (pl.splits > 1) {
+    pl.ws_tickets_off = round_up(tiles * pl.splits * 128 * pl.bn * 4, 256);
+    pl.ws_bytes = pl.ws_tickets_off + tiles * 4 * 4;
+  }
+  return true;
+}
+
+bool plan_gemv(const Op &o, int sms, const mb_gemm_desc *d, bool have_ws, Plan &pl) {
+  GemvParams g{};
+  int kind = 0;
+  if (o.M == 1) {
+    // y[n] = sum_k A(0,k) B(k,n): W = B
+    g.R = o.N; g.K = o.K; g.W = o.B; g.X = o.A; g.x_s = o.a_cs; g.y_s = o.c_cs; g.bias_s = o.bias_cs;
+    g.sW = o.sB; g.sX = o.sA; g.conj_w = o.conj_b; g.conj_x = o.conj_a;
+    if (o.b_cs == 1) { kind = PK_GEMV_COLS; g.w_ld = o.b_rs; }
+    else if (o.b_rs == 1) { kind = PK_GEMV_ROWS; g.w_ld = o.b_cs; }
+  } else if (o.N == 1) {
+    // y[m] = sum_k A(m,k) B(k,0): W = A
+    g.R = o.M; g.K = o.K; g.W = o.A; g.X = o.B; g.x_s = o.b_rs; g.y_s = o.c_rs; g.bias_s = o.bias_rs;
+    g.sW = o.sA; g.sX = o.sB; g.conj_w = o.conj_a; g.conj_x = o.conj_b;
+    if (o.a_cs == 1) { kind = PK_GEMV_ROWS; g.w_ld = o.a_rs; }
+    else if (o.a_rs == 1) { kind = PK_GEMV_COLS; g.w_ld = o.a_cs; }
+  }
+  if (!kind) return false;
+  g.Y = o.C; g.bias = o.bias; g.batch = o.batch; g.sY = o.sC; g.sBias = o.bias_bs;
+  const int esz = elem_size(o.dt);
+  const int vmax = 16 / esz;
+  const bool wvec = aligned16(g.W) && (g.w_ld % vmax == 0) && (o.batch <= 1 || (g.sW % vmax == 0));
+  pl.vec = wvec ? vmax : 1;
+  g.x_vec = (g.x_s == 1 && aligned16(g.X) && (o.batch <= 1 || g.sX % vmax == 0)) ? 1 : 0;
+  g.ksplit = 1;
+  g.kchunk = std::max<int64_t>(g.K, 1);
+  if (kind == PK_GEMV_COLS) {
+    const int64_t cols_per_cta = 32 * pl.vec;
+    const int64_t ctas_x = ceil_div(g.R, cols_per_cta);
+    pl.gemv_ctas_x = ctas_x;
+    const int64_t want = 4 * (int64_t)sms;  // CTAs wanted in flight
+    int64_t ks = d->split_k > 0 ? d->split_k : ceil_div(want, ctas_x * o.batch);
+    ks = std::max<int64_t>(1, std::min<int64_t>(ks, ceil_div(g.K, 64)));  // >= 64 rows per CTA
+    if (ks > 65535) ks = 65535;
+    if (ks > 1 && !have_ws) ks = 1;
+    if (ks > 1) {
+      g.kchunk = ceil_div(g.K, ks);
+      ks = ceil_div(g.K, g.kchunk);
+    }
+    g.ksplit = (int)ks;
+    if (ks > 1) {
+      const int64_t accb = acc_is_8byte(o.dt) ? 8 : 4;
+      pl.ws_tickets_off = round_up(ks * o.batch * g.R * accb, 256);
+      pl.ws_bytes = pl.ws_tickets_off + o.batch * ctas_x * 4;
+    }
+  }
+  pl.kind = kind;
+  pl.g = g;
+  return true;
+}
+
+int make_plan(const mb_gemm_desc *d, const Op &o, int sms, bool have_ws, Plan &pl) {
+  if (o.M == 0 || o.N == 0 || o.batch == 0) { pl.kind = PK_EMPTY; return MB_OK; }
+  const int be = d->backend;
+  if (be == MB_BACKEND_GEMV) {
+    if (!(o.M == 1 || o.N == 1)) return fail(MB_ERR_INVALID, "gemv backend requires M==1 or N==1");
+    if (o.K == 0) { pl.kind = PK_SIMT; return MB_OK; }
+    if (plan_gemv(o, sms, d, have_ws, pl)) return MB_OK;
+    pl.kind = PK_SIMT;  // no unit stride: CUDA-core kernel reads it in place
+    return MB_OK;
+  }
+  if (be == MB_BACKEND_SIMT || o.K == 0) { pl.kind = PK_SIMT; return MB_OK; }
+  if (be == MB_BACKEND_TC) {
+    if (!is_tc_dtype(o.dt)) return fail(MB_ERR_UNSUPPORTED, "tensor-core backend supports bf16/fp16/int8/uint8 only");
+    const bool want_swap = d->swap_ab == 1 || (d->swap_ab == 0 && o.M < 128 && o.N > o.M);
+    if (want_swap && d->swap_ab != -1) {
+      Op s = swapped(o);
+      if (plan_tc(s, sms, d, have_ws, pl)) { pl.swap = 1; return MB_OK; }
+    }
+    if (d->swap_ab != 1 && plan_tc(o, sms, d, have_ws, pl)) { pl.swap = 0; return MB_OK; }
+    return fail(MB_ERR_UNSUPPORTED, "tensor-core backend: operands not TMA-addressable (need a unit stride, "
+                                    "16-byte aligned base and leading/batch strides)");
+  }
+  // AUTO
+  if ((o.M == 1 || o.N == 1) && plan_gemv(o, sms, d, have_ws, pl)) return MB_OK;
+  if (is_tc_dtype(o.dt)) {
+    const bool want_swap = d->swap_ab == 1 || (d->swap_ab == 0 && o.M < 128 && o.N > o.M);
+    if (want_swap && d->swap_ab != -1) {
+      Op s = swapped(o);
+      if (plan_tc(s, sms, d, have_ws, pl)) { pl.swap = 1; return MB_OK; }
+    }
+    if (d->swap_ab != 1 && plan_tc(o, sms, d, have_ws, pl)) { pl.swap = 0; return MB_OK; }
+  }
+  pl.kind = PK_SIMT;
+  return MB_OK;
+}
+
+int validate(const mb_gemm_desc *d) {
+  if (!d) return fail(MB_ERR_INVALID, "null descriptor");
+  if (d->dtype < MB_F32 || d->dtype > MB_I64) return fail(MB_ERR_UNSUPPORTED, "dtype %d not supported", d->dtype);
+  if (d->M < 0 || d->N < 0 || d->K < 0 || d->batch < 0) return fail(MB_ERR_INVALID, "negative extent");
+  if (d->backend < MB_BACKEND_AUTO || d->backend > MB_BACKEND_SIMT) return fail(MB_ERR_INVALID, "unknown backend %d", d->backend);
+  if (d->tile_n && (d->tile_n % 16 || d->tile_n < 16 || d->tile_n > 256 || (d->tile_n & (d->tile_n - 1))))
+    return fail(MB_ERR_INVALID, "tile_n must be one of 16, 32, 64, 128, 256");
+  if (d->split_k < 0 || d->split_k > 65535) return fail(MB_ERR_INVALID, "split_k out of range");
+  const bool empty = d->M == 0 || d->N == 0 || d->batch == 0;
+  if (!empty) {
+    if (!d->C) return fail(MB_ERR_INVALID, "null C");
+    if (d->K > 0 && (!d->A || !d->B)) return fail(MB_ERR_INVALID, "null A or B");
+    if (d->epilogue && d->beta_nz && !d->bias) return fail(MB_ERR_INVALID, "beta != 0 needs a bias pointer");
+  }
+  return MB_OK;
+}
+
+EpiScalars make_epi(const mb_gemm_desc *d) {
+  EpiScalars e{};
+  e.enabled = d->epilogue ? 1 : 0;
+  e.alpha_nz = d->epilogue ? (d->alpha_nz ? 1 : 0) : 1;
+  e.beta_nz = d->epilogue ? (d->beta_nz ? 1 : 0) : 0;
+  e.alpha_re = (float)d->alpha_re; e.alpha_im = (float)d->alpha_im;
+  e.beta_re = (float)d->beta_re; e.beta_im = (float)d->beta_im;
+  e.ialpha = d->ialpha; e.ibeta = d->ibeta;
+  return e;
+}
+
+// --------------------------------------------------------------------------- launches
+template <class T>
+int launch_simt(const Op &o, const EpiScalars &e, cudaStream_t st) {
+  SimtParams p{};
+  p.A = o.A; p.B = o.B; p.C = o.C; p.bias = o.bias;
+  p.M = o.M; p.N = o.N; p.K = o.K; p.batch = o.batch;
+  p.a_rs = o.a_rs; p.a_cs = o.a_cs; p.sA = o.sA;
+  p.b_rs = o.b_rs; p.b_cs = o.b_cs; p.sB = o.sB;
+  p.c_rs = o.c_rs; p.c_cs = o.c_cs; p.sC = o.sC;
+  p.bias_rs = o.bias_rs; p.bias_cs = o.bias_cs; p.bias_bs = o.bias_bs;
+  p.conj_a = o.conj_a; p.conj_b = o.conj_b; p.epi = e;
+  using Acc = typename Elem<T>::acc;
+  if constexpr (sizeof(Acc) == 4) {
+    constexpr int BM = 128, BN = 128;
+    dim3 grid((unsigned)ceil_div(o.N, BN), (unsigned)ceil_div(o.M, BM), (unsigned)std::min<int64_t>(o.batch, 65535));
+    if (grid.y > 65535) return fail(MB_ERR_INVALID, "M too large for the CUDA-core kernel");
+    simt_gemm_kernel<T, BM, BN, 8, 8, 8><<<grid, 256, 0, st>>>(p);
+  } else {
+    constexpr int BM = 64, BN = 64;
+    dim3 grid((unsigned)ceil_div(o.N, BN), (unsigned)ceil_div(o.M, BM), (unsigned)std::min<int64_t>(o.batch, 65535));
+    if (grid.y > 65535) return fail(MB_ERR_INVALID, "M too large for the CUDA-core kernel");
+    simt_gemm_kernel<T, BM, BN, 16, 4, 4><<<grid, 256, 0, st>>>(p);
+  }
+  return cuda_check(cudaGetLastError(), "simt_gemm launch");
+}
+
+template <class T>
+int launch_gemv(const Plan &pl, const EpiScalars &e, void *ws, cudaStream_t st) {
+  GemvParams g = pl.g;
+  g.epi = e;
+  constexpr int NW = 8;
+  constexpr int V = 16 / sizeof(T);
+  if (g.ksplit > 1) {
+    g.ws = ws;
+    g.tickets = reinterpret_cast<unsigned *>(reinterpret_cast<char *>(ws) + pl.ws_tickets_off);
+  }
+  const unsigned gz = (unsigned)std::min<int64_t>(g.batch, 65535);
+  if (g.batch > 65535) return fail(MB_ERR_INVALID, "batch too large for GEMV");
+  if (pl.kind == PK_GEMV_COLS) {
+    dim3 grid((unsigned)pl.gemv_ctas_x, (unsigned)g.ksplit, gz);
+    if (pl.vec > 1) gemv_cols_kernel<T, V, NW><<<grid, NW * 32, 0, st>>>(g);
+    else gemv_cols_kernel<T, 1, NW><<<dim3((unsigned)ceil_div(g.R, 32), (unsigned)g.ksplit, gz), NW * 32, 0, st>>>(g);
+  } else {
+    dim3 grid((unsigned)ceil_div(g.R, NW), 1, gz);
+    if (grid.x > 2147483647u) return fail(MB_ERR_INVALID, "too many rows");
+    if (pl.vec > 1) gemv_rows_kernel<T, V, NW><<<grid, NW * 32, 0, st>>>(g);
+    else gemv_rows_kernel<T, 1, NW><<<grid, NW * 32, 0, st>>>(g);
+  }
+  return cuda_check(cudaGetLastError(), "gemv launch");
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+CUtensorMapDataType tma_dtype(int dt) {
+  switch (dt) {
+    case MB_BF16: return CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    case MB_F16: return CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    default: return CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  }
+}
+
+// 3-D tiled map {inner, outer, batch} with SWIZZLE_128B.
+int encode_map(CUtensorMap *m, int dt, const void *base, int64_t inner, int64_t outer, int64_t batch,
+               int64_t outer_stride_el, int64_t batch_stride_el, int box_inner, int box_outer) {
+  auto enc = get_encode();
+  if (!enc) return fail(MB_ERR_LAUNCH, "cuTensorMapEncodeTiled unavailable");
+  const int esz = elem_size(dt);
+  cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)outer, (cuuint64_t)std::max<int64_t>(batch, 1)};
+  int64_t ostr = outer_stride_el * esz;
+  int64_t bstr = batch_stride_el * esz;
+  if (batch <= 1 || bstr == 0) bstr = round_up(std::max<int64_t>(ostr * outer, 16), 16);
+  cuuint64_t strides[2] = {(cuuint64_t)ostr, (cuuint64_t)bstr};
+  cuuint32_t box[3] = {(cuuint32_t)box_inner, (cuuint32_t)box_outer, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(m, tma_dtype(dt), 3, const_cast<void *>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(MB_ERR_LAUNCH, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return MB_OK;
+}
+
+template <class T, int BN>
+int launch_tc_bn(const Op &o, const Plan &pl, const EpiScalars &e, void *ws, int sms, cudaStream_t st) {
+  using C_ = tc::Cfg<BN, sizeof(T)>;
+  constexpr int ESZ = sizeof(T);
+  constexpr int BK = C_::BK;
+  tc::TcParams p;
+  memset(&p, 0, sizeof(p));
+  int rc;
+  const int64_t bA = o.sA ? o.batch : 1, bB = o.sB ? o.batch : 1;
+  if (!pl.a_mn) rc = encode_map(&p.tmA, o.dt, o.A, o.K, o.M, bA, o.a_rs, o.sA, BK, tc::BM);
+  else rc = encode_map(&p.tmA, o.dt, o.A, o.M, o.K, bA, o.a_cs, o.sA, 128 / ESZ, BK);
+  if (rc) return rc;
+  if (!pl.b_mn) rc = encode_map(&p.tmB, o.dt, o.B, o.K, o.N, bB, o.b_cs, o.sB, BK, BN);
+  else rc = encode_map(&p.tmB, o.dt, o.B, o.N, o.K, bB, o.b_rs, o.sB, 128 / ESZ, BK);
+  if (rc) return rc;
+  p.M = (int)o.M; p.N = (int)o.N; p.K = (int)o.K; p.batch = (int)o.batch;
+  p.a_mn = pl.a_mn; p.b_mn = pl.b_mn;
+  p.a_bcast = o.sA == 0; p.b_bcast = o.sB == 0;
+  p.tiles_m = (int)pl.tiles_m; p.tiles_n = (int)pl.tiles_n;
+  p.splits = pl.splits; p.kb_total = (int)pl.kb_total; p.kb_per_split = (int)pl.kb_per_split;
+  const int64_t units = o.batch * pl.tiles_m * pl.tiles_n * pl.splits;
+  if (units >= (1ll << 31)) return fail(MB_ERR_INVALID, "too many tiles");
+  p.num_units = (int)units;
+  p.group_m = 16;
+  p.C = o.C; p.c_rs = o.c_rs; p.c_cs = o.c_cs; p.sC = o.sC;
+  p.bias = o.bias; p.bias_rs = o.bias_rs; p.bias_cs = o.bias_cs; p.bias_bs = o.bias_bs;
+  p.epi = e;
+  p.c_vec = (o.c_cs == 1 && aligned16(o.C) && (o.c_rs * ESZ) % 16 == 0 && (o.batch <= 1 || (o.sC * ESZ) % 16 == 0)) ? 1 : 0;
+  if (pl.splits > 1) {
+    p.ws = ws;
+    p.tickets = reinterpret_cast<unsigned *>(reinterpret_cast<char *>(ws) + pl.ws_tickets_off);
+  }
+  p.timeout_ns = wait_timeout_ns();
+  auto kern = tc::tc_gemm_kernel<T, BN>;
+  static int attr_done[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+    rc = cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C_::SMEM_BYTES),
+                    "cudaFuncSetAttribute");
+    if (rc) return rc;
+    attr_done[dev] = 1;
+  }
+  const int grid = (int)std::min<int64_t>(units, sms);
+  kern<<<grid, tc::NUM_THREADS, C_::SMEM_BYTES, st>>>(p);
+  return cuda_check(cudaGetLastError(), "tc_gemm launch");
+}
+
+template <class T>
+int launch_tc(const Op &o, const Plan &pl, const EpiScalars &e, void *ws, int sms, cudaStream_t st) {
+  switch (pl.bn) {
+    case 16: return launch_tc_bn<T, 16>(o, pl, e, ws, sms, st);
+    case 32: return launch_tc_bn<T, 32>(o, pl, e, ws, sms, st);
+    case 64: return launch_tc_bn<T, 64>(o, pl, e, ws, sms, st);
+    case 128: return launch_tc_bn<T, 128>(o, pl, e, ws, sms, st);
+    case 256: return launch_tc_bn<T, 256>(o, pl, e, ws, sms, st);
+  }
+  return fail(MB_ERR_INVALID, "bad tile_n %d", pl.bn);
+}
+
+template <class F>
+int by_dtype(int dt, F &&f) {
+  switch (dt) {
+    case MB_F32: return f((float *)nullptr);
+    case MB_F16: return f((__half *)nullptr);
+    case MB_BF16: return f((__nv_bfloat16 *)nullptr);
+    case MB_C64: return f((float2 *)nullptr);
+    case MB_C32: return f((__half2 *)nullptr);
+    case MB_I8: return f((int8_t *)nullptr);
+    case MB_U8: return f((uint8_t *)nullptr);
+    case MB_I16: return f((int16_t *)nullptr);
+    case MB_I32: return f((int32_t *)nullptr);
+    case MB_I64: return f((int64_t *)nullptr);
+  }
+  return fail(MB_ERR_UNSUPPORTED, "dtype");
+}
+
+template <class T> struct IsTc { static constexpr bool v = false; };
+template <> struct IsTc<__half> { static constexpr bool v = true; };
+template <> struct IsTc<__nv_bfloat16> { static constexpr bool v = true; };
+template <> struct IsTc<int8_t> { static constexpr bool v = true; };
+template <> struct IsTc<uint8_t> { static constexpr bool v = true; };
+
+int plan_for(const mb_gemm_desc *d, Plan &pl, Op &o, int &sms) {
+  int rc = validate(d);
+  if (rc) return rc;
+  int dev = 0;
+  rc = current_device(&dev);
+  if (rc) return rc;
+  sms = num_sms(dev);
+  o = make_op(d);
+  const bool have_ws = d->workspace != nullptr || d->workspace_bytes < 0;  // <0: size query
+  return make_plan(d, o, sms, have_ws, pl);
+}
+
+}  // namespace
+
+// =========================================================================== C ABI
+extern "C" {
+
+void mb_gemm_desc_init(mb_gemm_desc *d) {
+  if (!d) return;
+  memset(d, 0, sizeof(*d));
+  d->batch = 1;
+  d->alpha_re = 1.0; d->beta_re = 1.0;
+  d->ialpha = 1; d->ibeta = 1;
+  d->alpha_nz = 1; d->beta_nz = 1;
+}
+
+int64_t mb_gemm_workspace_size(const mb_gemm_desc *d) {
+  if (!d) return 0;
+  mb_gemm_desc q = *d;
+  q.workspace = nullptr;
+  q.workspace_bytes = -1;  // plan as if a workspace were available
+  Plan pl; Op o; int sms;
+  if (plan_for(&q, pl, o, sms)) return 0;
+  return pl.ws_bytes;
+}
+
+int mb_plan_query(const mb_gemm_desc *d, char *buf, int buflen) {
+  Plan pl; Op o; int sms;
+  int rc = plan_for(d, pl, o, sms);
+  if (rc) return -rc;
+  char tmp[256];
+  switch (pl.kind) {
+    case PK_EMPTY: snprintf(tmp, sizeof(tmp), "empty"); break;
+    case PK_GEMV_COLS: snprintf(tmp, sizeof(tmp), "gemv_cols vec=%d ksplit=%d", pl.vec, pl.g.ksplit); break;
+    case PK_GEMV_ROWS: snprintf(tmp, sizeof(tmp), "gemv_rows vec=%d", pl.vec); break;
+    case PK_TC:
+      snprintf(tmp, sizeof(tmp), "tc bn=%d split=%d swap=%d a_mn=%d b_mn=%d tiles=%lldx%lld ws=%lld", pl.bn,
+               pl.splits, pl.swap, pl.a_mn, pl.b_mn, (long long)pl.tiles_m, (long long)pl.tiles_n,
+               (long long)pl.ws_bytes);
+      break;
+    default: snprintf(tmp, sizeof(tmp), "simt"); break;
+  }
+  const int n = (int)strlen(tmp);
+  if (buf && buflen > 0) {
+    strncpy(buf, tmp, (size_t)buflen - 1);
+    buf[buflen - 1] = 0;
+  }
+  return n;
+}
+
+int mb_gemm(const mb_gemm_desc *d, void *stream) {
+  Plan pl; Op o; int sms;
+  int rc = plan_for(d, pl, o, sms);
+  if (rc) return rc;
+  if (pl.kind == PK_EMPTY) return MB_OK;
+  if (pl.ws_bytes > 0 && (d->workspace == nullptr || d->workspace_bytes < pl.ws_bytes))
+    return fail(MB_ERR_WORKSPACE, "workspace of %lld bytes required", (long long)pl.ws_bytes);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const EpiScalars e = make_epi(d);
+  return by_dtype(d->dtype, [&](auto *tag) -> int {
+    using T = std::remove_pointer_t<decltype(tag)>;
+    switch (pl.kind) {
+      case PK_GEMV_COLS:
+      case PK_GEMV_ROWS: return launch_gemv<T>(pl, e, d->workspace, st);
+      case PK_TC:
+        if constexpr (IsTc<T>::v) return launch_tc<T>(pl.swap ? swapped(o) : o, pl, e, d->workspace, sms, st);
+        else return fail(MB_ERR_UNSUPPORTED, "tensor-core path for non-TC dtype");
+      default: return launch_simt<T>(o, e, st);
+    }
+  });
+}
+
+const char *mb_last_error_string(void) { return g_err.c_str(); }
+
+int mb_device_status(void) {
+  int rc = cuda_check(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+  if (rc) return rc;
+  int v = 0;
+  rc = cuda_check(cudaMemcpyFromSymbol(&v, g_mb_status, sizeof(int)), "read status");
+  if (rc) return rc;
+  return v;
+}
+
+void mb_device_status_clear(void) {
+  int z = 0;
+  cudaMemcpyToSymbol(g_mb_status, &z, sizeof(int));
+}
+
+int mb_debug_wait_timeout(int64_t limit_us, void *stream) {
+  if (limit_us <= 0 || limit_us > 10000000) return fail(MB_ERR_INVALID, "limit_us out of range");
+  tc::wait_timeout_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>((unsigned long long)limit_us * 1000ull);
+  return cuda_check(cudaGetLastError(), "wait_timeout launch");
+}
+
+int mb_abi_version(void) { return MB_ABI_VERSION; }
+int mb_built_sm(void) { return 100; }
+
+}  // extern "C"

@@ -1,0 +1,522 @@
+// tcgen05 / TMEM / TMA tensor-core GEMM for bf16, fp16, int8 and uint8.
+//
+// B200 replacement for the reference's Apple tensor-unit kernel
+// mpp_tensor_gemm (metalblas/shaders/mpp_tensor.h:58-142: tiled GEMM, fp32
+// accumulate, transposes via strides, batch via tgid.z + int4 strides, fused
+// addmm epilogue in MB_STORE_TILE :38-55), of its split-K sibling
+// (metalblas/shaders/splitk.h:21-82) and of the thin-M streaming kernel gemv_bt
+// (metalblas/shaders/gemv_bt.h:47-269), which here is the same kernel run on
+// Cᵀ = Bᵀ·Aᵀ so that the thin dimension becomes the UMMA N (16..64).
+//
+// Structure (one CTA per SM, persistent over work units):
+//   warp 0      TMA producer: cp.async.bulk.tensor 3-D loads (no multicast)
+//               into a STAGES-deep ring of 128B-swizzled shared-memory tiles,
+//               completion tracked by mbarrier transaction counts.
+//   warp 1      allocates TMEM, and one elected lane issues tcgen05.mma
+//               (M=128, N=BN, K=16 for 16-bit / 32 for 8-bit) into one of two
+//               TMEM accumulators, releasing each smem stage with
+//               tcgen05.commit -> empty barrier.
+//   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns per warp, apply
+//               alpha/beta/bias (mb_epi semantics), convert, store; or, for a
+//               split-K unit, publish fp32/int32 partials and let the last CTA
+//               to draw a ticket reduce them in split order.
+// The two TMEM accumulators let the epilogue of tile i overlap the mainloop of
+// tile i+1.
+//
+// Operand layouts: each operand may be K-major or MN-major in global memory;
+// TMA copies it into the matching canonical SWIZZLE_128B layout and the UMMA
+// instruction descriptor's major bits say which.  Tile edges in M, N and K are
+// zero-filled by TMA (out-of-bounds fill), and the epilogue masks stores.
+//
+// Every mbarrier wait is bounded by a %globaltimer deadline; a wait that runs
+// out records MB_ERR_DEVICE_TIMEOUT in g_mb_status, raises a CTA-wide abort
+// flag so every role leaves its loop, drains what it issued (bounded), frees
+// TMEM and returns.  Nothing traps.
+#pragma once
+#include <cuda.h>
+#include "mb_common.cuh"
+
+namespace mb {
+namespace tc {
+
+constexpr int BM = 128;                 // UMMA M (cta_group::1)
+constexpr int NUM_THREADS = 192;        // 6 warps
+constexpr int SMEM_BUDGET = 200 * 1024; // operand ring budget (bytes)
+
+struct TcParams {
+  CUtensorMap tmA;   // UMMA-A operand (rows of C), 3-D {inner, outer, batch}
+  CUtensorMap tmB;   // UMMA-B operand (cols of C)
+  int M, N, K, batch;
+  int a_mn, b_mn;        // operand is MN-major in global memory
+  int a_bcast, b_bcast;  // batch stride 0: always load batch 0
+  int tiles_m, tiles_n, splits, kb_total, kb_per_split;
+  int num_units, group_m;
+  void *C;
+  int64_t c_rs, c_cs, sC;
+  const void *bias;
+  int64_t bias_rs, bias_cs, bias_bs;
+  EpiScalars epi;
+  int c_vec;             // c_cs == 1 and every row start is 16-byte aligned
+  void *ws;              // split-K partials: num_tiles * splits * BM * BN * 4 bytes
+  unsigned *tickets;     // four per output tile (one per epilogue warp), zero on entry and exit
+  unsigned long long timeout_ns;
+};
+
+template <int BN, int ESZ>
+struct Cfg {
+  static constexpr int BK = 128 / ESZ;          // one 128-byte swizzle row of K
+  static constexpr int UMMA_K = 32 / ESZ;       // K per tcgen05.mma
+  static constexpr int KSTEPS = BK / UMMA_K;    // 4
+  static constexpr int A_BYTES = BM * 128;
+  static constexpr int B_BYTES = BN * 128;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES_RAW = SMEM_BUDGET / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
+  static constexpr int ACC_COLS = BN;           // fp32/s32: one column per N
+  static constexpr int TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
+  static constexpr int BAR_BYTES = (2 * STAGES + 4 + 1) * 8;
+  static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + BAR_BYTES + 16;
+  static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N for M=128");
+  static_assert(STAGES >= 2, "need a pipeline");
+};
+
+// ---------------------------------------------------------------------------
+// PTX wrappers
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: true when the phase with `parity` completed; false on abort
+// (another role gave up) or deadline (this one gives up and raises abort).
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort_flag,
+                                          unsigned long long timeout_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 63) == 0) {
+      if (*abort_flag) return false;
+      if (globaltimer_ns() - t0 > timeout_ns) {
+        *abort_flag = 1;
+        atomicExch(&g_mb_status, 4 /*MB_ERR_DEVICE_TIMEOUT*/);
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map, uint32_t bar, int c0, int c1,
+                                            int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap *map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+template <int ESZ>
+__device__ __forceinline__ void umma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accum) {
+  if constexpr (ESZ == 2) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accum)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accum)
+        : "memory");
+  }
+}
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+// 32 lanes x 32 consecutive 32-bit TMEM columns -> 32 registers per thread.
+__device__ __forceinline__ void tmem_ld_x32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_x16(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor, SWIZZLE_128B, sm100 version bits.
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+// Instruction descriptor: D f32 (f16 kind) or s32 (i8 kind), operand formats,
+// major-ness, N>>3 at bit 17, M>>4 at bit 24.
+template <class T> struct UFmt;
+template <> struct UFmt<__half> { static constexpr uint32_t d = 1, ab = 0; };
+template <> struct UFmt<__nv_bfloat16> { static constexpr uint32_t d = 1, ab = 1; };
+template <> struct UFmt<uint8_t> { static constexpr uint32_t d = 2, ab = 0; };
+template <> struct UFmt<int8_t> { static constexpr uint32_t d = 2, ab = 1; };
+
+template <class T, int BN>
+__device__ __forceinline__ uint32_t make_idesc(int a_mn, int b_mn) {
+  return (UFmt<T>::d << 4) | (UFmt<T>::ab << 7) | (UFmt<T>::ab << 10) | ((uint32_t)a_mn << 15) |
+         ((uint32_t)b_mn << 16) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+struct Unit {
+  int b, tm, tn, s, tile;
+};
+__device__ __forceinline__ Unit decode_unit(const TcParams &p, int u) {
+  Unit r;
+  r.s = u % p.splits;
+  const int t = u / p.splits;
+  r.tile = t;
+  const int per_batch = p.tiles_m * p.tiles_n;
+  r.b = t / per_batch;
+  const int q = t % per_batch;
+  const int per_group = p.group_m * p.tiles_n;
+  const int g = q / per_group;
+  const int first_m = g * p.group_m;
+  const int gsz = min(p.tiles_m - first_m, p.group_m);
+  const int w = q % per_group;
+  r.tm = first_m + w % gsz;
+  r.tn = w / gsz;
+  return r;
+}
+
+template <class T>
+__device__ __forceinline__ typename Elem<T>::acc acc_from_bits(uint32_t bits) {
+  if constexpr (Elem<T>::is_int) return bits;
+  else return __uint_as_float(bits);
+}
+
+// Store 32 consecutive columns of one output row (or fewer at the right edge).
+template <class T>
+__device__ __forceinline__ void store_row_chunk(const TcParams &p, int b, int m, int n0, int ncols,
+                                                const uint32_t (&r)[32]) {
+  using E = Elem<T>;
+  T *C = (T *)p.C + (int64_t)b * p.sC;
+  const T *bias = (const T *)p.bias + (p.epi.enabled ? (int64_t)b * p.bias_bs : 0);
+  T out[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    typename E::acc v = acc_from_bits<T>(r[j]);
+    if (j < ncols && p.epi.enabled && n0 + j < p.N)
+      v = EpiOps<T>::apply(v, bias + (int64_t)m * p.bias_rs + (int64_t)(n0 + j) * p.bias_cs, p.epi);
+    out[j] = E::store(v);
+  }
+  if (p.c_vec && ncols == 32 && n0 + 32 <= p.N) {
+    constexpr int PER16 = 16 / sizeof(T);
+    uint4 *dst = reinterpret_cast<uint4 *>(C + (int64_t)m * p.c_rs + n0);
+#pragma unroll
+    for (int v = 0; v < 32 / PER16; ++v) dst[v] = *reinterpret_cast<const uint4 *>(&out[v * PER16]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < ncols && n0 + j < p.N) C[(int64_t)m * p.c_rs + (int64_t)(n0 + j) * p.c_cs] = out[j];
+  }
+}
+
+// ---------------------------------------------------------------------------
+template <class T, int BN>
+__global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_constant__ TcParams p) {
+  constexpr int ESZ = sizeof(T);
+  using C_ = Cfg<BN, ESZ>;
+  constexpr int BK = C_::BK, STAGES = C_::STAGES;
+  constexpr uint32_t A_BYTES = C_::A_BYTES, B_BYTES = C_::B_BYTES, STAGE_BYTES = C_::STAGE_BYTES;
+  constexpr int CHUNK = BN < 32 ? BN : 32;  // columns per tcgen05.ld
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // 1024-byte alignment for the swizzled operand tiles.
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *ring = smem;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(ring + STAGES * STAGE_BYTES);
+  // bars: full[STAGES], empty[STAGES], tfull[2], tempty[2], drain
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 5);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t ring_u32 = smem_u32(ring);
+  const uint32_t bar_u32 = smem_u32(bars);
+  auto full_bar = [&](int s) { return bar_u32 + 8u * s; };
+  auto empty_bar = [&](int s) { return bar_u32 + 8u * (STAGES + s); };
+  auto tfull_bar = [&](int a) { return bar_u32 + 8u * (2 * STAGES + a); };
+  auto tempty_bar = [&](int a) { return bar_u32 + 8u * (2 * STAGES + 2 + a); };
+  const uint32_t drain_bar = bar_u32 + 8u * (2 * STAGES + 4);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull_bar(a), 1);
+      mbar_init(tempty_bar(a), 4);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&p.tmA);
+    prefetch_tmap(&p.tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), C_::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued_stage = -1;
+      uint32_t issued_phase = 0;
+      for (int u = blockIdx.x; u < p.num_units; u += gridDim.x) {
+        const Unit w = decode_unit(p, u);
+        const int kb0 = w.s * p.kb_per_split;
+        const int kb1 = min(p.kb_total, kb0 + p.kb_per_split);
+        const int ba = p.a_bcast ? 0 : w.b, bb = p.b_bcast ? 0 : w.b;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag, p.timeout_ns)) goto producer_done;
+          mbar_arrive_expect_tx(full_bar(stage), STAGE_BYTES);
+          const uint32_t sa = ring_u32 + stage * STAGE_BYTES;
+          const uint32_t sb = sa + A_BYTES;
+          if (!p.a_mn) {
+            tma_load_3d(sa, &p.tmA, full_bar(stage), kb * BK, w.tm * BM, ba);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BM * ESZ / 128; ++j)
+              tma_load_3d(sa + j * (BK * 128), &p.tmA, full_bar(stage), w.tm * BM + j * (128 / ESZ), kb * BK, ba);
+          }
+          if (!p.b_mn) {
+            tma_load_3d(sb, &p.tmB, full_bar(stage), kb * BK, w.tn * BN, bb);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN * ESZ / 128; ++j)
+              tma_load_3d(sb + j * (BK * 128), &p.tmB, full_bar(stage), w.tn * BN + j * (128 / ESZ), kb * BK, bb);
+          }
+          issued_stage = stage;
+          issued_phase = phase;
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+      }
+    producer_done:
+      // Drain: the last issued stage's copies must land before the CTA can exit.
+      if (issued_stage >= 0) {
+        volatile int no_abort = 0;
+        mbar_wait(full_bar(issued_stage), issued_phase, &no_abort, p.timeout_ns);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = make_idesc<T, BN>(p.a_mn, p.b_mn);
+      // Canonical SW128 layouts: K-major SBO = 8 rows * 128 B; MN-major
+      // LBO = next 128-byte MN column block (one TMA box), SBO = 8 K rows.
+      const uint32_t a_lbo = p.a_mn ? BK * 128 : 16, b_lbo = p.b_mn ? BK * 128 : 16;
+      const uint32_t a_kstep = p.a_mn ? C_::UMMA_K * 128 : 32, b_kstep = p.b_mn ? C_::UMMA_K * 128 : 32;
+      int stage = 0;
+      uint32_t phase = 0;
+      int abuf = 0;
+      uint32_t aphase = 0;
+      bool issued_any = false;
+      for (int u = blockIdx.x; u < p.num_units; u += gridDim.x) {
+        const Unit w = decode_unit(p, u);
+        const int kb0 = w.s * p.kb_per_split;
+        const int kb1 = min(p.kb_total, kb0 + p.kb_per_split);
+        if (!mbar_wait(tempty_bar(abuf), aphase ^ 1u, abort_flag, p.timeout_ns)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(abuf * C_::ACC_COLS);
+        bool aborted = false;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(full_bar(stage), phase, abort_flag, p.timeout_ns)) { aborted = true; break; }
+          tc_fence_after();
+          const uint32_t sa = ring_u32 + stage * STAGE_BYTES;
+          const uint32_t sb = sa + A_BYTES;
+#pragma unroll
+          for (int ks = 0; ks < C_::KSTEPS; ++ks) {
+            const uint64_t ad = sdesc(sa + ks * a_kstep, a_lbo, 1024);
+            const uint64_t bd = sdesc(sb + ks * b_kstep, b_lbo, 1024);
+            umma<ESZ>(d_tmem, ad, bd, idesc, (kb > kb0 || ks > 0) ? 1u : 0u);
+          }
+          issued_any = true;
+          umma_commit(empty_bar(stage));  // frees this smem stage when the MMAs finish
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+        if (aborted) break;
+        umma_commit(tfull_bar(abuf));     // accumulator ready for the epilogue
+        if (++abuf == 2) { abuf = 0; aphase ^= 1u; }
+      }
+      if (*abort_flag && issued_any) {
+        // Drain every MMA this thread issued before TMEM is freed.
+        umma_commit(drain_bar);
+        volatile int no_abort = 0;
+        mbar_wait(drain_bar, 0, &no_abort, p.timeout_ns);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int lg = warp & 3;  // TMEM lane quarter this warp may access
+    const int row = lg * 32 + lane;
+    int abuf = 0;
+    uint32_t aphase = 0;
+    for (int u = blockIdx.x; u < p.num_units; u += gridDim.x) {
+      const Unit w = decode_unit(p, u);
+      if (!mbar_wait(tfull_bar(abuf), aphase, abort_flag, p.timeout_ns)) break;
+      tc_fence_after();
+      const int m = w.tm * BM + row;
+      const uint32_t tbase = tmem_base + ((uint32_t)(lg * 32) << 16) + (uint32_t)(abuf * C_::ACC_COLS);
+      if (p.splits == 1) {
+#pragma unroll 1
+        for (int c = 0; c < BN; c += CHUNK) {
+          uint32_t r[32];
+          if constexpr (CHUNK == 32) tmem_ld_x32(tbase + c, r); else tmem_ld_x16(tbase + c, r);
+          tmem_wait_ld();
+          const int n0 = w.tn * BN + c;
+          if (m < p.M && n0 < p.N) store_row_chunk<T>(p, w.b, m, n0, CHUNK, r);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(tempty_bar(abuf));
+      } else {
+        // Split-K: publish raw accumulators (tile-local row-major, 4 B each).
+        uint32_t *part = reinterpret_cast<uint32_t *>(p.ws) +
+                         ((int64_t)w.tile * p.splits + w.s) * (int64_t)(BM * BN) + (int64_t)row * BN;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += CHUNK) {
+          uint32_t r[32];
+          if constexpr (CHUNK == 32) tmem_ld_x32(tbase + c, r); else tmem_ld_x16(tbase + c, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < CHUNK; j += 4)
+            __stcg(reinterpret_cast<uint4 *>(part + c + j), make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]));
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(tempty_bar(abuf));
+        // Each warp owns 32 rows of the tile and reduces them on its own:
+        // per-(tile, lane quarter) tickets, so no cross-warp barrier exists
+        // that an aborting warp could leave the others waiting at.
+        __threadfence();
+        __syncwarp();
+        unsigned tk = 0;
+        if (lane == 0) tk = atomicAdd(p.tickets + (int64_t)w.tile * 4 + lg, 1u);
+        tk = __shfl_sync(0xffffffffu, tk, 0);
+        if (tk == (unsigned)(p.splits - 1)) {
+          __threadfence();
+          const uint32_t *base = reinterpret_cast<const uint32_t *>(p.ws) +
+                                 (int64_t)w.tile * p.splits * (int64_t)(BM * BN) + (int64_t)row * BN;
+#pragma unroll 1
+          for (int c = 0; c < BN; c += CHUNK) {
+            uint32_t r[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) r[j] = 0;
+            for (int s = 0; s < p.splits; ++s) {
+              const uint32_t *src = base + (int64_t)s * (BM * BN) + c;
+#pragma unroll
+              for (int j = 0; j < CHUNK; j += 4) {
+                const uint4 v = __ldcg(reinterpret_cast<const uint4 *>(src + j));
+                if constexpr (Elem<T>::is_int) {
+                  r[j] += v.x; r[j + 1] += v.y; r[j + 2] += v.z; r[j + 3] += v.w;
+                } else {
+                  r[j] = __float_as_uint(__uint_as_float(r[j]) + __uint_as_float(v.x));
+                  r[j + 1] = __float_as_uint(__uint_as_float(r[j + 1]) + __uint_as_float(v.y));
+                  r[j + 2] = __float_as_uint(__uint_as_float(r[j + 2]) + __uint_as_float(v.z));
+                  r[j + 3] = __float_as_uint(__uint_as_float(r[j + 3]) + __uint_as_float(v.w));
+                }
+              }
+            }
+            const int n0 = w.tn * BN + c;
+            if (m < p.M && n0 < p.N) store_row_chunk<T>(p, w.b, m, n0, CHUNK, r);
+          }
+          if (lane == 0) p.tickets[(int64_t)w.tile * 4 + lg] = 0u;
+        }
+      }
+      if (++abuf == 2) { abuf = 0; aphase ^= 1u; }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C_::TMEM_COLS);
+  }
+}
+
+// Debug kernel for the bounded-wait path: waits on a barrier nobody arrives at.
+__global__ void wait_timeout_kernel(unsigned long long timeout_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&bar), 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_wait(smem_u32(&bar), 0, &abort_flag, timeout_ns);
+  __syncthreads();
+}
+
+}  // namespace tc
+}  // namespace mb

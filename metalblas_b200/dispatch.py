@@ -1,0 +1,378 @@
+"""Public API and operand resolution (B200 form of metalblas/dispatch.py).
+
+Same names, signatures and exception types as the reference
+(metalblas/__init__.py:16-19, metalblas/dispatch.py:148-302); the tensors are
+CUDA tensors and every product runs through one C-ABI call, ``mb_gemm``
+(include/metalblas_b200.h).  What changes against the reference:
+
+* one descriptor covers every dtype family: float, complex (fused: read once,
+  conj applied on load) and integer, so there is no four-product complex path
+  (metalblas/complex_dispatch.py:69-115) and no per-batch Python loop
+  (metalblas/dispatch.py:134-145);
+* output views are written in place through their strides (the reference copies
+  non-row-major ``out`` through a temporary, metalblas/dispatch.py:106-114);
+* baddbmm is fused for every dtype (the reference computes complex baddbmm with
+  torch arithmetic, metalblas/complex_dispatch.py:132-144).
+"""
+from __future__ import annotations
+
+import ctypes
+from math import prod
+
+import torch
+
+from . import _lib
+from . import plan as _plan
+
+INTS = (torch.int8, torch.uint8, torch.int16, torch.int32, torch.int64)
+FLOATS = (torch.float32, torch.float16, torch.bfloat16)
+COMPLEX = (torch.complex64, torch.complex32)
+TC_DTYPES = (torch.bfloat16, torch.float16, torch.int8, torch.uint8)
+_INT64_MASK = (1 << 64) - 1
+
+
+def _ceildiv(n, d):
+    return (n + d - 1) // d
+
+
+def _unit_lead(t, rows, cols):
+    """``(is_column_major, leading_stride)`` for a simple matrix view, else None.
+
+    Same rule as the reference (metalblas/dispatch.py:23-30): row-major when the
+    last stride is 1 and the leading stride covers a row; column-major when the
+    first stride is 1 and the leading stride covers a column.
+    """
+    s0, s1 = map(int, t.stride()[-2:])
+    if s1 == 1 and s0 >= cols:
+        return False, s0
+    if s0 == 1 and s1 >= rows:
+        return True, s1
+    return None
+
+
+def _matrix_view(t, rows, cols):
+    """Keep unit-stride views; copy anything else (metalblas/dispatch.py:33-35)."""
+    return t if _unit_lead(t, rows, cols) is not None else t.contiguous()
+
+
+def _plain(t):
+    """Drop a lazy negation bit; the conjugation bit is kept and applied in-kernel."""
+    return t.resolve_neg() if t.is_neg() else t
+
+
+def _int64(v: int) -> int:
+    v = int(v) & _INT64_MASK
+    return v - (1 << 64) if v >> 63 else v
+
+
+def _scalars(dtype, beta, alpha):
+    """Cast beta/alpha like metalblas/dispatch.py:127-131."""
+    if dtype in INTS:
+        beta, alpha = int(beta), int(alpha)
+    elif dtype not in COMPLEX:
+        beta, alpha = float(beta), float(alpha)
+    return beta, alpha, beta != 0, alpha != 0
+
+
+# --------------------------------------------------------------------------- workspace
+_WS: dict = {}
+
+
+def _workspace(device: torch.device, stream: int, nbytes: int) -> torch.Tensor:
+    """Zero-filled scratch for split-K partials, one per (device, stream).
+
+    Kernels leave the ticket region zeroed, so the buffer is reused as is.
+    """
+    key = (device.index, stream)
+    buf = _WS.get(key)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        _WS[key] = buf
+    return buf
+
+
+# --------------------------------------------------------------------------- launch
+_BACKENDS = {None: _lib.MB_BACKEND_AUTO, "auto": _lib.MB_BACKEND_AUTO, "gemv": _lib.MB_BACKEND_GEMV,
+             "mpp_tensor": _lib.MB_BACKEND_TC, "mpp": _lib.MB_BACKEND_TC, "simd": _lib.MB_BACKEND_SIMT}
+
+
+def _launch(A, B, C, M, N, K, batch, a3, b3, c3, *, epilogue=None, backend=_lib.MB_BACKEND_AUTO,
+            tile_n=0, split_k=0, swap_ab=0, autotune=True):
+    """Fill an mb_gemm_desc and call mb_gemm on the current stream of C's device.
+
+    a3/b3/c3 are (row stride, col stride, batch stride) in elements.
+    epilogue: (bias, (rs, cs, bs), beta, alpha, beta_nz, alpha_nz) or None.
+    """
+    lib = _lib.load()
+    dtype = C.dtype
+    d = _lib.new_desc()
+    d.dtype = _lib.DTYPE_CODE[dtype]
+    d.backend = backend
+    d.M, d.N, d.K, d.batch = int(M), int(N), int(K), int(batch)
+    d.A = A.data_ptr() if A is not None else None
+    d.B = B.data_ptr() if B is not None else None
+    d.C = C.data_ptr()
+    d.a_rs, d.a_cs, d.sA = a3
+    d.b_rs, d.b_cs, d.sB = b3
+    d.c_rs, d.c_cs, d.sC = c3
+    d.conj_a = int(A is not None and A.is_conj())
+    d.conj_b = int(B is not None and B.is_conj())
+    if epilogue is not None:
+        bias, (brs, bcs, bbs), beta, alpha, bnz, anz = epilogue
+        d.epilogue = 1
+        d.alpha_nz, d.beta_nz = int(bool(anz)), int(bool(bnz))
+        d.bias = bias.data_ptr() if bnz else None
+        d.bias_rs, d.bias_cs, d.bias_bs = brs, bcs, bbs
+        if dtype in INTS:
+            d.ialpha, d.ibeta = _int64(alpha), _int64(beta)
+        else:
+            d.alpha_re, d.alpha_im = float(complex(alpha).real), float(complex(alpha).imag)
+            d.beta_re, d.beta_im = float(complex(beta).real), float(complex(beta).imag)
+    d.tile_n, d.split_k, d.swap_ab = int(tile_n), int(split_k), int(swap_ab)
+    dev = C.device
+    if torch.cuda.current_device() != dev.index:
+        with torch.cuda.device(dev):
+            return _launch(A, B, C, M, N, K, batch, a3, b3, c3, epilogue=epilogue, backend=backend,
+                           tile_n=tile_n, split_k=split_k, swap_ab=swap_ab, autotune=autotune)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    if autotune and backend == _lib.MB_BACKEND_AUTO and not tile_n and not split_k and not swap_ab:
+        choice = _plan.choose(d, A, B, C, stream)
+        if choice is not None:
+            d.backend, d.tile_n, d.split_k, d.swap_ab = choice
+    nbytes = int(lib.mb_gemm_workspace_size(ctypes.byref(d)))
+    if nbytes > 0:
+        ws = _workspace(dev, stream, nbytes)
+        d.workspace, d.workspace_bytes = ws.data_ptr(), ws.numel()
+    rc = lib.mb_gemm(ctypes.byref(d), ctypes.c_void_p(stream))
+    if rc == _lib.MB_ERR_UNSUPPORTED and backend == _lib.MB_BACKEND_TC:
+        # "mpp"/"mpp_tensor" on operands TMA cannot address: CUDA-core kernel
+        d.backend = _lib.MB_BACKEND_SIMT
+        rc = lib.mb_gemm(ctypes.byref(d), ctypes.c_void_p(stream))
+    _lib.raise_for(rc)
+    return C
+
+
+def _parse_tile(backend, tile):
+    """tile= override.  For "mpp_tensor" it is (BM, BN[, split_k]) of the tcgen05
+    kernel: BM must be 128 (the UMMA M), BN one of 16/32/64/128/256.  The
+    CUDA-core tiles of "simd"/"mpp" are fixed; their tuples are checked for
+    shape only, as the reference does (metalblas/float_dispatch.py:826-844)."""
+    if tile is None:
+        return 0, 0
+    tile = tuple(int(x) for x in tile)
+    if backend == "mpp_tensor":
+        assert len(tile) >= 2, "mpp_tensor tile is (BM, BN[, split_k])"
+        if tile[0] != 128 or tile[1] not in (16, 32, 64, 128, 256):
+            raise ValueError(f"mpp_tensor tile {tile}: BM must be 128 and BN one of 16, 32, 64, 128, 256")
+        split = tile[2] if len(tile) > 2 else 0
+        if split < 0:
+            raise ValueError("split_k must be >= 0")
+        return tile[1], split
+    assert len(tile) >= 3, "tile must have at least 3 entries"
+    return 0, 0
+
+
+# --------------------------------------------------------------------------- ops
+def _complex_inputs(a, b):
+    """Promote the real operand to the complex dtype (metalblas/complex_dispatch.py:25-30)."""
+    dtype = a.dtype if a.dtype in COMPLEX else b.dtype
+    a = a.to(dtype) if a.dtype != dtype else a
+    b = b.to(dtype) if b.dtype != dtype else b
+    return a, b, dtype
+
+
+def _mm2d(a, b, out, epilogue=None, backend=None, tile=None):
+    if a.is_complex() or b.is_complex():
+        a, b, _ = _complex_inputs(a, b)
+    assert a.is_cuda and b.is_cuda, "metalblas_b200 expects cuda tensors"
+    assert a.dtype == b.dtype, "matmul requires both operands the same dtype"
+    dtype = a.dtype
+    if dtype not in _lib.DTYPE_CODE:
+        raise NotImplementedError(f"dtype {dtype} not supported")
+    M, K = a.shape
+    K2, N = b.shape
+    assert K == K2, f"shape mismatch: A is {a.shape}, B is {b.shape}"
+    if backend not in _BACKENDS:
+        raise ValueError(f"unknown backend {backend}")
+    if backend == "gemv" and not (M == 1 or N == 1):
+        raise ValueError("gemv backend requires M==1 or N==1")
+    tile_n, split_k = _parse_tile(backend, tile)
+    A = _plain(_matrix_view(a, M, K))
+    B = _plain(_matrix_view(b, K, N))
+    if out is None:
+        out = torch.empty((M, N), dtype=dtype, device=a.device)
+    else:
+        assert out.shape == (M, N) and out.dtype == dtype and out.is_cuda, \
+            f"out must be ({M}, {N}) {dtype} on cuda"
+    be = _BACKENDS[backend]
+    if backend in ("mpp", "mpp_tensor") and dtype not in TC_DTYPES:
+        be = _lib.MB_BACKEND_SIMT
+    return _launch(A, B, out, M, N, K, 1,
+                   (A.stride(0), A.stride(1), 0), (B.stride(0), B.stride(1), 0),
+                   (out.stride(0), out.stride(1), 0),
+                   epilogue=epilogue, backend=be, tile_n=tile_n, split_k=split_k)
+
+
+def _matmul_nd(a, b, out=None):
+    """Vector promotion and broadcast batches around the 2-D/3-D kernels
+    (metalblas/dispatch.py:148-171)."""
+    assert a.ndim and b.ndim, "matmul operands must be at least 1-D"
+    a_vec, b_vec = a.ndim == 1, b.ndim == 1
+    if a_vec:
+        a = a.unsqueeze(0)
+    if b_vec:
+        b = b.unsqueeze(-1)
+    M, K = a.shape[-2:]
+    K2, N = b.shape[-2:]
+    assert K == K2, f"shape mismatch: A is {a.shape}, B is {b.shape}"
+    batch = torch.broadcast_shapes(a.shape[:-2], b.shape[:-2])
+    if batch:
+        size = prod(batch)
+        a3 = a.expand(*batch, M, K).reshape(size, M, K)
+        b3 = b.expand(*batch, K, N).reshape(size, K, N)
+        result = bmm(a3, b3).reshape(*batch, M, N)
+    else:
+        result = matmul(a, b)
+    if a_vec:
+        result = result.squeeze(-2)
+    if b_vec:
+        result = result.squeeze(-1)
+    return out.copy_(result) if out is not None else result
+
+
+def matmul(a: torch.Tensor, b: torch.Tensor, *, backend: str | None = None,
+           tile: tuple | None = None, swizzle_log: int | None = None,
+           out: torch.Tensor | None = None) -> torch.Tensor:
+    """Compute ``a @ b`` on a CUDA device (metalblas/dispatch.py:174-185).
+
+    backend: None/"auto" (tile table + autotune cache), "gemv" (needs M==1 or
+    N==1), "mpp_tensor" (tcgen05 kernel, tile=(128, BN[, split_k])), "mpp"
+    (tcgen05 when the dtype and layout allow, else CUDA cores) or "simd"
+    (CUDA-core FFMA/IMAD kernel).  swizzle_log is accepted for compatibility;
+    rasterisation is done by the persistent tile scheduler.
+    """
+    if swizzle_log is not None:
+        assert int(swizzle_log) >= 0, "swizzle_log must be >= 0"
+    if a.ndim != 2 or b.ndim != 2:
+        return _matmul_nd(a, b, out)
+    return _mm2d(a, b, out, backend=backend, tile=tile)
+
+
+def addmm(input: torch.Tensor, mat1: torch.Tensor, mat2: torch.Tensor, *,
+          beta=1, alpha=1, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``beta * input + alpha * (mat1 @ mat2)``, fused (metalblas/dispatch.py:188-208)."""
+    assert mat1.is_cuda and mat2.is_cuda
+    assert mat1.dim() == 2 and mat2.dim() == 2, "addmm expects 2-D mat1, mat2"
+    M, K = mat1.shape
+    K2, N = mat2.shape
+    assert K == K2, f"shape mismatch: mat1 is {mat1.shape}, mat2 is {mat2.shape}"
+    dtype = mat1.dtype
+    assert mat2.dtype == dtype, "addmm requires mat1.dtype == mat2.dtype"
+    if out is not None:
+        assert out.shape == (M, N) and out.dtype == dtype and out.is_cuda
+    beta, alpha, bnz, anz = _scalars(dtype, beta, alpha)
+    bias = input if input.dtype == dtype else input.to(dtype)
+    bias = _plain(bias.resolve_conj() if bias.is_conj() else bias)
+    br, bc = map(int, bias.expand(M, N).stride())
+    return _mm2d(mat1, mat2, out, epilogue=(bias, (br, bc, 0), beta, alpha, bnz, anz))
+
+
+def _bmm_shape(a, b, op):
+    assert a.is_cuda and b.is_cuda, f"{op} expects cuda tensors"
+    assert a.dim() == 3 and b.dim() == 3, f"{op} expects 3-D inputs"
+    assert a.dtype == b.dtype, f"{op} requires both operands the same dtype"
+    Bb, M, K = a.shape
+    Bb2, K2, N = b.shape
+    assert Bb == Bb2 and K == K2, f"{op} shape mismatch: {a.shape} @ {b.shape}"
+    return Bb, M, N, K, a.dtype
+
+
+def _bmm(a, b, out, epilogue=None):
+    Bb, M, N, K, dtype = _bmm_shape(a, b, "bmm")
+    if dtype not in _lib.DTYPE_CODE:
+        raise NotImplementedError(f"dtype {dtype} not supported")
+    if out is None:
+        out = torch.empty((Bb, M, N), dtype=dtype, device=a.device)
+    else:
+        assert out.shape == (Bb, M, N) and out.dtype == dtype and out.is_cuda, \
+            f"out must be ({Bb}, {M}, {N}) {dtype} on cuda"
+    if Bb == 0 or M == 0 or N == 0:
+        return out
+    A = _plain(_matrix_view(a, M, K))
+    B = _plain(_matrix_view(b, K, N))
+    return _launch(A, B, out, M, N, K, Bb,
+                   (A.stride(1), A.stride(2), A.stride(0)), (B.stride(1), B.stride(2), B.stride(0)),
+                   (out.stride(1), out.stride(2), out.stride(0)), epilogue=epilogue)
+
+
+def bmm(a: torch.Tensor, b: torch.Tensor, *, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Batched 3-D product; a batch stride of 0 broadcasts (metalblas/dispatch.py:211-225)."""
+    return _bmm(a, b, out)
+
+
+def baddbmm(input: torch.Tensor, batch1: torch.Tensor, batch2: torch.Tensor, *,
+            beta=1, alpha=1, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``beta * input + alpha * (batch1 @ batch2)``, fused for every dtype
+    (metalblas/dispatch.py:228-242)."""
+    Bb, M, N, _, dtype = _bmm_shape(batch1, batch2, "baddbmm")
+    beta, alpha, bnz, anz = _scalars(dtype, beta, alpha)
+    bias = input if input.dtype == dtype else input.to(dtype)
+    bias = _plain(bias.resolve_conj() if bias.is_conj() else bias)
+    sb, br, bc = map(int, bias.expand(Bb, M, N).stride())
+    return _bmm(batch1, batch2, out, epilogue=(bias, (br, bc, sb), beta, alpha, bnz, anz))
+
+
+def addbmm(input: torch.Tensor, batch1: torch.Tensor, batch2: torch.Tensor, *,
+           beta=1, alpha=1, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``beta * input + alpha * sum_b(batch1[b] @ batch2[b])`` as one addmm over the
+    concatenated K (metalblas/dispatch.py:245-260)."""
+    Bb, M, N, K, dtype = _bmm_shape(batch1, batch2, "addbmm")
+    if Bb == 0 or K == 0:
+        bias = input if input.dtype == dtype else input.to(dtype)
+        beta = int(beta) if dtype in INTS else beta
+        result = ((bias * beta).expand(M, N).contiguous() if beta != 0 else
+                  bias.new_zeros(M, N))
+        if out is not None:
+            assert out.shape == (M, N) and out.dtype == dtype and out.is_cuda
+            return out.copy_(result)
+        return result
+    A = batch1.permute(1, 0, 2).reshape(M, Bb * K)
+    B = batch2.reshape(Bb * K, N)
+    return addmm(input, A, B, beta=beta, alpha=alpha, out=out)
+
+
+def dot(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """1-D inner product, matching ``torch.dot`` (metalblas/dispatch.py:263-271)."""
+    assert a.dim() == 1 and b.dim() == 1, \
+        f"1D tensors expected, but got {a.dim()}D and {b.dim()}D tensors"
+    assert a.shape[0] == b.shape[0], \
+        f"inconsistent tensor size, expected [{a.shape[0]}] and [{b.shape[0]}]"
+    assert a.dtype == b.dtype, \
+        f"dot : expected both vectors to have same dtype, got {a.dtype} and {b.dtype}"
+    return matmul(a, b)
+
+
+def vdot(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """Inner product conjugating the first argument (metalblas/dispatch.py:274-276);
+    the conjugation is a load flag, not a copy."""
+    return dot(a.conj() if a.is_complex() else a, b)
+
+
+def outer(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """Outer product of two vectors (metalblas/dispatch.py:279-283)."""
+    assert a.dim() == 1, f"outer: Expected 1-D argument self, but got {a.dim()}-D"
+    assert b.dim() == 1, f"outer: Expected 1-D argument vec2, but got {b.dim()}-D"
+    return a.unsqueeze(1) * b.unsqueeze(0)
+
+
+def mv(mat: torch.Tensor, vec: torch.Tensor) -> torch.Tensor:
+    """Matrix-vector product (metalblas/dispatch.py:286-293)."""
+    assert mat.dim() == 2 and vec.dim() == 1, \
+        f"vector + matrix @ vector expected, got {mat.dim()}, {mat.dim()}, {vec.dim()}"
+    assert mat.shape[1] == vec.shape[0], \
+        f"size mismatch, got mat ({mat.shape[0]}x{mat.shape[1]}), vec ({vec.shape[0]})"
+    return matmul(mat, vec)
+
+
+gemm = matmul
+ger = outer
