@@ -116,6 +116,13 @@ void normalize(int64_t rows, int64_t cols, int64_t &rs, int64_t &cs) {
 }
 
 // --------------------------------------------------------------------------- plan
+// Workspace layout, identical for every plan: a fixed region of ticket counters
+// at offset 0, then the split-K partials.  Because the ticket region never
+// moves, partials written by one plan can never land on the counters another
+// plan reads; each kernel returns the counters it used to zero.
+constexpr int64_t kTicketBytes = 256 * 1024;
+constexpr int64_t kMaxTickets = kTicketBytes / 4;
+
 enum PlanKind { PK_EMPTY = 0, PK_GEMV_COLS, PK_GEMV_ROWS, PK_TC, PK_SIMT };
 
 struct Plan {
@@ -129,7 +136,7 @@ struct Plan {
   int64_t tiles_m = 0, tiles_n = 0, kb_total = 0, kb_per_split = 0;
   int a_mn = 0, b_mn = 0;
   // shared
-  int64_t ws_bytes = 0, ws_tickets_off = 0;
+  int64_t ws_bytes = 0;
   std::string why;
 };
 
@@ -208,6 +215,7 @@ void choose_tc_tile(const Op &o, int sms, int force_bn, int force_split, bool ha
     if (!force_bn && bn > 16 && round_up(o.N, 16) <= bn / 2) continue;  // a smaller tile already covers N
     const int64_t tiles = o.batch * ceil_div(o.M, 128) * ceil_div(o.N, bn);
     int max_split = have_ws ? (int)std::min<int64_t>(kb_total, 32) : 1;
+    if (tiles * 4 > kMaxTickets) max_split = 1;  // not enough ticket counters
     for (int s = 1; s <= max_split; ++s) {
       if (force_split && s != force_split) continue;
       const int64_t kbp = ceil_div(kb_total, s);
@@ -239,8 +247,7 @@ bool plan_tc(const Op &o, int sms, const mb_gemm_desc *d, bool have_ws, Plan &pl
   pl.kind = PK_TC;
   const int64_t tiles = o.batch * pl.tiles_m * pl.tiles_n;
   if (pl.splits > 1) {
-    pl.ws_tickets_off = round_up(tiles * pl.splits * 128 * pl.bn * 4, 256);
-    pl.ws_bytes = pl.ws_tickets_off + tiles * 4 * 4;
+    pl.ws_bytes = kTicketBytes + tiles * pl.splits * 128 * pl.bn * 4;
   }
   return true;
 }
@@ -279,6 +286,7 @@ bool plan_gemv(const Op &o, int sms, const mb_gemm_desc *d, bool have_ws, Plan &
     ks = std::max<int64_t>(1, std::min<int64_t>(ks, ceil_div(g.K, 64)));  // >= 64 rows per CTA
     if (ks > 65535) ks = 65535;
     if (ks > 1 && !have_ws) ks = 1;
+    if (o.batch * ctas_x > kMaxTickets) ks = 1;  // not enough ticket counters
     if (ks > 1) {
       g.kchunk = ceil_div(g.K, ks);
       ks = ceil_div(g.K, g.kchunk);
@@ -286,8 +294,7 @@ bool plan_gemv(const Op &o, int sms, const mb_gemm_desc *d, bool have_ws, Plan &
     g.ksplit = (int)ks;
     if (ks > 1) {
       const int64_t accb = acc_is_8byte(o.dt) ? 8 : 4;
-      pl.ws_tickets_off = round_up(ks * o.batch * g.R * accb, 256);
-      pl.ws_bytes = pl.ws_tickets_off + o.batch * ctas_x * 4;
+      pl.ws_bytes = kTicketBytes + ks * o.batch * g.R * accb;
     }
   }
   pl.kind = kind;
@@ -392,8 +399,8 @@ int launch_gemv(const Plan &pl, const EpiScalars &e, void *ws, cudaStream_t st) 
   constexpr int NW = 8;
   constexpr int V = 16 / sizeof(T);
   if (g.ksplit > 1) {
-    g.ws = ws;
-    g.tickets = reinterpret_cast<unsigned *>(reinterpret_cast<char *>(ws) + pl.ws_tickets_off);
+    g.tickets = reinterpret_cast<unsigned *>(ws);
+    g.ws = reinterpret_cast<char *>(ws) + kTicketBytes;
   }
   const unsigned gz = (unsigned)std::min<int64_t>(g.batch, 65535);
   if (g.batch > 65535) return fail(MB_ERR_INVALID, "batch too large for GEMV");
@@ -480,8 +487,8 @@ int launch_tc_bn(const Op &o, const Plan &pl, const EpiScalars &e, void *ws, int
   p.epi = e;
   p.c_vec = (o.c_cs == 1 && aligned16(o.C) && (o.c_rs * ESZ) % 16 == 0 && (o.batch <= 1 || (o.sC * ESZ) % 16 == 0)) ? 1 : 0;
   if (pl.splits > 1) {
-    p.ws = ws;
-    p.tickets = reinterpret_cast<unsigned *>(reinterpret_cast<char *>(ws) + pl.ws_tickets_off);
+    p.tickets = reinterpret_cast<unsigned *>(ws);
+    p.ws = reinterpret_cast<char *>(ws) + kTicketBytes;
   }
   p.timeout_ns = wait_timeout_ns();
   auto kern = tc::tc_gemm_kernel<T, BN>;

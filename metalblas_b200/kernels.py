@@ -51,7 +51,12 @@ def device_status() -> int:
 
 
 def device_status_clear() -> None:
+    """Reset the status word and drop the cached split-K workspaces: a kernel that
+    gave up may have left ticket counters non-zero, so fresh zeroed buffers are
+    allocated on the next call."""
+    from . import dispatch
     _lib.device_status_clear()
+    dispatch._WS.clear()
 
 
 def debug_wait_timeout(limit_us: int) -> None:

@@ -1,0 +1,76 @@
+"""Every plan of the sm_100a tile table gives the oracle's answer, whatever plan
+ran before it on the same (shared, cached) split-K workspace.
+
+This pins the workspace contract of include/metalblas_b200.h: ticket counters
+live at a fixed offset for every plan and are returned to zero by the kernel
+that used them, so a split-K launch never reads counters or partials left by
+a different plan.
+"""
+from __future__ import annotations
+
+import itertools
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as orc
+from metalblas_b200 import _lib, dispatch
+from tests.helpers import NAME, rand, to_np
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [(128, 8192, 4096), (64, 2048, 8192), (256, 512, 16384), (4, 4096, 4096), (16, 1024, 2048)]
+VARIANTS = [(0, 0, 0), (64, 1, -1), (64, 4, -1), (128, 2, -1), (256, 4, -1), (256, 8, -1), (128, 3, -1),
+            (0, 0, 1), (32, 4, 1), (16, 2, 1), (64, 1, 1)]
+
+
+def _run(a, b, tile_n, split, swap, epilogue=None):
+    M, K = a.shape
+    N = b.shape[1]
+    c = torch.empty(M, N, dtype=a.dtype, device=a.device)
+    try:
+        dispatch._launch(a, b, c, M, N, K, 1, (a.stride(0), a.stride(1), 0), (b.stride(0), b.stride(1), 0),
+                         (c.stride(0), c.stride(1), 0), epilogue=epilogue, backend=_lib.MB_BACKEND_TC,
+                         tile_n=tile_n, split_k=split, swap_ab=swap, autotune=False)
+    except NotImplementedError:
+        return None  # this layout cannot take the forced variant (e.g. MN-major B with a narrow tile)
+    return c
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.int8], ids=NAME.get)
+def test_interleaved_plans_share_workspace(dtype):
+    gen = torch.Generator().manual_seed(7)
+    cases = []
+    for (M, N, K) in SHAPES:
+        a = rand((M, K), dtype, gen, full_range=dtype is torch.int8)
+        b = rand((K, N), dtype, gen, full_range=dtype is torch.int8)
+        cases.append((a, b, orc.product(to_np(a), to_np(b), NAME[dtype])))
+    ran = 0
+    # round-robin over shapes so consecutive launches always switch plan and shape
+    for v, (a, b, ref) in itertools.product(VARIANTS, cases):
+        c = _run(a, b, *v)
+        if c is None:
+            continue
+        ran += 1
+        ok, err = orc.check(to_np(c), ref, NAME[dtype])
+        assert ok, f"{dtype} {tuple(a.shape)}x{b.shape[1]} variant={v} plan err={err}"
+    assert ran >= len(cases) * 6
+
+
+def test_split_k_epilogue_int8_wraps():
+    """Split-K partials are summed as int32 with wraparound, then alpha/beta/bias."""
+    gen = torch.Generator().manual_seed(8)
+    a = rand((128, 8192), torch.int8, gen, full_range=True)
+    b = rand((8192, 384), torch.int8, gen, full_range=True)
+    bias = rand((384,), torch.int8, gen, full_range=True)
+    for split in (1, 2, 4, 8):
+        c = _run(a, b, 128, split, -1, epilogue=(bias, (0, 1, 0), 3, -7, True, True))
+        ref = orc.fused(to_np(bias), to_np(a), to_np(b), 3, -7, "int8")
+        ok, _ = orc.check(to_np(c), ref, "int8")
+        assert ok, f"split={split}"
+
+
+def test_no_device_timeouts():
+    from metalblas_b200 import kernels
+    assert kernels.device_status() == 0
