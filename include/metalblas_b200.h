@@ -118,6 +118,28 @@ void mb_gemm_desc_init(mb_gemm_desc *d);
  * metalblas/integer_dispatch.py:92-150 and metalblas/complex_dispatch.py:33-129. */
 int mb_gemm(const mb_gemm_desc *d, void *stream);
 
+/* Allocation-free variant of mb_gemm.  No counterpart in the reference.
+ *
+ * For callers that cannot call cudaMalloc and have no workspace to pass:
+ * inference runtimes that reserve all device memory at start-up and forbid
+ * allocation on the request path (cudaMalloc may synchronise the device and its
+ * latency is unbounded), plugin hosts whose callbacks hand a plugin only its
+ * input/output buffers and a stream, and foreign-language callers without a
+ * CUDA allocator.  Same descriptor and plan as mb_gemm, but d->workspace is
+ * ignored: split-K scratch comes from a buffer compiled into the library,
+ * MB_NOALLOC_SCRATCH_BYTES per GPU, held by every GPU that loads the library
+ * until the process exits.  A plan that needs more scratch than that is
+ * rejected with MB_ERR_WORKSPACE (set split_k = 1 to run it without scratch).
+ * The call allocates nothing: no cudaMalloc / cudaFree, no allocating library
+ * routine.  The first call on a device looks up the buffer's device address
+ * (per-device set-up); make that first call before any stream capture.  All
+ * calls on a device share the one buffer, which keeps the last call's
+ * contents; its counters are cleared on the call's stream before use.  Calls
+ * that overlap on the GPU (e.g. on two streams at once) race on the buffer:
+ * keep them ordered on one stream. */
+#define MB_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
+int mb_gemm_noalloc(const mb_gemm_desc *d, void *stream);
+
 /* Bytes of workspace mb_gemm needs for this descriptor's plan (0 if none).
  * Replaces the split-K partial pool of metalblas/float_dispatch.py:183-192. */
 int64_t mb_gemm_workspace_size(const mb_gemm_desc *d);

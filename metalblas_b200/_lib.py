@@ -33,7 +33,7 @@ DTYPE_CODE = {
 
 # Every symbol the header declares (checked by the CPU test suite).
 EXPORTS = (
-    "mb_gemm_desc_init", "mb_gemm", "mb_gemm_workspace_size", "mb_plan_query",
+    "mb_gemm_desc_init", "mb_gemm", "mb_gemm_noalloc", "mb_gemm_workspace_size", "mb_plan_query",
     "mb_last_error_string", "mb_device_status", "mb_device_status_clear",
     "mb_debug_wait_timeout", "mb_abi_version", "mb_built_sm",
 )
@@ -84,6 +84,8 @@ def load():
         lib.mb_gemm_desc_init.restype = None
         lib.mb_gemm.argtypes = [P, ctypes.c_void_p]
         lib.mb_gemm.restype = ctypes.c_int
+        lib.mb_gemm_noalloc.argtypes = [P, ctypes.c_void_p]
+        lib.mb_gemm_noalloc.restype = ctypes.c_int
         lib.mb_gemm_workspace_size.argtypes = [P]
         lib.mb_gemm_workspace_size.restype = ctypes.c_int64
         lib.mb_plan_query.argtypes = [P, ctypes.c_char_p, ctypes.c_int]

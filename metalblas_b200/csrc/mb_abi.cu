@@ -623,6 +623,92 @@ int mb_gemm(const mb_gemm_desc *d, void *stream) {
   });
 }
 
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of mb_gemm.
+//
+// Some callers of this library cannot call cudaMalloc and have no workspace to
+// hand over: inference runtimes that reserve all device memory at start-up and
+// forbid allocation on the request path (cudaMalloc may synchronise the device
+// and its latency is unbounded), plugin hosts whose per-layer callback passes a
+// plugin nothing but its input/output buffers and a stream, and foreign-language
+// callers of the C ABI that have no CUDA allocator of their own.  For them the
+// split-K scratch lives in this file-scope device array, of fixed size
+// MB_NOALLOC_SCRATCH_BYTES, which every GPU that loads the library holds until
+// the process exits.
+//
+// In host code `g_noalloc_scratch` names a host-side stand-in, not a device
+// address, so its device address is looked up with cudaGetSymbolAddress once
+// per device (with that device current) and that pointer is what the kernels
+// get.  Every call on a device shares the array and it keeps the last call's
+// contents: the ticket counters, which must start at zero, are cleared on the
+// call's stream before each launch that uses them, and calls that overlap on
+// the GPU (for example on two streams at once) race on the array.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[MB_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+std::mutex g_noalloc_mu;
+void *g_noalloc_ptr[64] = {nullptr};
+
+// Device address of the scratch array on the current device (set-up on the
+// first call for that device).
+int noalloc_scratch(void **out) {
+  int dev = 0;
+  int rc = current_device(&dev);
+  if (rc) return rc;
+  if (dev < 0 || dev >= 64) return fail(MB_ERR_UNSUPPORTED, "device index %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void *p = nullptr;
+    rc = cuda_check(cudaGetSymbolAddress(&p, g_noalloc_scratch), "cudaGetSymbolAddress(g_noalloc_scratch)");
+    if (rc) return rc;
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return MB_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int mb_gemm_noalloc(const mb_gemm_desc *d, void *stream) {
+  if (!d) return fail(MB_ERR_INVALID, "null descriptor");
+  // Same plan as mb_gemm given a workspace; d->workspace is ignored.
+  mb_gemm_desc q = *d;
+  q.workspace = nullptr;
+  q.workspace_bytes = -1;
+  Plan pl; Op o; int sms;
+  int rc = plan_for(&q, pl, o, sms);
+  if (rc) return rc;
+  if (pl.kind == PK_EMPTY) return MB_OK;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  void *scratch = nullptr;
+  if (pl.ws_bytes > 0) {
+    if (pl.ws_bytes > (int64_t)MB_NOALLOC_SCRATCH_BYTES)
+      return fail(MB_ERR_WORKSPACE,
+                  "mb_gemm_noalloc: this plan needs %lld bytes of split-K scratch but the built-in scratch "
+                  "holds %lld bytes; set split_k=1 (no scratch) or call mb_gemm with a workspace",
+                  (long long)pl.ws_bytes, (long long)MB_NOALLOC_SCRATCH_BYTES);
+    rc = noalloc_scratch(&scratch);
+    if (rc) return rc;
+    rc = cuda_check(cudaMemsetAsync(scratch, 0, (size_t)kTicketBytes, st), "clear noalloc ticket counters");
+    if (rc) return rc;
+  }
+  const EpiScalars e = make_epi(d);
+  return by_dtype(d->dtype, [&](auto *tag) -> int {
+    using T = std::remove_pointer_t<decltype(tag)>;
+    switch (pl.kind) {
+      case PK_GEMV_COLS:
+      case PK_GEMV_ROWS: return launch_gemv<T>(pl, e, scratch, st);
+      case PK_TC:
+        if constexpr (IsTc<T>::v) return launch_tc<T>(pl.swap ? swapped(o) : o, pl, e, scratch, sms, st);
+        else return fail(MB_ERR_UNSUPPORTED, "tensor-core path for non-TC dtype");
+      default: return launch_simt<T>(o, e, st);
+    }
+  });
+}
+
 const char *mb_last_error_string(void) { return g_err.c_str(); }
 
 int mb_device_status(void) {
