@@ -134,6 +134,8 @@ struct Plan {
   // TC (operands already swapped when swap == 1)
   int swap = 0, bn = 0, splits = 1;
   int64_t tiles_m = 0, tiles_n = 0, kb_total = 0, kb_per_split = 0;
+  int64_t dp_tiles = 0;  // whole tiles; tiles after them are split `splits` ways along K,
+  int tail_half = 0;     // or (tail_half) into two half-width units each
   int a_mn = 0, b_mn = 0;
   // shared
   int64_t ws_bytes = 0;
@@ -198,9 +200,14 @@ bool tc_layout_ok(const Op &o, int bn, int &a_mn, int &b_mn, std::string *why) {
   return true;
 }
 
-// Cycles per K-block of a 128 x BN tile: tensor time vs. shared-memory operand
-// bandwidth (128 B/clk/SM), four UMMA K-steps per block.
-double kblock_cycles(int bn) { return 4.0 * std::max(bn / 2.0, 32.0 + bn / 4.0); }
+// Cycles per 128-byte K-block of a 128 x BN tile on one SM.  Measured on the
+// B200 (4096^3 .. 8192^3 bf16, warm L2) the mainloop is bounded by operand
+// traffic into shared memory at ~45 B/clk/SM rather than by the nominal UMMA
+// rate (BN/2 cycles per K=16 step); the model takes the slower of the two.
+double kblock_cycles(int bn) { return std::max(2.0 * bn, (128.0 + bn) * 128.0 / 45.0); }
+
+// HBM bytes per clock per SM when every SM streams (6537 GB/s / 148 / 1.965 GHz).
+constexpr double kHbmBytesPerClkPerSm = 22.4;
 
 void choose_tc_tile(const Op &o, int sms, int force_bn, int force_split, bool have_ws, Plan &pl) {
   const int esz = elem_size(o.dt);
@@ -208,33 +215,61 @@ void choose_tc_tile(const Op &o, int sms, int force_bn, int force_split, bool ha
   const int64_t kb_total = ceil_div(o.K, BK);
   static const int bns[] = {16, 32, 64, 128, 256};
   double best = 1e300;
+  const double opnd_bytes =
+      (double)(o.M * o.K * (o.sA ? o.batch : 1) + o.N * o.K * (o.sB ? o.batch : 1)) * esz +
+      (double)(o.M * o.N * o.batch) * esz;
+  auto consider = [&](double compute, double units, double waves, double extra_bytes, int bn, int am, int bm,
+                      int seff, int64_t kbp, int64_t dp, int half) {
+    // HBM floor, streamed by the SMs busy on average across the waves
+    const double avg_active = units / std::max(1.0, waves);
+    const double mem = (opnd_bytes + extra_bytes) / (kHbmBytesPerClkPerSm * avg_active);
+    const double t = std::max(compute, mem) * (1.0 + 0.002 * seff);
+    if (t < best) {
+      best = t;
+      pl.bn = bn; pl.splits = seff; pl.a_mn = am; pl.b_mn = bm;
+      pl.tiles_m = ceil_div(o.M, 128); pl.tiles_n = ceil_div(o.N, bn);
+      pl.kb_total = kb_total; pl.kb_per_split = kbp;
+      pl.dp_tiles = dp; pl.tail_half = half;
+    }
+  };
   for (int bn : bns) {
     if (force_bn && bn != force_bn) continue;
     int am, bm;
     if (!tc_layout_ok(o, bn, am, bm, nullptr)) continue;
     if (!force_bn && bn > 16 && round_up(o.N, 16) <= bn / 2) continue;  // a smaller tile already covers N
     const int64_t tiles = o.batch * ceil_div(o.M, 128) * ceil_div(o.N, bn);
-    int max_split = have_ws ? (int)std::min<int64_t>(kb_total, 32) : 1;
-    if (tiles * 4 > kMaxTickets) max_split = 1;  // not enough ticket counters
-    for (int s = 1; s <= max_split; ++s) {
+    const double unit_full = kb_total * kblock_cycles(bn) + 4.0 * bn;
+    if (!force_split || force_split == 1) {
+      // whole tiles
+      const int64_t w = ceil_div(tiles, sms);
+      consider(w * unit_full, (double)tiles, (double)w, 0.0, bn, am, bm, 1, kb_total, tiles, 0);
+      // whole tiles for the full waves, half-width units for the tiles left over
+      const bool half_ok = bn >= 128 && (!bm || (bn / 2) * esz >= 128);
+      if (half_ok && tiles > sms && tiles % sms) {
+        const int64_t dp = (tiles / sms) * sms;
+        const int64_t tail_units = 2 * (tiles - dp);
+        const double unit_half = kb_total * kblock_cycles(bn / 2) + 2.0 * bn;
+        const double waves = (double)(dp / sms + ceil_div(tail_units, sms));
+        consider((dp / sms) * unit_full + ceil_div(tail_units, sms) * unit_half, (double)(dp + tail_units), waves,
+                 0.0, bn, am, bm, 1, kb_total, dp, 1);
+      }
+    }
+    // every tile split along K (long-K, few tiles: skinny and thin shapes)
+    int max_split = have_ws ? (int)std::min<int64_t>(kb_total, 64) : 1;
+    if (tiles * tc::NUM_EPI_WARPS > kMaxTickets) max_split = 1;  // ticket counters
+    for (int s = 2; s <= max_split; ++s) {
       if (force_split && s != force_split) continue;
       const int64_t kbp = ceil_div(kb_total, s);
       const int64_t seff = ceil_div(kb_total, kbp);
       if (seff != s && !force_split) continue;
+      // a split unit writes 128 x BN fp32 partials and the last warp to arrive
+      // re-reads all of them before the epilogue: measured far costlier than a
+      // whole-tile epilogue, so it is charged per split and per column
+      const double unit_split = kbp * kblock_cycles(bn) + 4.0 * bn + 16.0 * seff * bn;
       const int64_t units = tiles * seff;
-      const int64_t waves = ceil_div(units, sms);
-      double unit = kbp * kblock_cycles(bn) + 2.0 * bn + (seff > 1 ? 12.0 * seff * bn : 0.0);
-      // memory floor: operands streamed at ~22 B/clk per active SM
-      const double active = (double)std::min<int64_t>(units, sms);
-      const double bytes = (double)(o.M * o.K * (o.sA ? o.batch : 1) + o.N * o.K * (o.sB ? o.batch : 1)) * esz;
-      const double mem = bytes / (22.0 * active * (units > sms ? 1.0 : 1.0));
-      const double t = std::max(waves * unit, mem) * (1.0 + 0.002 * seff);
-      if (t < best) {
-        best = t;
-        pl.bn = bn; pl.splits = (int)seff; pl.a_mn = am; pl.b_mn = bm;
-        pl.tiles_m = ceil_div(o.M, 128); pl.tiles_n = ceil_div(o.N, bn);
-        pl.kb_total = kb_total; pl.kb_per_split = kbp;
-      }
+      const int64_t w = ceil_div(units, sms);
+      consider(w * unit_split, (double)units, (double)w, (double)tiles * seff * 128.0 * bn * 8.0, bn, am, bm,
+               (int)seff, kbp, 0, 0);
     }
   }
 }
@@ -246,8 +281,11 @@ bool plan_tc(const Op &o, int sms, const mb_gemm_desc *d, bool have_ws, Plan &pl
   if (!pl.bn) return false;
   pl.kind = PK_TC;
   const int64_t tiles = o.batch * pl.tiles_m * pl.tiles_n;
-  if (pl.splits > 1) {
-    pl.ws_bytes = kTicketBytes + tiles * pl.splits * 128 * pl.bn * 4;
+  if (pl.splits > 1 && tiles > pl.dp_tiles) {
+    pl.ws_bytes = kTicketBytes + (tiles - pl.dp_tiles) * pl.splits * 128 * pl.bn * 4;
+  } else if (!pl.tail_half) {
+    pl.splits = 1;
+    pl.dp_tiles = tiles;
   }
   return true;
 }
@@ -440,7 +478,8 @@ CUtensorMapDataType tma_dtype(int dt) {
 
 // 3-D tiled map {inner, outer, batch} with SWIZZLE_128B.
 int encode_map(CUtensorMap *m, int dt, const void *base, int64_t inner, int64_t outer, int64_t batch,
-               int64_t outer_stride_el, int64_t batch_stride_el, int box_inner, int box_outer) {
+               int64_t outer_stride_el, int64_t batch_stride_el, int box_inner, int box_outer,
+               CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
   auto enc = get_encode();
   if (!enc) return fail(MB_ERR_LAUNCH, "cuTensorMapEncodeTiled unavailable");
   const int esz = elem_size(dt);
@@ -452,7 +491,7 @@ int encode_map(CUtensorMap *m, int dt, const void *base, int64_t inner, int64_t 
   cuuint32_t box[3] = {(cuuint32_t)box_inner, (cuuint32_t)box_outer, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = enc(m, tma_dtype(dt), 3, const_cast<void *>(base), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(MB_ERR_LAUNCH, "cuTensorMapEncodeTiled failed (%d)", (int)r);
   return MB_OK;
@@ -478,14 +517,24 @@ int launch_tc_bn(const Op &o, const Plan &pl, const EpiScalars &e, void *ws, int
   p.a_bcast = o.sA == 0; p.b_bcast = o.sB == 0;
   p.tiles_m = (int)pl.tiles_m; p.tiles_n = (int)pl.tiles_n;
   p.splits = pl.splits; p.kb_total = (int)pl.kb_total; p.kb_per_split = (int)pl.kb_per_split;
-  const int64_t units = o.batch * pl.tiles_m * pl.tiles_n * pl.splits;
+  const int64_t tiles = o.batch * pl.tiles_m * pl.tiles_n;
+  const int64_t units = pl.dp_tiles + (tiles - pl.dp_tiles) * (pl.tail_half ? 2 : pl.splits);
   if (units >= (1ll << 31)) return fail(MB_ERR_INVALID, "too many tiles");
+  p.dp_tiles = (int)pl.dp_tiles;
+  p.tail_half = pl.tail_half;
   p.num_units = (int)units;
   p.group_m = 16;
   p.C = o.C; p.c_rs = o.c_rs; p.c_cs = o.c_cs; p.sC = o.sC;
   p.bias = o.bias; p.bias_rs = o.bias_rs; p.bias_cs = o.bias_cs; p.bias_bs = o.bias_bs;
   p.epi = e;
   p.c_vec = (o.c_cs == 1 && aligned16(o.C) && (o.c_rs * ESZ) % 16 == 0 && (o.batch <= 1 || (o.sC * ESZ) % 16 == 0)) ? 1 : 0;
+  // Row-major output that TMA can address: staged epilogue with TMA stores.
+  if (C_::TMA_STORE && p.c_vec && o.c_rs >= o.N && o.sC >= 0 && (o.batch <= 1 || o.sC >= o.c_rs * o.M || o.sC == 0) &&
+      o.N < (1ll << 31) && o.M < (1ll << 31)) {
+    const int64_t bC = o.batch > 1 ? o.batch : 1;
+    if (encode_map(&p.tmC, o.dt, o.C, o.N, o.M, bC, o.c_rs, o.sC, C_::CC, 32, CU_TENSOR_MAP_SWIZZLE_64B) == MB_OK)
+      p.c_tma = 1;
+  }
   if (pl.splits > 1) {
     p.tickets = reinterpret_cast<unsigned *>(ws);
     p.ws = reinterpret_cast<char *>(ws) + kTicketBytes;
@@ -541,13 +590,15 @@ template <> struct IsTc<__nv_bfloat16> { static constexpr bool v = true; };
 template <> struct IsTc<int8_t> { static constexpr bool v = true; };
 template <> struct IsTc<uint8_t> { static constexpr bool v = true; };
 
-int plan_for(const mb_gemm_desc *d, Plan &pl, Op &o, int &sms) {
+// `query`: plan without a device if none is present (a B200's 148 SMs are
+// assumed), so the tile table can be inspected on a host without a GPU.
+int plan_for(const mb_gemm_desc *d, Plan &pl, Op &o, int &sms, bool query = false) {
   int rc = validate(d);
   if (rc) return rc;
   int dev = 0;
   rc = current_device(&dev);
-  if (rc) return rc;
-  sms = num_sms(dev);
+  if (rc && !query) return rc;
+  sms = rc ? 148 : num_sms(dev);
   o = make_op(d);
   const bool have_ws = d->workspace != nullptr || d->workspace_bytes < 0;  // <0: size query
   return make_plan(d, o, sms, have_ws, pl);
@@ -573,13 +624,13 @@ int64_t mb_gemm_workspace_size(const mb_gemm_desc *d) {
   q.workspace = nullptr;
   q.workspace_bytes = -1;  // plan as if a workspace were available
   Plan pl; Op o; int sms;
-  if (plan_for(&q, pl, o, sms)) return 0;
+  if (plan_for(&q, pl, o, sms, true)) return 0;
   return pl.ws_bytes;
 }
 
 int mb_plan_query(const mb_gemm_desc *d, char *buf, int buflen) {
   Plan pl; Op o; int sms;
-  int rc = plan_for(d, pl, o, sms);
+  int rc = plan_for(d, pl, o, sms, true);
   if (rc) return -rc;
   char tmp[256];
   switch (pl.kind) {
@@ -587,9 +638,9 @@ int mb_plan_query(const mb_gemm_desc *d, char *buf, int buflen) {
     case PK_GEMV_COLS: snprintf(tmp, sizeof(tmp), "gemv_cols vec=%d ksplit=%d", pl.vec, pl.g.ksplit); break;
     case PK_GEMV_ROWS: snprintf(tmp, sizeof(tmp), "gemv_rows vec=%d", pl.vec); break;
     case PK_TC:
-      snprintf(tmp, sizeof(tmp), "tc bn=%d split=%d swap=%d a_mn=%d b_mn=%d tiles=%lldx%lld ws=%lld", pl.bn,
-               pl.splits, pl.swap, pl.a_mn, pl.b_mn, (long long)pl.tiles_m, (long long)pl.tiles_n,
-               (long long)pl.ws_bytes);
+      snprintf(tmp, sizeof(tmp), "tc bn=%d split=%d dp=%lld half=%d swap=%d a_mn=%d b_mn=%d tiles=%lldx%lld ws=%lld",
+               pl.bn, pl.splits, (long long)pl.dp_tiles, pl.tail_half, pl.swap, pl.a_mn, pl.b_mn,
+               (long long)pl.tiles_m, (long long)pl.tiles_n, (long long)pl.ws_bytes);
       break;
     default: snprintf(tmp, sizeof(tmp), "simt"); break;
   }

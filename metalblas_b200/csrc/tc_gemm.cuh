@@ -16,17 +16,26 @@
 //               (M=128, N=BN, K=16 for 16-bit / 32 for 8-bit) into one of two
 //               TMEM accumulators, releasing each smem stage with
 //               tcgen05.commit -> empty barrier.
-//   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns per warp, apply
-//               alpha/beta/bias (mb_epi semantics), convert, store; or, for a
-//               split-K unit, publish fp32/int32 partials and let the last CTA
-//               to draw a ticket reduce them in split order.
+//   warps 2..9  epilogue, two warps per TMEM lane quarter (each takes half of
+//               the tile's columns): tcgen05.ld, alpha/beta/bias (mb_epi
+//               semantics), convert, then either a 128B-swizzled staging tile in
+//               shared memory written back by a TMA store (row-major outputs)
+//               or direct stores (transposed / unaligned outputs).  For a
+//               split-K unit the raw accumulators go to the workspace and the
+//               last warp to draw a ticket for its slice reduces them in order.
 // The two TMEM accumulators let the epilogue of tile i overlap the mainloop of
 // tile i+1.
+//
+// Schedule: units are whole output tiles, except that when the tiles do not
+// fill the last wave of the grid, the leftover tiles ("tail") are split along K
+// so the last wave is full as well (dp_tiles whole tiles first, then
+// (tiles - dp_tiles) * splits split units).
 //
 // Operand layouts: each operand may be K-major or MN-major in global memory;
 // TMA copies it into the matching canonical SWIZZLE_128B layout and the UMMA
 // instruction descriptor's major bits say which.  Tile edges in M, N and K are
-// zero-filled by TMA (out-of-bounds fill), and the epilogue masks stores.
+// zero-filled by TMA (out-of-bounds fill); TMA stores clip at the edges and the
+// direct-store path masks.
 //
 // Every mbarrier wait is bounded by a %globaltimer deadline; a wait that runs
 // out records MB_ERR_DEVICE_TIMEOUT in g_mb_status, raises a CTA-wide abort
@@ -35,21 +44,30 @@
 #pragma once
 #include <cuda.h>
 #include "mb_common.cuh"
+#include <type_traits>
 
 namespace mb {
 namespace tc {
 
 constexpr int BM = 128;                 // UMMA M (cta_group::1)
-constexpr int NUM_THREADS = 192;        // 6 warps
-constexpr int SMEM_BUDGET = 200 * 1024; // operand ring budget (bytes)
+constexpr int NUM_EPI_WARPS = 8;
+constexpr int NUM_THREADS = 64 + 32 * NUM_EPI_WARPS;
+constexpr int SMEM_LIMIT = 232448;      // max dynamic shared memory per CTA on sm_100
+constexpr int STAGING_ROW = 64;             // bytes per staged output row (SWIZZLE_64B)
+constexpr int STAGING_BUF = 32 * STAGING_ROW;  // one 32-row box
+constexpr int STAGING_PER_WARP = 2 * STAGING_BUF;  // double-buffered
 
 struct TcParams {
   CUtensorMap tmA;   // UMMA-A operand (rows of C), 3-D {inner, outer, batch}
   CUtensorMap tmB;   // UMMA-B operand (cols of C)
+  CUtensorMap tmC;   // output, 3-D {N, M, batch}, box {64 B, 32 rows}, SWIZZLE_64B; valid when c_tma
   int M, N, K, batch;
   int a_mn, b_mn;        // operand is MN-major in global memory
   int a_bcast, b_bcast;  // batch stride 0: always load batch 0
   int tiles_m, tiles_n, splits, kb_total, kb_per_split;
+  int dp_tiles;          // tiles [0, dp_tiles) run whole; later ("tail") tiles are either
+  int tail_half;         //   split into two half-width (BN/2) units (tail_half = 1) or
+                         //   split along K `splits` ways (tail_half = 0)
   int num_units, group_m;
   void *C;
   int64_t c_rs, c_cs, sC;
@@ -57,8 +75,9 @@ struct TcParams {
   int64_t bias_rs, bias_cs, bias_bs;
   EpiScalars epi;
   int c_vec;             // c_cs == 1 and every row start is 16-byte aligned
-  void *ws;              // split-K partials: num_tiles * splits * BM * BN * 4 bytes
-  unsigned *tickets;     // four per output tile (one per epilogue warp), zero on entry and exit
+  int c_tma;             // write C through tmC
+  void *ws;              // split-K partials: tail_tiles * splits * BM * BN * 4 bytes
+  unsigned *tickets;     // NUM_EPI_WARPS per tail tile, zero on entry and exit
   unsigned long long timeout_ns;
 };
 
@@ -70,14 +89,22 @@ struct Cfg {
   static constexpr int A_BYTES = BM * 128;
   static constexpr int B_BYTES = BN * 128;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES_RAW = SMEM_BUDGET / STAGE_BYTES;
+  static constexpr int HALF = BN / 2;           // columns per epilogue warp (whole-tile unit)
+  static constexpr int QUART = BN / 4;          // columns per epilogue warp (half-width unit)
+  static constexpr int CC = STAGING_ROW / ESZ;  // columns per staged row
+  static constexpr bool TMA_STORE = (QUART % CC) == 0;
+  static constexpr int STAGING_BYTES = TMA_STORE ? NUM_EPI_WARPS * STAGING_PER_WARP : 0;
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int STAGES_RAW = (SMEM_LIMIT - 1024 - STAGING_BYTES - BAR_BYTES) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
   static constexpr int ACC_COLS = BN;           // fp32/s32: one column per N
   static constexpr int TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
-  static constexpr int BAR_BYTES = (2 * STAGES + 4 + 1) * 8;
-  static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + BAR_BYTES + 16;
+  static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + STAGING_BYTES + BAR_BYTES;
+  static constexpr int RCH = QUART < 32 ? (QUART < 8 ? 8 : QUART) : 32;  // columns per tcgen05.ld, direct path
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N for M=128");
   static_assert(STAGES >= 2, "need a pipeline");
+  static_assert(SMEM_BYTES <= SMEM_LIMIT, "shared memory");
+  static_assert(2 * STAGES + 5 <= BAR_BYTES / 8 - 2, "barrier area");
 };
 
 // ---------------------------------------------------------------------------
@@ -192,6 +219,34 @@ __device__ __forceinline__ void tmem_ld_x16(uint32_t taddr, uint32_t (&r)[32]) {
         "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
 }
+__device__ __forceinline__ void tmem_ld_x8(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+template <int N>
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[32]) {
+  if constexpr (N == 32) tmem_ld_x32(taddr, r);
+  else if constexpr (N == 16) tmem_ld_x16(taddr, r);
+  else tmem_ld_x8(taddr, r);
+}
+// TMA store of a shared-memory box to global (bulk async-group completion).
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap *map, uint32_t src, int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(src), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// The source shared memory of every committed bulk store may be reused.
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// Every committed bulk store has completed.
+__device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// Generic-proxy shared-memory writes become visible to the async (TMA) proxy.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // Shared-memory matrix descriptor, SWIZZLE_128B, sm100 version bits.
@@ -220,16 +275,37 @@ __device__ __forceinline__ uint32_t make_idesc(int a_mn, int b_mn) {
 }
 
 struct Unit {
-  int b, tm, tn, s, tile;
+  int b, tm, tn;
+  int tile;          // raster index over all output tiles
+  int s;             // split index (0 unless a K-split unit)
+  int kb0, kb1;      // K-blocks of this unit
+  bool split;        // partial-sum unit (tail tile split along K)
+  int half;          // -1: whole tile; 0/1: which half-width (BN/2 columns) of the tile
+  int tail;          // tile - dp_tiles (valid for tail units)
 };
 __device__ __forceinline__ Unit decode_unit(const TcParams &p, int u) {
   Unit r;
-  r.s = u % p.splits;
-  const int t = u / p.splits;
-  r.tile = t;
+  r.s = 0; r.split = false; r.half = -1; r.tail = 0;
+  r.kb0 = 0; r.kb1 = p.kb_total;
+  if (u < p.dp_tiles) {
+    r.tile = u;
+  } else if (p.tail_half) {
+    const int v = u - p.dp_tiles;
+    r.tail = v >> 1;
+    r.tile = p.dp_tiles + r.tail;
+    r.half = v & 1;
+  } else {
+    const int v = u - p.dp_tiles;
+    r.tail = v / p.splits;
+    r.tile = p.dp_tiles + r.tail;
+    r.s = v % p.splits;
+    r.split = true;
+    r.kb0 = r.s * p.kb_per_split;
+    r.kb1 = min(p.kb_total, r.kb0 + p.kb_per_split);
+  }
   const int per_batch = p.tiles_m * p.tiles_n;
-  r.b = t / per_batch;
-  const int q = t % per_batch;
+  r.b = r.tile / per_batch;
+  const int q = r.tile % per_batch;
   const int per_group = p.group_m * p.tiles_n;
   const int g = q / per_group;
   const int first_m = g * p.group_m;
@@ -246,31 +322,70 @@ __device__ __forceinline__ typename Elem<T>::acc acc_from_bits(uint32_t bits) {
   else return __uint_as_float(bits);
 }
 
-// Store 32 consecutive columns of one output row (or fewer at the right edge).
+// Epilogue value of C(m, n) from its raw accumulator bits.
 template <class T>
-__device__ __forceinline__ void store_row_chunk(const TcParams &p, int b, int m, int n0, int ncols,
-                                                const uint32_t (&r)[32]) {
-  using E = Elem<T>;
-  T *C = (T *)p.C + (int64_t)b * p.sC;
-  const T *bias = (const T *)p.bias + (p.epi.enabled ? (int64_t)b * p.bias_bs : 0);
-  T out[32];
-#pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    typename E::acc v = acc_from_bits<T>(r[j]);
-    if (j < ncols && p.epi.enabled && n0 + j < p.N)
-      v = EpiOps<T>::apply(v, bias + (int64_t)m * p.bias_rs + (int64_t)(n0 + j) * p.bias_cs, p.epi);
-    out[j] = E::store(v);
+__device__ __forceinline__ T epi_value(const TcParams &p, int b, int m, int n, uint32_t bits) {
+  typename Elem<T>::acc v = acc_from_bits<T>(bits);
+  if (p.epi.enabled && m < p.M && n < p.N) {
+    const T *bias = (const T *)p.bias + (int64_t)b * p.bias_bs;
+    v = EpiOps<T>::apply(v, bias + (int64_t)m * p.bias_rs + (int64_t)n * p.bias_cs, p.epi);
   }
-  if (p.c_vec && ncols == 32 && n0 + 32 <= p.N) {
-    constexpr int PER16 = 16 / sizeof(T);
+  return Elem<T>::store(v);
+}
+
+// Direct stores of NC (<= 32) consecutive columns of one output row.
+template <class T, int NC>
+__device__ __forceinline__ void store_row_chunk(const TcParams &p, int b, int m, int n0, const uint32_t (&r)[32]) {
+  T *C = (T *)p.C + (int64_t)b * p.sC;
+  T out[NC];
+#pragma unroll
+  for (int j = 0; j < NC; ++j) out[j] = epi_value<T>(p, b, m, n0 + j, r[j]);
+  constexpr int PER16 = 16 / sizeof(T);
+  if (NC % PER16 == 0 && p.c_vec && n0 + NC <= p.N) {
     uint4 *dst = reinterpret_cast<uint4 *>(C + (int64_t)m * p.c_rs + n0);
 #pragma unroll
-    for (int v = 0; v < 32 / PER16; ++v) dst[v] = *reinterpret_cast<const uint4 *>(&out[v * PER16]);
+    for (int v = 0; v < NC / PER16; ++v) dst[v] = *reinterpret_cast<const uint4 *>(&out[v * PER16]);
   } else {
 #pragma unroll
-    for (int j = 0; j < 32; ++j)
-      if (j < ncols && n0 + j < p.N) C[(int64_t)m * p.c_rs + (int64_t)(n0 + j) * p.c_cs] = out[j];
+    for (int j = 0; j < NC; ++j)
+      if (n0 + j < p.N) C[(int64_t)m * p.c_rs + (int64_t)(n0 + j) * p.c_cs] = out[j];
   }
+}
+
+// Convert 32 raw accumulators of C(m, n0..n0+31) to packed output words
+// (32 * sizeof(T) / 4 words).  The plain product (no epilogue) is branch-free:
+// pairs of fp32 round with one cvt to bf16x2 / f16x2, 8-bit outputs keep the
+// low byte of each s32 (two's-complement wrap) via byte permutes.
+template <class T>
+__device__ __forceinline__ void pack32(const TcParams &p, int b, int m, int n0, const uint32_t (&r)[32],
+                                       uint32_t (&pk)[32 * sizeof(T) / 4]) {
+  if (!p.epi.enabled) {
+    if constexpr (sizeof(T) == 2) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        if constexpr (std::is_same_v<T, __nv_bfloat16>) {
+          __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
+          pk[j] = *reinterpret_cast<uint32_t *>(&h);
+        } else {
+          __half2 h = __floats2half2_rn(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
+          pk[j] = *reinterpret_cast<uint32_t *>(&h);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const uint32_t lo = __byte_perm(r[4 * j], r[4 * j + 1], 0x0040);
+        const uint32_t hi = __byte_perm(r[4 * j + 2], r[4 * j + 3], 0x0040);
+        pk[j] = __byte_perm(lo, hi, 0x5410);
+      }
+    }
+    return;
+  }
+  T out[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) out[j] = epi_value<T>(p, b, m, n0 + j, r[j]);
+#pragma unroll
+  for (int j = 0; j < 32 * (int)sizeof(T) / 4; ++j) pk[j] = reinterpret_cast<const uint32_t *>(out)[j];
 }
 
 // ---------------------------------------------------------------------------
@@ -279,14 +394,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
   constexpr int ESZ = sizeof(T);
   using C_ = Cfg<BN, ESZ>;
   constexpr int BK = C_::BK, STAGES = C_::STAGES;
-  constexpr uint32_t A_BYTES = C_::A_BYTES, B_BYTES = C_::B_BYTES, STAGE_BYTES = C_::STAGE_BYTES;
-  constexpr int CHUNK = BN < 32 ? BN : 32;  // columns per tcgen05.ld
+  constexpr uint32_t A_BYTES = C_::A_BYTES, STAGE_BYTES = C_::STAGE_BYTES;
+  constexpr int RCH = C_::RCH, CC = C_::CC;
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  // 1024-byte alignment for the swizzled operand tiles.
+  // 1024-byte alignment for the swizzled operand and staging tiles.
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t *ring = smem;
-  uint64_t *bars = reinterpret_cast<uint64_t *>(ring + STAGES * STAGE_BYTES);
+  uint8_t *staging = ring + STAGES * STAGE_BYTES;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(staging + C_::STAGING_BYTES);
   // bars: full[STAGES], empty[STAGES], tfull[2], tempty[2], drain
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 5);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
@@ -307,13 +423,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(tfull_bar(a), 1);
-      mbar_init(tempty_bar(a), 4);
+      mbar_init(tempty_bar(a), NUM_EPI_WARPS);
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
     fence_mbar_init();
     prefetch_tmap(&p.tmA);
     prefetch_tmap(&p.tmB);
+    if (p.c_tma) prefetch_tmap(&p.tmC);
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), C_::TMEM_COLS);
@@ -333,12 +450,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
       uint32_t issued_phase = 0;
       for (int u = blockIdx.x; u < p.num_units; u += gridDim.x) {
         const Unit w = decode_unit(p, u);
-        const int kb0 = w.s * p.kb_per_split;
-        const int kb1 = min(p.kb_total, kb0 + p.kb_per_split);
         const int ba = p.a_bcast ? 0 : w.b, bb = p.b_bcast ? 0 : w.b;
-        for (int kb = kb0; kb < kb1; ++kb) {
+        // A half-width unit loads only its BN/2 columns of an MN-major B; a
+        // K-major B tile is one box, loaded whole.
+        const bool half_b = w.half >= 0 && p.b_mn;
+        const uint32_t b_bytes = half_b ? (uint32_t)(BN / 2) * 128u : (uint32_t)BN * 128u;
+        const int b_boxes = (half_b ? BN / 2 : BN) * ESZ / 128;
+        const int b_col0 = w.tn * BN + (half_b ? w.half * (BN / 2) : 0);
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag, p.timeout_ns)) goto producer_done;
-          mbar_arrive_expect_tx(full_bar(stage), STAGE_BYTES);
+          mbar_arrive_expect_tx(full_bar(stage), A_BYTES + b_bytes);
           const uint32_t sa = ring_u32 + stage * STAGE_BYTES;
           const uint32_t sb = sa + A_BYTES;
           if (!p.a_mn) {
@@ -351,9 +472,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
           if (!p.b_mn) {
             tma_load_3d(sb, &p.tmB, full_bar(stage), kb * BK, w.tn * BN, bb);
           } else {
-#pragma unroll
-            for (int j = 0; j < BN * ESZ / 128; ++j)
-              tma_load_3d(sb + j * (BK * 128), &p.tmB, full_bar(stage), w.tn * BN + j * (128 / ESZ), kb * BK, bb);
+            for (int j = 0; j < b_boxes; ++j)
+              tma_load_3d(sb + j * (BK * 128), &p.tmB, full_bar(stage), b_col0 + j * (128 / ESZ), kb * BK, bb);
           }
           issued_stage = stage;
           issued_phase = phase;
@@ -370,7 +490,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = make_idesc<T, BN>(p.a_mn, p.b_mn);
+      const uint32_t idesc_full = make_idesc<T, BN>(p.a_mn, p.b_mn);
+      const uint32_t idesc_half = make_idesc<T, (BN >= 32 ? BN / 2 : BN)>(p.a_mn, p.b_mn);
       // Canonical SW128 layouts: K-major SBO = 8 rows * 128 B; MN-major
       // LBO = next 128-byte MN column block (one TMA box), SBO = 8 K rows.
       const uint32_t a_lbo = p.a_mn ? BK * 128 : 16, b_lbo = p.b_mn ? BK * 128 : 16;
@@ -382,22 +503,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
       bool issued_any = false;
       for (int u = blockIdx.x; u < p.num_units; u += gridDim.x) {
         const Unit w = decode_unit(p, u);
-        const int kb0 = w.s * p.kb_per_split;
-        const int kb1 = min(p.kb_total, kb0 + p.kb_per_split);
+        const uint32_t idesc = w.half >= 0 ? idesc_half : idesc_full;
+        // K-major B holds the whole tile: a half-width unit starts BN/2 rows in.
+        const uint32_t b_off = (w.half > 0 && !p.b_mn) ? (uint32_t)(BN / 2) * 128u : 0u;
         if (!mbar_wait(tempty_bar(abuf), aphase ^ 1u, abort_flag, p.timeout_ns)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(abuf * C_::ACC_COLS);
         bool aborted = false;
-        for (int kb = kb0; kb < kb1; ++kb) {
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait(full_bar(stage), phase, abort_flag, p.timeout_ns)) { aborted = true; break; }
           tc_fence_after();
           const uint32_t sa = ring_u32 + stage * STAGE_BYTES;
-          const uint32_t sb = sa + A_BYTES;
+          const uint32_t sb = sa + A_BYTES + b_off;
 #pragma unroll
           for (int ks = 0; ks < C_::KSTEPS; ++ks) {
             const uint64_t ad = sdesc(sa + ks * a_kstep, a_lbo, 1024);
             const uint64_t bd = sdesc(sb + ks * b_kstep, b_lbo, 1024);
-            umma<ESZ>(d_tmem, ad, bd, idesc, (kb > kb0 || ks > 0) ? 1u : 0u);
+            umma<ESZ>(d_tmem, ad, bd, idesc, (kb > w.kb0 || ks > 0) ? 1u : 0u);
           }
           issued_any = true;
           umma_commit(empty_bar(stage));  // frees this smem stage when the MMAs finish
@@ -416,8 +538,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int lg = warp & 3;  // TMEM lane quarter this warp may access
-    const int row = lg * 32 + lane;
+    const int ew = warp - 2;              // 0..7
+    const int q = warp & 3;               // TMEM lane quarter this warp may access
+    const int row = q * 32 + lane;
+    const uint32_t stg0 = smem_u32(staging) + (uint32_t)(ew * STAGING_PER_WARP);
+    int sbuf = 0;                         // staging buffer to fill next
     int abuf = 0;
     uint32_t aphase = 0;
     for (int u = blockIdx.x; u < p.num_units; u += gridDim.x) {
@@ -425,15 +550,76 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
       if (!mbar_wait(tfull_bar(abuf), aphase, abort_flag, p.timeout_ns)) break;
       tc_fence_after();
       const int m = w.tm * BM + row;
-      const uint32_t tbase = tmem_base + ((uint32_t)(lg * 32) << 16) + (uint32_t)(abuf * C_::ACC_COLS);
-      if (p.splits == 1) {
+      // Columns of this unit and of this warp's share (half of the unit).
+      const int ucols = w.half >= 0 ? BN / 2 : BN;
+      const int wcols = ucols / 2;
+      const int ucol0 = w.half > 0 ? BN / 2 : 0;            // unit's first column within the tile
+      const int col0 = (ew >> 2) * wcols;                    // warp's first column within the unit
+      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(abuf * C_::ACC_COLS + col0);
+      const int nbase = w.tn * BN + ucol0 + col0;            // global column of tbase
+      if (!w.split) {
+        if constexpr (C_::TMA_STORE) {
+          if (p.c_tma) {
+            // 64-byte rows staged with the SWIZZLE_64B pattern (16-byte chunk j
+            // of row r at chunk j ^ ((r >> 1) & 3)), one TMA store per 32-row
+            // box of CC columns, two staging buffers so a store overlaps the
+            // next box.  TMEM is read in 32-column sub-chunks, the next one
+            // issued before the current one is converted.
+            constexpr int SUBS = CC / 32;                // sub-chunks per staged row (1: 16-bit, 2: 8-bit)
+            constexpr int V = 32 * ESZ / 16;             // 16-byte pieces per sub-chunk
+            const int nsub = wcols / 32;
+            uint32_t ra[32];
+            tmem_ld_x32(tbase, ra);
+            for (int sc = 0; sc < nsub; ++sc) {
+              tmem_wait_ld();
+              uint32_t rb[32];
+#pragma unroll
+              for (int j = 0; j < 32; ++j) rb[j] = ra[j];
+              if (sc + 1 < nsub) {
+                tmem_ld_x32(tbase + (sc + 1) * 32, ra);
+              } else {                           // last TMEM read of this unit by this warp
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(tempty_bar(abuf));
+              }
+              const int sub = sc % SUBS;
+              const uint32_t stg = stg0 + (uint32_t)(sbuf * STAGING_BUF);
+              if (sub == 0) {                    // buffer's previous store has read it
+                if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+                __syncwarp();
+              }
+              const int n0 = nbase + sc * 32;
+              uint32_t pk[32 * ESZ / 4];
+              pack32<T>(p, w.b, m, n0, rb, pk);
+#pragma unroll
+              for (int v = 0; v < V; ++v) {
+                const int ci = sub * V + v;
+                const uint32_t addr = stg + lane * STAGING_ROW + ((ci ^ ((lane >> 1) & 3)) << 4);
+                asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(pk[4 * v]), "r"(pk[4 * v + 1]),
+                             "r"(pk[4 * v + 2]), "r"(pk[4 * v + 3])
+                             : "memory");
+              }
+              if (sub == SUBS - 1) {
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                  tma_store_3d(&p.tmC, stg, n0 - (SUBS - 1) * 32, w.tm * BM + q * 32, w.b);
+                  bulk_commit();
+                }
+                sbuf ^= 1;
+              }
+            }
+            if (++abuf == 2) { abuf = 0; aphase ^= 1u; }
+            continue;
+          }
+        }
 #pragma unroll 1
-        for (int c = 0; c < BN; c += CHUNK) {
+        for (int c = 0; c < wcols; c += RCH) {
           uint32_t r[32];
-          if constexpr (CHUNK == 32) tmem_ld_x32(tbase + c, r); else tmem_ld_x16(tbase + c, r);
+          tmem_ld<RCH>(tbase + c, r);
           tmem_wait_ld();
-          const int n0 = w.tn * BN + c;
-          if (m < p.M && n0 < p.N) store_row_chunk<T>(p, w.b, m, n0, CHUNK, r);
+          const int n0 = nbase + c;
+          if (m < p.M && n0 < p.N) store_row_chunk<T, RCH>(p, w.b, m, n0, r);
         }
         tc_fence_before();
         __syncwarp();
@@ -441,40 +627,41 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
       } else {
         // Split-K: publish raw accumulators (tile-local row-major, 4 B each).
         uint32_t *part = reinterpret_cast<uint32_t *>(p.ws) +
-                         ((int64_t)w.tile * p.splits + w.s) * (int64_t)(BM * BN) + (int64_t)row * BN;
+                         ((int64_t)w.tail * p.splits + w.s) * (int64_t)(BM * BN) + (int64_t)row * BN + col0;
 #pragma unroll 1
-        for (int c = 0; c < BN; c += CHUNK) {
+        for (int c = 0; c < wcols; c += RCH) {
           uint32_t r[32];
-          if constexpr (CHUNK == 32) tmem_ld_x32(tbase + c, r); else tmem_ld_x16(tbase + c, r);
+          tmem_ld<RCH>(tbase + c, r);
           tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < CHUNK; j += 4)
+          for (int j = 0; j < RCH; j += 4)
             __stcg(reinterpret_cast<uint4 *>(part + c + j), make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]));
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(tempty_bar(abuf));
-        // Each warp owns 32 rows of the tile and reduces them on its own:
-        // per-(tile, lane quarter) tickets, so no cross-warp barrier exists
+        // Each warp owns 32 rows x wcols columns of the tile and reduces them on
+        // its own: per-(tail tile, warp) tickets, so no cross-warp barrier exists
         // that an aborting warp could leave the others waiting at.
         __threadfence();
         __syncwarp();
         unsigned tk = 0;
-        if (lane == 0) tk = atomicAdd(p.tickets + (int64_t)w.tile * 4 + lg, 1u);
+        unsigned *ticket = p.tickets + (int64_t)w.tail * NUM_EPI_WARPS + ew;
+        if (lane == 0) tk = atomicAdd(ticket, 1u);
         tk = __shfl_sync(0xffffffffu, tk, 0);
         if (tk == (unsigned)(p.splits - 1)) {
           __threadfence();
           const uint32_t *base = reinterpret_cast<const uint32_t *>(p.ws) +
-                                 (int64_t)w.tile * p.splits * (int64_t)(BM * BN) + (int64_t)row * BN;
+                                 (int64_t)w.tail * p.splits * (int64_t)(BM * BN) + (int64_t)row * BN + col0;
 #pragma unroll 1
-          for (int c = 0; c < BN; c += CHUNK) {
+          for (int c = 0; c < wcols; c += RCH) {
             uint32_t r[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) r[j] = 0;
             for (int s = 0; s < p.splits; ++s) {
               const uint32_t *src = base + (int64_t)s * (BM * BN) + c;
 #pragma unroll
-              for (int j = 0; j < CHUNK; j += 4) {
+              for (int j = 0; j < RCH; j += 4) {
                 const uint4 v = __ldcg(reinterpret_cast<const uint4 *>(src + j));
                 if constexpr (Elem<T>::is_int) {
                   r[j] += v.x; r[j + 1] += v.y; r[j + 2] += v.z; r[j + 3] += v.w;
@@ -486,14 +673,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
                 }
               }
             }
-            const int n0 = w.tn * BN + c;
-            if (m < p.M && n0 < p.N) store_row_chunk<T>(p, w.b, m, n0, CHUNK, r);
+            const int n0 = nbase + c;
+            if (m < p.M && n0 < p.N) store_row_chunk<T, RCH>(p, w.b, m, n0, r);
           }
-          if (lane == 0) p.tickets[(int64_t)w.tile * 4 + lg] = 0u;
+          if (lane == 0) *ticket = 0u;
         }
       }
       if (++abuf == 2) { abuf = 0; aphase ^= 1u; }
     }
+    if (lane == 0) bulk_wait0();  // every TMA store of this warp has completed
+    __syncwarp();
   }
 
   tc_fence_before();
