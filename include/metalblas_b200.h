@@ -101,7 +101,7 @@ typedef struct mb_gemm_desc {
     int32_t tile_n;         /* TC: N-tile of the tcgen05 kernel (16..256)     */
     int32_t split_k;        /* TC/GEMV: number of K splits                    */
     int32_t swap_ab;        /* TC: -1 never, 0 planner decides, 1 force Cᵀ=BᵀAᵀ */
-    int32_t _pad1;
+    int32_t cta_pair;       /* TC: 0 planner decides, 1 one CTA per tile, 2 CTA pair (cta_group::2) */
     /* caller-owned scratch for split-K partials; must be zero-filled before
      * its first use; kernels leave the counter region zeroed again. */
     void *workspace;

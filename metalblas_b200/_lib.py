@@ -58,7 +58,7 @@ class GemmDesc(ctypes.Structure):
         ("beta_re", ctypes.c_double), ("beta_im", ctypes.c_double),
         ("ialpha", ctypes.c_int64), ("ibeta", ctypes.c_int64),
         ("tile_n", ctypes.c_int32), ("split_k", ctypes.c_int32), ("swap_ab", ctypes.c_int32),
-        ("_pad1", ctypes.c_int32),
+        ("cta_pair", ctypes.c_int32),
         ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_int64),
     ]
 

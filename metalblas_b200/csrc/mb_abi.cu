@@ -136,6 +136,7 @@ struct Plan {
   int64_t tiles_m = 0, tiles_n = 0, kb_total = 0, kb_per_split = 0;
   int64_t dp_tiles = 0;  // whole tiles; tiles after them are split `splits` ways along K,
   int tail_half = 0;     // or (tail_half) into two half-width units each
+  int pair = 1;          // 2: CTA-pair kernel (cta_group::2, 256-row tiles)
   int a_mn = 0, b_mn = 0;
   // shared
   int64_t ws_bytes = 0;
@@ -205,11 +206,22 @@ bool tc_layout_ok(const Op &o, int bn, int &a_mn, int &b_mn, std::string *why) {
 // traffic into shared memory at ~45 B/clk/SM rather than by the nominal UMMA
 // rate (BN/2 cycles per K=16 step); the model takes the slower of the two.
 double kblock_cycles(int bn) { return std::max(2.0 * bn, (128.0 + bn) * 128.0 / 45.0); }
+// The same for one SM of a CTA pair (cta_group::2): each SM computes 128 x BN
+// per K-block but loads only half of B's columns.  Calibrated on the B200:
+// 1.09-1.23x the single-CTA rate at BN=256 (4096^3 .. 8192^3, 2048x14336x4096).
+double kblock_cycles_pair(int bn) { return std::max(2.0 * bn, (128.0 + bn / 2.0) * 128.0 / 35.0); }
+
+// CTA-pair kernels in the tile table (METALBLAS_PAIR=0 leaves them out; they
+// can always be requested per call through mb_gemm_desc.cta_pair = 2).
+const bool g_pair_enabled = [] {
+  const char *s = getenv("METALBLAS_PAIR");
+  return !(s && s[0] == '0');
+}();
 
 // HBM bytes per clock per SM when every SM streams (6537 GB/s / 148 / 1.965 GHz).
 constexpr double kHbmBytesPerClkPerSm = 22.4;
 
-void choose_tc_tile(const Op &o, int sms, int force_bn, int force_split, bool have_ws, Plan &pl) {
+void choose_tc_tile(const Op &o, int sms, int force_bn, int force_split, int force_pair, bool have_ws, Plan &pl) {
   const int esz = elem_size(o.dt);
   const int64_t BK = 128 / esz;
   const int64_t kb_total = ceil_div(o.K, BK);
@@ -219,7 +231,7 @@ void choose_tc_tile(const Op &o, int sms, int force_bn, int force_split, bool ha
       (double)(o.M * o.K * (o.sA ? o.batch : 1) + o.N * o.K * (o.sB ? o.batch : 1)) * esz +
       (double)(o.M * o.N * o.batch) * esz;
   auto consider = [&](double compute, double units, double waves, double extra_bytes, int bn, int am, int bm,
-                      int seff, int64_t kbp, int64_t dp, int half) {
+                      int seff, int64_t kbp, int64_t dp, int half, int pair = 1) {
     // HBM floor, streamed by the SMs busy on average across the waves
     const double avg_active = units / std::max(1.0, waves);
     const double mem = (opnd_bytes + extra_bytes) / (kHbmBytesPerClkPerSm * avg_active);
@@ -227,9 +239,9 @@ void choose_tc_tile(const Op &o, int sms, int force_bn, int force_split, bool ha
     if (t < best) {
       best = t;
       pl.bn = bn; pl.splits = seff; pl.a_mn = am; pl.b_mn = bm;
-      pl.tiles_m = ceil_div(o.M, 128); pl.tiles_n = ceil_div(o.N, bn);
+      pl.tiles_m = ceil_div(o.M, 128 * pair); pl.tiles_n = ceil_div(o.N, bn);
       pl.kb_total = kb_total; pl.kb_per_split = kbp;
-      pl.dp_tiles = dp; pl.tail_half = half;
+      pl.dp_tiles = dp; pl.tail_half = half; pl.pair = pair;
     }
   };
   for (int bn : bns) {
@@ -239,7 +251,7 @@ void choose_tc_tile(const Op &o, int sms, int force_bn, int force_split, bool ha
     if (!force_bn && bn > 16 && round_up(o.N, 16) <= bn / 2) continue;  // a smaller tile already covers N
     const int64_t tiles = o.batch * ceil_div(o.M, 128) * ceil_div(o.N, bn);
     const double unit_full = kb_total * kblock_cycles(bn) + 4.0 * bn;
-    if (!force_split || force_split == 1) {
+    if ((!force_split || force_split == 1) && force_pair != 2) {
       // whole tiles
       const int64_t w = ceil_div(tiles, sms);
       consider(w * unit_full, (double)tiles, (double)w, 0.0, bn, am, bm, 1, kb_total, tiles, 0);
@@ -254,8 +266,30 @@ void choose_tc_tile(const Op &o, int sms, int force_bn, int force_split, bool ha
                  0.0, bn, am, bm, 1, kb_total, dp, 1);
       }
     }
+    // CTA pairs: 256-row tiles on sms/2 pairs, whole tiles (+ half-width tail)
+    // a CTA of the pair loads bn/2 columns of B: an MN-major box is 128 bytes wide
+    const bool pair_fits = !bm || (bn / 2) * esz >= 128;
+    // Pairs pay a cross-CTA handshake per tile (both epilogues must drain an
+    // accumulator before the next MMA): only worth it with enough K per tile.
+    const bool want_pair = force_pair == 2 || (force_pair == 0 && g_pair_enabled && o.M > 128 && kb_total >= 8);
+    if ((bn == 128 || bn == 256) && pair_fits && want_pair && (!force_split || force_split == 1)) {
+      const int pairs = sms / 2;
+      const int64_t ptiles = o.batch * ceil_div(o.M, 256) * ceil_div(o.N, bn);
+      const double punit = kb_total * kblock_cycles_pair(bn) + 4.0 * bn;
+      const int64_t w = ceil_div(ptiles, pairs);
+      consider(w * punit, (double)ptiles * 2, (double)w, 0.0, bn, am, bm, 1, kb_total, ptiles, 0, 2);
+      const bool half_ok = bn == 256 && bm && (bn / 4) * esz >= 128;
+      if (half_ok && ptiles > pairs && ptiles % pairs) {
+        const int64_t dp = (ptiles / pairs) * pairs;
+        const int64_t tail_units = 2 * (ptiles - dp);
+        const double phalf = kb_total * kblock_cycles_pair(bn / 2) + 2.0 * bn;
+        const double waves = (double)(dp / pairs + ceil_div(tail_units, pairs));
+        consider((dp / pairs) * punit + ceil_div(tail_units, pairs) * phalf, (double)(dp + tail_units) * 2, waves,
+                 0.0, bn, am, bm, 1, kb_total, dp, 1, 2);
+      }
+    }
     // every tile split along K (long-K, few tiles: skinny and thin shapes)
-    int max_split = have_ws ? (int)std::min<int64_t>(kb_total, 64) : 1;
+    int max_split = have_ws && force_pair != 2 ? (int)std::min<int64_t>(kb_total, 64) : 1;
     if (tiles * tc::NUM_EPI_WARPS > kMaxTickets) max_split = 1;  // ticket counters
     for (int s = 2; s <= max_split; ++s) {
       if (force_split && s != force_split) continue;
@@ -277,7 +311,7 @@ void choose_tc_tile(const Op &o, int sms, int force_bn, int force_split, bool ha
 // Fill pl for the TC path on operands o (possibly swapped); false if TMA can't.
 bool plan_tc(const Op &o, int sms, const mb_gemm_desc *d, bool have_ws, Plan &pl) {
   pl.bn = 0;
-  choose_tc_tile(o, sms, d->tile_n, d->split_k, have_ws, pl);
+  choose_tc_tile(o, sms, d->tile_n, d->split_k, d->cta_pair, have_ws, pl);
   if (!pl.bn) return false;
   pl.kind = PK_TC;
   const int64_t tiles = o.batch * pl.tiles_m * pl.tiles_n;
@@ -384,6 +418,7 @@ int validate(const mb_gemm_desc *d) {
   if (d->tile_n && (d->tile_n % 16 || d->tile_n < 16 || d->tile_n > 256 || (d->tile_n & (d->tile_n - 1))))
     return fail(MB_ERR_INVALID, "tile_n must be one of 16, 32, 64, 128, 256");
   if (d->split_k < 0 || d->split_k > 65535) return fail(MB_ERR_INVALID, "split_k out of range");
+  if (d->cta_pair < 0 || d->cta_pair > 2) return fail(MB_ERR_INVALID, "cta_pair must be 0, 1 or 2");
   const bool empty = d->M == 0 || d->N == 0 || d->batch == 0;
   if (!empty) {
     if (!d->C) return fail(MB_ERR_INVALID, "null C");
@@ -497,9 +532,9 @@ int encode_map(CUtensorMap *m, int dt, const void *base, int64_t inner, int64_t 
   return MB_OK;
 }
 
-template <class T, int BN>
+template <class T, int BN, int PAIR>
 int launch_tc_bn(const Op &o, const Plan &pl, const EpiScalars &e, void *ws, int sms, cudaStream_t st) {
-  using C_ = tc::Cfg<BN, sizeof(T)>;
+  using C_ = tc::Cfg<BN, sizeof(T), PAIR>;
   constexpr int ESZ = sizeof(T);
   constexpr int BK = C_::BK;
   tc::TcParams p;
@@ -509,7 +544,7 @@ int launch_tc_bn(const Op &o, const Plan &pl, const EpiScalars &e, void *ws, int
   if (!pl.a_mn) rc = encode_map(&p.tmA, o.dt, o.A, o.K, o.M, bA, o.a_rs, o.sA, BK, tc::BM);
   else rc = encode_map(&p.tmA, o.dt, o.A, o.M, o.K, bA, o.a_cs, o.sA, 128 / ESZ, BK);
   if (rc) return rc;
-  if (!pl.b_mn) rc = encode_map(&p.tmB, o.dt, o.B, o.K, o.N, bB, o.b_cs, o.sB, BK, BN);
+  if (!pl.b_mn) rc = encode_map(&p.tmB, o.dt, o.B, o.K, o.N, bB, o.b_cs, o.sB, BK, BN / PAIR);
   else rc = encode_map(&p.tmB, o.dt, o.B, o.N, o.K, bB, o.b_rs, o.sB, 128 / ESZ, BK);
   if (rc) return rc;
   p.M = (int)o.M; p.N = (int)o.N; p.K = (int)o.K; p.batch = (int)o.batch;
@@ -540,7 +575,7 @@ int launch_tc_bn(const Op &o, const Plan &pl, const EpiScalars &e, void *ws, int
     p.ws = reinterpret_cast<char *>(ws) + kTicketBytes;
   }
   p.timeout_ns = wait_timeout_ns();
-  auto kern = tc::tc_gemm_kernel<T, BN>;
+  auto kern = tc::tc_gemm_kernel<T, BN, PAIR>;
   static int attr_done[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -550,19 +585,45 @@ int launch_tc_bn(const Op &o, const Plan &pl, const EpiScalars &e, void *ws, int
     if (rc) return rc;
     attr_done[dev] = 1;
   }
-  const int grid = (int)std::min<int64_t>(units, sms);
-  kern<<<grid, tc::NUM_THREADS, C_::SMEM_BYTES, st>>>(p);
+  if constexpr (PAIR == 1) {
+    const int grid = (int)std::min<int64_t>(units, sms);
+    kern<<<grid, tc::NUM_THREADS, C_::SMEM_BYTES, st>>>(p);
+  } else {
+    // one cluster (CTA pair) per unit slot; the pair shares each 256-row tile
+    const int pairs = (int)std::min<int64_t>(units, sms / 2);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * pairs, 1, 1);
+    cfg.blockDim = dim3(tc::NUM_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = C_::SMEM_BYTES;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    rc = cuda_check(cudaLaunchKernelEx(&cfg, kern, p), "tc_gemm (CTA pair) launch");
+    if (rc) return rc;
+  }
   return cuda_check(cudaGetLastError(), "tc_gemm launch");
 }
 
 template <class T>
 int launch_tc(const Op &o, const Plan &pl, const EpiScalars &e, void *ws, int sms, cudaStream_t st) {
+  if (pl.pair == 2) {
+    switch (pl.bn) {
+      case 128: return launch_tc_bn<T, 128, 2>(o, pl, e, ws, sms, st);
+      case 256: return launch_tc_bn<T, 256, 2>(o, pl, e, ws, sms, st);
+    }
+    return fail(MB_ERR_INVALID, "bad tile_n %d for a CTA pair", pl.bn);
+  }
   switch (pl.bn) {
-    case 16: return launch_tc_bn<T, 16>(o, pl, e, ws, sms, st);
-    case 32: return launch_tc_bn<T, 32>(o, pl, e, ws, sms, st);
-    case 64: return launch_tc_bn<T, 64>(o, pl, e, ws, sms, st);
-    case 128: return launch_tc_bn<T, 128>(o, pl, e, ws, sms, st);
-    case 256: return launch_tc_bn<T, 256>(o, pl, e, ws, sms, st);
+    case 16: return launch_tc_bn<T, 16, 1>(o, pl, e, ws, sms, st);
+    case 32: return launch_tc_bn<T, 32, 1>(o, pl, e, ws, sms, st);
+    case 64: return launch_tc_bn<T, 64, 1>(o, pl, e, ws, sms, st);
+    case 128: return launch_tc_bn<T, 128, 1>(o, pl, e, ws, sms, st);
+    case 256: return launch_tc_bn<T, 256, 1>(o, pl, e, ws, sms, st);
   }
   return fail(MB_ERR_INVALID, "bad tile_n %d", pl.bn);
 }
@@ -638,8 +699,9 @@ int mb_plan_query(const mb_gemm_desc *d, char *buf, int buflen) {
     case PK_GEMV_COLS: snprintf(tmp, sizeof(tmp), "gemv_cols vec=%d ksplit=%d", pl.vec, pl.g.ksplit); break;
     case PK_GEMV_ROWS: snprintf(tmp, sizeof(tmp), "gemv_rows vec=%d", pl.vec); break;
     case PK_TC:
-      snprintf(tmp, sizeof(tmp), "tc bn=%d split=%d dp=%lld half=%d swap=%d a_mn=%d b_mn=%d tiles=%lldx%lld ws=%lld",
-               pl.bn, pl.splits, (long long)pl.dp_tiles, pl.tail_half, pl.swap, pl.a_mn, pl.b_mn,
+      snprintf(tmp, sizeof(tmp),
+               "tc bn=%d split=%d dp=%lld half=%d pair=%d swap=%d a_mn=%d b_mn=%d tiles=%lldx%lld ws=%lld", pl.bn,
+               pl.splits, (long long)pl.dp_tiles, pl.tail_half, pl.pair, pl.swap, pl.a_mn, pl.b_mn,
                (long long)pl.tiles_m, (long long)pl.tiles_n, (long long)pl.ws_bytes);
       break;
     default: snprintf(tmp, sizeof(tmp), "simt"); break;

@@ -81,13 +81,13 @@ struct TcParams {
   unsigned long long timeout_ns;
 };
 
-template <int BN, int ESZ>
+template <int BN, int ESZ, int PAIR = 1>
 struct Cfg {
   static constexpr int BK = 128 / ESZ;          // one 128-byte swizzle row of K
   static constexpr int UMMA_K = 32 / ESZ;       // K per tcgen05.mma
   static constexpr int KSTEPS = BK / UMMA_K;    // 4
   static constexpr int A_BYTES = BM * 128;
-  static constexpr int B_BYTES = BN * 128;
+  static constexpr int B_BYTES = (BN / PAIR) * 128;  // this CTA's share of B's columns
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int HALF = BN / 2;           // columns per epilogue warp (whole-tile unit)
   static constexpr int QUART = BN / 4;          // columns per epilogue warp (half-width unit)
@@ -104,7 +104,7 @@ struct Cfg {
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N for M=128");
   static_assert(STAGES >= 2, "need a pipeline");
   static_assert(SMEM_BYTES <= SMEM_LIMIT, "shared memory");
-  static_assert(2 * STAGES + 5 <= BAR_BYTES / 8 - 2, "barrier area");
+  static_assert(3 * STAGES + 5 <= BAR_BYTES / 8 - 2, "barrier area");
 };
 
 // ---------------------------------------------------------------------------
@@ -160,6 +160,17 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map
       "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+// CTA-pair form: the copy lands in this CTA's shared memory and its bytes are
+// counted on `bar_cluster`, the pair leader's barrier (cluster address).  No
+// multicast: each CTA fetches its own tiles.
+__device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const CUtensorMap *map, uint32_t bar_cluster, int c0,
+                                                 int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
 }
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap *map) {
@@ -219,6 +230,122 @@ __device__ __forceinline__ void tmem_ld_x16(uint32_t taddr, uint32_t (&r)[32]) {
         "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
 }
+// ---- CTA-pair (cluster of 2) helpers
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Address of the same shared-memory offset in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait on a barrier that receives arrivals from the peer CTA.
+__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, volatile int *abort_flag,
+                                                  unsigned long long timeout_ns) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if ((it & 63) == 0) {
+      if (*abort_flag) return false;
+      if (globaltimer_ns() - t0 > timeout_ns) {
+        *abort_flag = 1;
+        atomicExch(&g_mb_status, 4 /*MB_ERR_DEVICE_TIMEOUT*/);
+        return false;
+      }
+    }
+  }
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+template <int PAIR>
+__device__ __forceinline__ void tmem_alloc_g(uint32_t dst_smem, uint32_t ncols) {
+  if constexpr (PAIR == 2)
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
+                 : "memory");
+  else
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
+                 : "memory");
+}
+template <int PAIR>
+__device__ __forceinline__ void tmem_relinquish_g() {
+  if constexpr (PAIR == 2) asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  else asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+template <int PAIR>
+__device__ __forceinline__ void tmem_dealloc_g(uint32_t taddr, uint32_t ncols) {
+  if constexpr (PAIR == 2)
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+  else
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// MMA issue: cta_group::2 runs one M=256 instruction over the CTA pair (each CTA
+// supplies 128 rows of A and half of B's columns, and holds its 128 rows of D).
+template <int ESZ, int PAIR>
+__device__ __forceinline__ void umma_g(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accum) {
+  if constexpr (PAIR == 1) {
+    umma<ESZ>(d_tmem, adesc, bdesc, idesc, accum);
+  } else if constexpr (ESZ == 2) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accum)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accum)
+        : "memory");
+  }
+}
+// Commit: arrive once on the barrier at this offset in every CTA of the pair
+// (tcgen05.commit with multicast; the loads themselves never multicast).
+template <int PAIR>
+__device__ __forceinline__ void umma_commit_g(uint32_t bar) {
+  if constexpr (PAIR == 1) {
+    umma_commit(bar);
+  } else {
+    asm volatile(
+        "{\n\t.reg .b16 m;\n\tmov.b16 m, 3;\n\t"
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], m;\n\t}" ::"r"(
+            bar)
+        : "memory");
+  }
+}
+// Commit to this CTA's barrier only (drain on abort).
+template <int PAIR>
+__device__ __forceinline__ void umma_commit_self(uint32_t bar) {
+  if constexpr (PAIR == 1) {
+    umma_commit(bar);
+  } else {
+    asm volatile(
+        "{\n\t.reg .b16 m;\n\tmov.b16 m, 1;\n\t"
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], m;\n\t}" ::"r"(
+            bar)
+        : "memory");
+  }
+}
+
 __device__ __forceinline__ void tmem_ld_x8(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
@@ -268,10 +395,10 @@ template <> struct UFmt<__nv_bfloat16> { static constexpr uint32_t d = 1, ab = 1
 template <> struct UFmt<uint8_t> { static constexpr uint32_t d = 2, ab = 0; };
 template <> struct UFmt<int8_t> { static constexpr uint32_t d = 2, ab = 1; };
 
-template <class T, int BN>
+template <class T, int BN, int UM = BM>
 __device__ __forceinline__ uint32_t make_idesc(int a_mn, int b_mn) {
   return (UFmt<T>::d << 4) | (UFmt<T>::ab << 7) | (UFmt<T>::ab << 10) | ((uint32_t)a_mn << 15) |
-         ((uint32_t)b_mn << 16) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+         ((uint32_t)b_mn << 16) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(UM >> 4) << 24);
 }
 
 struct Unit {
@@ -389,10 +516,11 @@ __device__ __forceinline__ void pack32(const TcParams &p, int b, int m, int n0, 
 }
 
 // ---------------------------------------------------------------------------
-template <class T, int BN>
+template <class T, int BN, int PAIR = 1>
 __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_constant__ TcParams p) {
   constexpr int ESZ = sizeof(T);
-  using C_ = Cfg<BN, ESZ>;
+  using C_ = Cfg<BN, ESZ, PAIR>;
+  constexpr int TM_ROWS = BM * PAIR;  // output rows per tile (256 for a CTA pair)
   constexpr int BK = C_::BK, STAGES = C_::STAGES;
   constexpr uint32_t A_BYTES = C_::A_BYTES, STAGE_BYTES = C_::STAGE_BYTES;
   constexpr int RCH = C_::RCH, CC = C_::CC;
@@ -415,6 +543,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
   auto tfull_bar = [&](int a) { return bar_u32 + 8u * (2 * STAGES + a); };
   auto tempty_bar = [&](int a) { return bar_u32 + 8u * (2 * STAGES + 2 + a); };
   const uint32_t drain_bar = bar_u32 + 8u * (2 * STAGES + 4);
+  const uint32_t rank = PAIR == 2 ? cluster_rank() : 0u;
+  // the pair leader's full barrier of stage s, as a cluster address
+  auto leader_full = [&](int s) { return mapa_shared(full_bar(s), 0); };
+  const int pair_id = blockIdx.x / PAIR, npairs = gridDim.x / PAIR;
+  // Waits on barriers that the peer CTA (or the pair's MMA) arrives on use
+  // cluster-scope acquire.
+  auto wait_x = [&](uint32_t bar, uint32_t parity) {
+    if constexpr (PAIR == 2) return mbar_wait_cluster(bar, parity, abort_flag, p.timeout_ns);
+    else return mbar_wait(bar, parity, abort_flag, p.timeout_ns);
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -423,7 +561,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(tfull_bar(a), 1);
-      mbar_init(tempty_bar(a), NUM_EPI_WARPS);
+      mbar_init(tempty_bar(a), NUM_EPI_WARPS * PAIR);
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -433,11 +571,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
     if (p.c_tma) prefetch_tmap(&p.tmC);
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_slot), C_::TMEM_COLS);
-    tmem_relinquish();
+    tmem_alloc_g<PAIR>(smem_u32(tmem_slot), C_::TMEM_COLS);
+    tmem_relinquish_g<PAIR>();
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR == 2) cluster_sync_all();  // peer barriers initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -448,32 +587,38 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
       uint32_t phase = 0;
       int issued_stage = -1;
       uint32_t issued_phase = 0;
-      for (int u = blockIdx.x; u < p.num_units; u += gridDim.x) {
+      for (int u = pair_id; u < p.num_units; u += npairs) {
         const Unit w = decode_unit(p, u);
         const int ba = p.a_bcast ? 0 : w.b, bb = p.b_bcast ? 0 : w.b;
-        // A half-width unit loads only its BN/2 columns of an MN-major B; a
-        // K-major B tile is one box, loaded whole.
+        // This CTA's columns of B: its share (1/PAIR) of the unit's columns.  A
+        // half-width unit loads only its BN/2 columns of an MN-major B; a
+        // K-major B share is one box, loaded whole.
         const bool half_b = w.half >= 0 && p.b_mn;
-        const uint32_t b_bytes = half_b ? (uint32_t)(BN / 2) * 128u : (uint32_t)BN * 128u;
-        const int b_boxes = (half_b ? BN / 2 : BN) * ESZ / 128;
-        const int b_col0 = w.tn * BN + (half_b ? w.half * (BN / 2) : 0);
+        const int ccols = (half_b ? BN / 2 : BN) / PAIR;
+        const uint32_t b_bytes = (uint32_t)ccols * 128u;
+        const int b_boxes = ccols * ESZ / 128;
+        const int b_col0 = w.tn * BN + (half_b ? w.half * (BN / 2) : 0) + (int)rank * ccols;
+        const int a_row0 = w.tm * TM_ROWS + (int)rank * BM;
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
-          if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag, p.timeout_ns)) goto producer_done;
-          mbar_arrive_expect_tx(full_bar(stage), A_BYTES + b_bytes);
+          if (!wait_x(empty_bar(stage), phase ^ 1u)) goto producer_done;
+          // Both CTAs' bytes of this stage are counted on the leader's full barrier.
+          if (rank == 0) mbar_arrive_expect_tx(full_bar(stage), (A_BYTES + b_bytes) * PAIR);
           const uint32_t sa = ring_u32 + stage * STAGE_BYTES;
           const uint32_t sb = sa + A_BYTES;
+          auto load = [&](uint32_t dst, const CUtensorMap *map, int c0, int c1, int c2) {
+            if constexpr (PAIR == 2) tma_load_3d_pair(dst, map, leader_full(stage), c0, c1, c2);
+            else tma_load_3d(dst, map, full_bar(stage), c0, c1, c2);
+          };
           if (!p.a_mn) {
-            tma_load_3d(sa, &p.tmA, full_bar(stage), kb * BK, w.tm * BM, ba);
+            load(sa, &p.tmA, kb * BK, a_row0, ba);
           } else {
 #pragma unroll
-            for (int j = 0; j < BM * ESZ / 128; ++j)
-              tma_load_3d(sa + j * (BK * 128), &p.tmA, full_bar(stage), w.tm * BM + j * (128 / ESZ), kb * BK, ba);
+            for (int j = 0; j < BM * ESZ / 128; ++j) load(sa + j * (BK * 128), &p.tmA, a_row0 + j * (128 / ESZ), kb * BK, ba);
           }
           if (!p.b_mn) {
-            tma_load_3d(sb, &p.tmB, full_bar(stage), kb * BK, w.tn * BN, bb);
+            load(sb, &p.tmB, kb * BK, w.tn * BN + (int)rank * (BN / PAIR), bb);
           } else {
-            for (int j = 0; j < b_boxes; ++j)
-              tma_load_3d(sb + j * (BK * 128), &p.tmB, full_bar(stage), b_col0 + j * (128 / ESZ), kb * BK, bb);
+            for (int j = 0; j < b_boxes; ++j) load(sb + j * (BK * 128), &p.tmB, b_col0 + j * (128 / ESZ), kb * BK, bb);
           }
           issued_stage = stage;
           issued_phase = phase;
@@ -482,16 +627,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
       }
     producer_done:
       // Drain: the last issued stage's copies must land before the CTA can exit.
+      // The leader sees them on its full barrier; the peer's are counted there
+      // too, so the peer waits until the pair's MMA has consumed that stage.
       if (issued_stage >= 0) {
         volatile int no_abort = 0;
-        mbar_wait(full_bar(issued_stage), issued_phase, &no_abort, p.timeout_ns);
+        if (rank == 0) mbar_wait(full_bar(issued_stage), issued_phase, &no_abort, p.timeout_ns);
+        else mbar_wait_cluster(empty_bar(issued_stage), issued_phase, &no_abort, p.timeout_ns);
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      const uint32_t idesc_full = make_idesc<T, BN>(p.a_mn, p.b_mn);
-      const uint32_t idesc_half = make_idesc<T, (BN >= 32 ? BN / 2 : BN)>(p.a_mn, p.b_mn);
+    if (rank == 0 && lane == 0) {
+      const uint32_t idesc_full = make_idesc<T, BN, TM_ROWS>(p.a_mn, p.b_mn);
+      const uint32_t idesc_half = make_idesc<T, (BN >= 32 ? BN / 2 : BN), TM_ROWS>(p.a_mn, p.b_mn);
       // Canonical SW128 layouts: K-major SBO = 8 rows * 128 B; MN-major
       // LBO = next 128-byte MN column block (one TMA box), SBO = 8 K rows.
       const uint32_t a_lbo = p.a_mn ? BK * 128 : 16, b_lbo = p.b_mn ? BK * 128 : 16;
@@ -501,17 +649,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
       int abuf = 0;
       uint32_t aphase = 0;
       bool issued_any = false;
-      for (int u = blockIdx.x; u < p.num_units; u += gridDim.x) {
+      for (int u = pair_id; u < p.num_units; u += npairs) {
         const Unit w = decode_unit(p, u);
         const uint32_t idesc = w.half >= 0 ? idesc_half : idesc_full;
         // K-major B holds the whole tile: a half-width unit starts BN/2 rows in.
         const uint32_t b_off = (w.half > 0 && !p.b_mn) ? (uint32_t)(BN / 2) * 128u : 0u;
-        if (!mbar_wait(tempty_bar(abuf), aphase ^ 1u, abort_flag, p.timeout_ns)) break;
+        if (!wait_x(tempty_bar(abuf), aphase ^ 1u)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(abuf * C_::ACC_COLS);
         bool aborted = false;
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
-          if (!mbar_wait(full_bar(stage), phase, abort_flag, p.timeout_ns)) { aborted = true; break; }
+          if (!wait_x(full_bar(stage), phase)) { aborted = true; break; }
           tc_fence_after();
           const uint32_t sa = ring_u32 + stage * STAGE_BYTES;
           const uint32_t sb = sa + A_BYTES + b_off;
@@ -519,19 +667,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
           for (int ks = 0; ks < C_::KSTEPS; ++ks) {
             const uint64_t ad = sdesc(sa + ks * a_kstep, a_lbo, 1024);
             const uint64_t bd = sdesc(sb + ks * b_kstep, b_lbo, 1024);
-            umma<ESZ>(d_tmem, ad, bd, idesc, (kb > w.kb0 || ks > 0) ? 1u : 0u);
+            umma_g<ESZ, PAIR>(d_tmem, ad, bd, idesc, (kb > w.kb0 || ks > 0) ? 1u : 0u);
           }
           issued_any = true;
-          umma_commit(empty_bar(stage));  // frees this smem stage when the MMAs finish
+          umma_commit_g<PAIR>(empty_bar(stage));  // frees this smem stage (in both CTAs) when the MMAs finish
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
         if (aborted) break;
-        umma_commit(tfull_bar(abuf));     // accumulator ready for the epilogue
+        umma_commit_g<PAIR>(tfull_bar(abuf));  // accumulators ready for the epilogue(s)
         if (++abuf == 2) { abuf = 0; aphase ^= 1u; }
       }
       if (*abort_flag && issued_any) {
         // Drain every MMA this thread issued before TMEM is freed.
-        umma_commit(drain_bar);
+        umma_commit_self<PAIR>(drain_bar);
         volatile int no_abort = 0;
         mbar_wait(drain_bar, 0, &no_abort, p.timeout_ns);
       }
@@ -542,14 +690,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
     const int q = warp & 3;               // TMEM lane quarter this warp may access
     const int row = q * 32 + lane;
     const uint32_t stg0 = smem_u32(staging) + (uint32_t)(ew * STAGING_PER_WARP);
+    // Hand a drained accumulator back to the (pair leader's) MMA issuer.
+    auto release_tmem = [&](int a) {
+      if constexpr (PAIR == 2) mbar_arrive_cluster(mapa_shared(tempty_bar(a), 0));
+      else mbar_arrive(tempty_bar(a));
+    };
     int sbuf = 0;                         // staging buffer to fill next
     int abuf = 0;
     uint32_t aphase = 0;
-    for (int u = blockIdx.x; u < p.num_units; u += gridDim.x) {
+    for (int u = pair_id; u < p.num_units; u += npairs) {
       const Unit w = decode_unit(p, u);
-      if (!mbar_wait(tfull_bar(abuf), aphase, abort_flag, p.timeout_ns)) break;
+      if (!wait_x(tfull_bar(abuf), aphase)) break;
       tc_fence_after();
-      const int m = w.tm * BM + row;
+      const int m0 = w.tm * TM_ROWS + (int)rank * BM;  // this CTA's first output row of the tile
+      const int m = m0 + row;
       // Columns of this unit and of this warp's share (half of the unit).
       const int ucols = w.half >= 0 ? BN / 2 : BN;
       const int wcols = ucols / 2;
@@ -580,7 +734,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
               } else {                           // last TMEM read of this unit by this warp
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(tempty_bar(abuf));
+                if (lane == 0) release_tmem(abuf);
               }
               const int sub = sc % SUBS;
               const uint32_t stg = stg0 + (uint32_t)(sbuf * STAGING_BUF);
@@ -603,7 +757,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) {
-                  tma_store_3d(&p.tmC, stg, n0 - (SUBS - 1) * 32, w.tm * BM + q * 32, w.b);
+                  tma_store_3d(&p.tmC, stg, n0 - (SUBS - 1) * 32, m0 + q * 32, w.b);
                   bulk_commit();
                 }
                 sbuf ^= 1;
@@ -623,7 +777,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(tempty_bar(abuf));
+        if (lane == 0) release_tmem(abuf);
       } else {
         // Split-K: publish raw accumulators (tile-local row-major, 4 B each).
         uint32_t *part = reinterpret_cast<uint32_t *>(p.ws) +
@@ -639,7 +793,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(tempty_bar(abuf));
+        if (lane == 0) release_tmem(abuf);
         // Each warp owns 32 rows x wcols columns of the tile and reduces them on
         // its own: per-(tail tile, warp) tickets, so no cross-warp barrier exists
         // that an aborting warp could leave the others waiting at.
@@ -687,9 +841,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
 
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR == 2) cluster_sync_all();  // the pair's MMAs and remote arrivals are done
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, C_::TMEM_COLS);
+    tmem_dealloc_g<PAIR>(tmem_base, C_::TMEM_COLS);
   }
 }
 

@@ -20,19 +20,22 @@ from tests.helpers import NAME, rand, to_np
 
 pytestmark = pytest.mark.gpu
 
-SHAPES = [(128, 8192, 4096), (64, 2048, 8192), (256, 512, 16384), (4, 4096, 4096), (16, 1024, 2048)]
-VARIANTS = [(0, 0, 0), (64, 1, -1), (64, 4, -1), (128, 2, -1), (256, 4, -1), (256, 8, -1), (128, 3, -1),
-            (0, 0, 1), (32, 4, 1), (16, 2, 1), (64, 1, 1)]
+SHAPES = [(128, 8192, 4096), (64, 2048, 8192), (256, 512, 16384), (4, 4096, 4096), (16, 1024, 2048),
+          (520, 1000, 1024)]
+# (tile_n, split_k, swap_ab, cta_pair)
+VARIANTS = [(0, 0, 0, 0), (64, 1, -1, 1), (64, 4, -1, 0), (128, 2, -1, 0), (256, 4, -1, 0), (256, 8, -1, 0),
+            (128, 3, -1, 0), (0, 0, 1, 0), (32, 4, 1, 0), (16, 2, 1, 0), (64, 1, 1, 0),
+            (256, 1, -1, 2), (128, 1, -1, 2), (256, 0, -1, 2)]
 
 
-def _run(a, b, tile_n, split, swap, epilogue=None):
+def _run(a, b, tile_n, split, swap, pair=0, epilogue=None):
     M, K = a.shape
     N = b.shape[1]
     c = torch.empty(M, N, dtype=a.dtype, device=a.device)
     try:
         dispatch._launch(a, b, c, M, N, K, 1, (a.stride(0), a.stride(1), 0), (b.stride(0), b.stride(1), 0),
                          (c.stride(0), c.stride(1), 0), epilogue=epilogue, backend=_lib.MB_BACKEND_TC,
-                         tile_n=tile_n, split_k=split, swap_ab=swap, autotune=False)
+                         tile_n=tile_n, split_k=split, swap_ab=swap, cta_pair=pair, autotune=False)
     except NotImplementedError:
         return None  # this layout cannot take the forced variant (e.g. MN-major B with a narrow tile)
     return c
@@ -55,7 +58,7 @@ def test_interleaved_plans_share_workspace(dtype):
         ran += 1
         ok, err = orc.check(to_np(c), ref, NAME[dtype])
         assert ok, f"{dtype} {tuple(a.shape)}x{b.shape[1]} variant={v} plan err={err}"
-    assert ran >= len(cases) * 6
+    assert ran >= len(cases) * 8
 
 
 def test_split_k_epilogue_int8_wraps():
@@ -69,6 +72,11 @@ def test_split_k_epilogue_int8_wraps():
         ref = orc.fused(to_np(bias), to_np(a), to_np(b), 3, -7, "int8")
         ok, _ = orc.check(to_np(c), ref, "int8")
         assert ok, f"split={split}"
+    for pair in (1, 2):
+        c = _run(a, b, 256, 1, -1, pair=pair, epilogue=(bias, (0, 1, 0), 3, -7, True, True))
+        ref = orc.fused(to_np(bias), to_np(a), to_np(b), 3, -7, "int8")
+        ok, _ = orc.check(to_np(c), ref, "int8")
+        assert ok, f"pair={pair}"
 
 
 def test_no_device_timeouts():
