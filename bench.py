@@ -248,31 +248,52 @@ def run_ours(args, w, rank, world, device):
         gathered = {"value": flops * world / (gms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": gms,
                     "layout": "[N_ranks, M, N/N_ranks] via NCCL all_gather_into_tensor"}
 
-    # e2e: host buffers -> public API -> host result, every step
+    # e2e: host buffers -> public API -> host result, every step.  Three streams
+    # (copy-in, compute, copy-out) and two device buffer sets, so step i's
+    # host-to-device copy overlaps step i-1's product and step i-2's read-back;
+    # every step still copies its own inputs and reads its own result.
     e2e_steps = max(1, min(args.steps, 100))
-    c_pin = torch.empty(M, N, dtype=dt).pin_memory()
-    a_d = torch.empty(M, K, dtype=dt, device=device)
-    b_d = torch.empty(K, N, dtype=dt, device=device)
-    for _ in range(2):
-        a_d.copy_(a_pin, non_blocking=True)
-        b_d.copy_(b_pin, non_blocking=True)
-        c = mb.matmul(a_d, b_d)
-        c_pin.copy_(c, non_blocking=True)
+    elt = a_h.element_size()
+    s_in, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    a_d = [torch.empty(M, K, dtype=dt, device=device) for _ in range(2)]
+    b_d = [torch.empty(K, N, dtype=dt, device=device) for _ in range(2)]
+    c_d = [torch.empty(M, N, dtype=dt, device=device) for _ in range(2)]
+    c_pin = [torch.empty(M, N, dtype=dt).pin_memory() for _ in range(2)]
+    in_done = [torch.cuda.Event() for _ in range(2)]
+    mm_done = [torch.cuda.Event() for _ in range(2)]
+    out_done = [torch.cuda.Event() for _ in range(2)]
+
+    def e2e_step(i):
+        j = i % 2
+        with torch.cuda.stream(s_in):
+            s_in.wait_event(mm_done[j])          # buffer set j free (product i-2 consumed it)
+            a_d[j].copy_(a_pin, non_blocking=True)
+            b_d[j].copy_(b_pin, non_blocking=True)
+            in_done[j].record(s_in)
+        stream.wait_event(in_done[j])
+        stream.wait_event(out_done[j])           # c_d[j] read back (step i-2)
+        mb.matmul(a_d[j], b_d[j], out=c_d[j])
+        mm_done[j].record(stream)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(mm_done[j])
+            c_pin[j].copy_(c_d[j], non_blocking=True)
+            out_done[j].record(s_out)
+
+    for i in range(4):
+        e2e_step(i)
+    torch.cuda.synchronize(device)
     _barrier(world, device)
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t0.record(stream)
-    for _ in range(e2e_steps):
-        a_d.copy_(a_pin, non_blocking=True)
-        b_d.copy_(b_pin, non_blocking=True)
-        c = mb.matmul(a_d, b_d)
-        c_pin.copy_(c, non_blocking=True)
-    t1.record(stream)
+    t0.record(s_in)
+    for i in range(e2e_steps):
+        e2e_step(i)
+    t1.record(s_out)
     t1.synchronize()
     _barrier(world, device)
     ems = _max_over_ranks(t0.elapsed_time(t1) / e2e_steps, world, device)
-    elt = a_h.element_size()
     e2e = {"value": flops * world / (ems * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ems,
-           "h2d_bytes_per_step": (M * K + K * N) * elt, "d2h_bytes_per_step": M * N * elt, "steps": e2e_steps}
+           "h2d_bytes_per_step": (M * K + K * N) * elt, "d2h_bytes_per_step": M * N * elt, "steps": e2e_steps,
+           "pipelining": "copy-in / compute / copy-out streams, 2 device buffer sets"}
 
     peak, hbm, src = _peaks()
     achieved = flops / (ms * 1e-3) / 1e12

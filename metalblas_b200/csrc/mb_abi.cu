@@ -33,6 +33,7 @@
 #include "simt_gemm.cuh"
 #include "gemv.cuh"
 #include "tc_gemm.cuh"
+#include "c32.cuh"
 
 using namespace mb;
 
@@ -123,7 +124,7 @@ void normalize(int64_t rows, int64_t cols, int64_t &rs, int64_t &cs) {
 constexpr int64_t kTicketBytes = 256 * 1024;
 constexpr int64_t kMaxTickets = kTicketBytes / 4;
 
-enum PlanKind { PK_EMPTY = 0, PK_GEMV_COLS, PK_GEMV_ROWS, PK_TC, PK_SIMT };
+enum PlanKind { PK_EMPTY = 0, PK_GEMV_COLS, PK_GEMV_ROWS, PK_TC, PK_SIMT, PK_TC_C32 };
 
 struct Plan {
   int kind = PK_EMPTY;
@@ -137,6 +138,11 @@ struct Plan {
   int64_t dp_tiles = 0;  // whole tiles; tiles after them are split `splits` ways along K,
   int tail_half = 0;     // or (tail_half) into two half-width units each
   int pair = 1;          // 2: CTA-pair kernel (cta_group::2, 256-row tiles)
+  // complex32 as one real fp16 GEMM C' = A' B' (PK_TC_C32); the TC fields above
+  // describe that real GEMM
+  int c32_pack_a = 0;               // A' is a packed copy (else A's own storage)
+  int64_t c32_lda = 0, c32_ldb = 0; // row pitch of packed A' / of B', in half2 pairs
+  int64_t c32_a_off = 0, c32_b_off = 0, c32_a_batches = 1, c32_b_batches = 1;
   int a_mn = 0, b_mn = 0;
   // shared
   int64_t ws_bytes = 0;
@@ -324,6 +330,56 @@ bool plan_tc(const Op &o, int sms, const mb_gemm_desc *d, bool have_ws, Plan &pl
   return true;
 }
 
+// The real fp16 GEMM that computes a complex32 product (see c32.cuh): A' is A's
+// storage viewed as M x 2K halves (or a packed copy at `a`), B' the expanded
+// 2K x 2N matrix at `b`, C' is C's storage viewed as M x 2N halves.
+Op c32_inner(const Op &o, const Plan &pl, const void *a, const void *b) {
+  Op r = o;
+  r.dt = MB_F16;
+  r.N = 2 * o.N;
+  r.K = 2 * o.K;
+  if (pl.c32_pack_a) {
+    r.A = a; r.a_rs = 2 * pl.c32_lda; r.a_cs = 1; r.sA = o.sA ? o.M * 2 * pl.c32_lda : 0;
+  } else {
+    r.a_rs = 2 * o.a_rs; r.a_cs = 1; r.sA = 2 * o.sA;
+  }
+  r.B = b; r.b_rs = 2 * pl.c32_ldb; r.b_cs = 1; r.sB = o.sB ? 2 * o.K * 2 * pl.c32_ldb : 0;
+  r.c_rs = 2 * o.c_rs; r.c_cs = 1; r.sC = 2 * o.sC;
+  r.conj_a = r.conj_b = 0;
+  return r;  // bias keeps its complex strides: the epilogue reads half2 pairs
+}
+
+bool plan_c32(const Op &o, int sms, const mb_gemm_desc *d, bool have_ws, Plan &pl) {
+  if (o.dt != MB_C32 || o.M < 2 || o.N < 2 || o.K < 1 || !have_ws) return false;
+  if (o.c_cs != 1 || o.c_rs < o.N) return false;  // C' must be a row-major real view
+  if (o.K >= (1ll << 30) || o.N >= (1ll << 30)) return false;
+  Plan t;
+  t.c32_pack_a = !(o.a_cs == 1 && o.a_rs >= o.K && o.a_rs % 4 == 0 && aligned16(o.A) &&
+                   (o.batch <= 1 || o.sA % 4 == 0));
+  t.c32_lda = round_up(o.K, 4);
+  t.c32_ldb = round_up(o.N, 4);
+  t.c32_a_batches = o.sA ? o.batch : 1;
+  t.c32_b_batches = o.sB ? o.batch : 1;
+  // plan the real GEMM on placeholder (aligned) operand addresses; no swap:
+  // the complex epilogue needs both halves of a pair in one thread
+  const void *ph = reinterpret_cast<const void *>(uintptr_t(1) << 20);
+  Op r = c32_inner(o, t, ph, ph);
+  mb_gemm_desc q = *d;
+  q.swap_ab = -1;
+  if (!plan_tc(r, sms, &q, have_ws, t)) return false;
+  // after the ticket region (and any split-K partials): the counters at offset 0
+  // are shared by every plan and must never be overwritten
+  const int64_t base = std::max<int64_t>(t.ws_bytes, kTicketBytes);
+  const int64_t a_bytes = t.c32_pack_a ? t.c32_a_batches * o.M * t.c32_lda * 4 : 0;
+  const int64_t b_bytes = t.c32_b_batches * 2 * o.K * t.c32_ldb * 4;
+  t.c32_a_off = round_up(base, 256);
+  t.c32_b_off = round_up(t.c32_a_off + a_bytes, 256);
+  t.ws_bytes = t.c32_b_off + b_bytes;
+  t.kind = PK_TC_C32;
+  pl = t;
+  return true;
+}
+
 bool plan_gemv(const Op &o, int sms, const mb_gemm_desc *d, bool have_ws, Plan &pl) {
   GemvParams g{};
   int kind = 0;
@@ -385,6 +441,10 @@ int make_plan(const mb_gemm_desc *d, const Op &o, int sms, bool have_ws, Plan &p
     return MB_OK;
   }
   if (be == MB_BACKEND_SIMT || o.K == 0) { pl.kind = PK_SIMT; return MB_OK; }
+  if (be == MB_BACKEND_TC && o.dt == MB_C32) {
+    if (plan_c32(o, sms, d, have_ws, pl)) return MB_OK;
+    return fail(MB_ERR_UNSUPPORTED, "tensor-core complex32 needs a row-major output and a workspace");
+  }
   if (be == MB_BACKEND_TC) {
     if (!is_tc_dtype(o.dt)) return fail(MB_ERR_UNSUPPORTED, "tensor-core backend supports bf16/fp16/int8/uint8 only");
     const bool want_swap = d->swap_ab == 1 || (d->swap_ab == 0 && o.M < 128 && o.N > o.M);
@@ -398,6 +458,7 @@ int make_plan(const mb_gemm_desc *d, const Op &o, int sms, bool have_ws, Plan &p
   }
   // AUTO
   if ((o.M == 1 || o.N == 1) && plan_gemv(o, sms, d, have_ws, pl)) return MB_OK;
+  if (o.dt == MB_C32 && plan_c32(o, sms, d, have_ws, pl)) return MB_OK;
   if (is_tc_dtype(o.dt)) {
     const bool want_swap = d->swap_ab == 1 || (d->swap_ab == 0 && o.M < 128 && o.N > o.M);
     if (want_swap && d->swap_ab != -1) {
@@ -628,6 +689,35 @@ int launch_tc(const Op &o, const Plan &pl, const EpiScalars &e, void *ws, int sm
   return fail(MB_ERR_INVALID, "bad tile_n %d", pl.bn);
 }
 
+// complex32 on the tensor cores: build B' (and A' when A is not row-major),
+// then one real fp16 GEMM with the complex-pair epilogue.
+int launch_c32(const Op &o, const Plan &pl, EpiScalars e, void *ws, int sms, cudaStream_t st) {
+  char *w = reinterpret_cast<char *>(ws);
+  __half2 *bp = reinterpret_cast<__half2 *>(w + pl.c32_b_off);
+  __half2 *ap = reinterpret_cast<__half2 *>(w + pl.c32_a_off);
+  const int grid_cap = sms * 16;
+  C32Prep pb{};
+  pb.src = reinterpret_cast<const __half2 *>(o.B); pb.dst = bp;
+  pb.rows = o.K; pb.cols = o.N; pb.rs = o.b_rs; pb.cs = o.b_cs; pb.bs = o.sB;
+  pb.batch = pl.c32_b_batches; pb.conj_a = o.conj_a; pb.conj_b = o.conj_b;
+  const int64_t nb = pb.batch * pb.rows * pb.cols;
+  c32_build_b_kernel<<<(unsigned)std::min<int64_t>(ceil_div(nb, 256), grid_cap), 256, 0, st>>>(pb, pl.c32_ldb);
+  int rc = cuda_check(cudaGetLastError(), "complex32 B' build");
+  if (rc) return rc;
+  if (pl.c32_pack_a) {
+    C32Prep pa{};
+    pa.src = reinterpret_cast<const __half2 *>(o.A); pa.dst = ap;
+    pa.rows = o.M; pa.cols = o.K; pa.rs = o.a_rs; pa.cs = o.a_cs; pa.bs = o.sA;
+    pa.batch = pl.c32_a_batches;
+    const int64_t na = pa.batch * pa.rows * pa.cols;
+    c32_pack_a_kernel<<<(unsigned)std::min<int64_t>(ceil_div(na, 256), grid_cap), 256, 0, st>>>(pa, pl.c32_lda);
+    rc = cuda_check(cudaGetLastError(), "complex32 A' pack");
+    if (rc) return rc;
+  }
+  e.cplx = e.enabled ? 1 : 0;
+  return launch_tc<__half>(c32_inner(o, pl, ap, bp), pl, e, ws, sms, st);
+}
+
 template <class F>
 int by_dtype(int dt, F &&f) {
   switch (dt) {
@@ -704,6 +794,10 @@ int mb_plan_query(const mb_gemm_desc *d, char *buf, int buflen) {
                pl.splits, (long long)pl.dp_tiles, pl.tail_half, pl.pair, pl.swap, pl.a_mn, pl.b_mn,
                (long long)pl.tiles_m, (long long)pl.tiles_n, (long long)pl.ws_bytes);
       break;
+    case PK_TC_C32:
+      snprintf(tmp, sizeof(tmp), "tc_c32 pack_a=%d bn=%d split=%d pair=%d tiles=%lldx%lld ws=%lld", pl.c32_pack_a,
+               pl.bn, pl.splits, pl.pair, (long long)pl.tiles_m, (long long)pl.tiles_n, (long long)pl.ws_bytes);
+      break;
     default: snprintf(tmp, sizeof(tmp), "simt"); break;
   }
   const int n = (int)strlen(tmp);
@@ -731,6 +825,7 @@ int mb_gemm(const mb_gemm_desc *d, void *stream) {
       case PK_TC:
         if constexpr (IsTc<T>::v) return launch_tc<T>(pl.swap ? swapped(o) : o, pl, e, d->workspace, sms, st);
         else return fail(MB_ERR_UNSUPPORTED, "tensor-core path for non-TC dtype");
+      case PK_TC_C32: return launch_c32(o, pl, e, d->workspace, sms, st);
       default: return launch_simt<T>(o, e, st);
     }
   });
@@ -795,6 +890,13 @@ int mb_gemm_noalloc(const mb_gemm_desc *d, void *stream) {
   int rc = plan_for(&q, pl, o, sms);
   if (rc) return rc;
   if (pl.kind == PK_EMPTY) return MB_OK;
+  if (pl.kind == PK_TC_C32 && pl.ws_bytes > (int64_t)MB_NOALLOC_SCRATCH_BYTES && q.backend == MB_BACKEND_AUTO) {
+    // complex32 on the tensor cores needs its expanded B' in scratch; when it
+    // does not fit, the CUDA-core kernel (no scratch) computes the product
+    q.backend = MB_BACKEND_SIMT;
+    rc = plan_for(&q, pl, o, sms);
+    if (rc) return rc;
+  }
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   void *scratch = nullptr;
   if (pl.ws_bytes > 0) {
@@ -817,6 +919,7 @@ int mb_gemm_noalloc(const mb_gemm_desc *d, void *stream) {
       case PK_TC:
         if constexpr (IsTc<T>::v) return launch_tc<T>(pl.swap ? swapped(o) : o, pl, e, scratch, sms, st);
         else return fail(MB_ERR_UNSUPPORTED, "tensor-core path for non-TC dtype");
+      case PK_TC_C32: return launch_c32(o, pl, e, scratch, sms, st);
       default: return launch_simt<T>(o, e, st);
     }
   });

@@ -103,6 +103,7 @@ struct EpiScalars {
   float alpha_re, alpha_im, beta_re, beta_im;
   int64_t ialpha, ibeta;
   int alpha_nz, beta_nz, enabled;
+  int cplx;  // tensor-core complex32: columns (2j, 2j+1) are one complex value, bias is half2
 };
 
 template <class T> struct EpiOps;

@@ -460,13 +460,48 @@ __device__ __forceinline__ T epi_value(const TcParams &p, int b, int m, int n, u
   return Elem<T>::store(v);
 }
 
+// complex32 epilogue on one interleaved pair: real columns (n, n+1) of C' are
+// (re, im) of complex C(m, n/2); bias is complex32 with complex strides.
+__device__ __forceinline__ void epi_cplx_pair(const TcParams &p, int b, int m, int n, uint32_t re_bits,
+                                              uint32_t im_bits, __half &o_re, __half &o_im) {
+  const float re = __uint_as_float(re_bits), im = __uint_as_float(im_bits);
+  float vr = 0.f, vi = 0.f;
+  if (p.epi.alpha_nz) {
+    vr = p.epi.alpha_re * re - p.epi.alpha_im * im;
+    vi = p.epi.alpha_re * im + p.epi.alpha_im * re;
+  }
+  if (p.epi.beta_nz && m < p.M && n < p.N) {
+    const __half2 *bias = (const __half2 *)p.bias + (int64_t)b * p.bias_bs + (int64_t)m * p.bias_rs +
+                          (int64_t)(n >> 1) * p.bias_cs;
+    const float2 bv = __half22float2(*bias);
+    vr += p.epi.beta_re * bv.x - p.epi.beta_im * bv.y;
+    vi += p.epi.beta_re * bv.y + p.epi.beta_im * bv.x;
+  }
+  o_re = __float2half_rn(vr);
+  o_im = __float2half_rn(vi);
+}
+
+// Epilogue values of NC consecutive columns n0.. of one row (real or complex pairs).
+template <class T, int NC>
+__device__ __forceinline__ void epi_values(const TcParams &p, int b, int m, int n0, const uint32_t (&r)[32],
+                                           T (&out)[NC]) {
+  if constexpr (std::is_same_v<T, __half>) {
+    if (p.epi.cplx) {
+#pragma unroll
+      for (int j = 0; j < NC; j += 2) epi_cplx_pair(p, b, m, n0 + j, r[j], r[j + 1], out[j], out[j + 1]);
+      return;
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < NC; ++j) out[j] = epi_value<T>(p, b, m, n0 + j, r[j]);
+}
+
 // Direct stores of NC (<= 32) consecutive columns of one output row.
 template <class T, int NC>
 __device__ __forceinline__ void store_row_chunk(const TcParams &p, int b, int m, int n0, const uint32_t (&r)[32]) {
   T *C = (T *)p.C + (int64_t)b * p.sC;
   T out[NC];
-#pragma unroll
-  for (int j = 0; j < NC; ++j) out[j] = epi_value<T>(p, b, m, n0 + j, r[j]);
+  epi_values<T, NC>(p, b, m, n0, r, out);
   constexpr int PER16 = 16 / sizeof(T);
   if (NC % PER16 == 0 && p.c_vec && n0 + NC <= p.N) {
     uint4 *dst = reinterpret_cast<uint4 *>(C + (int64_t)m * p.c_rs + n0);
@@ -509,8 +544,7 @@ __device__ __forceinline__ void pack32(const TcParams &p, int b, int m, int n0, 
     return;
   }
   T out[32];
-#pragma unroll
-  for (int j = 0; j < 32; ++j) out[j] = epi_value<T>(p, b, m, n0 + j, r[j]);
+  epi_values<T, 32>(p, b, m, n0, r, out);
 #pragma unroll
   for (int j = 0; j < 32 * (int)sizeof(T) / 4; ++j) pk[j] = reinterpret_cast<const uint32_t *>(out)[j];
 }

@@ -42,6 +42,7 @@ def plan(a, b, *, backend=None) -> str:
     d.a_rs, d.a_cs = A.stride()
     d.b_rs, d.b_cs = B.stride()
     d.c_rs, d.c_cs = N, 1
+    d.workspace_bytes = -1  # plan as a call with a workspace (the public API always provides one)
     return _lib.plan_query(d)
 
 

@@ -79,6 +79,29 @@ def test_split_k_epilogue_int8_wraps():
         assert ok, f"pair={pair}"
 
 
+def test_complex32_workspace_does_not_clobber_tickets():
+    """complex32 on the tensor cores keeps its expanded B' in the shared
+    workspace; split-K plans that run after it must still find zeroed tickets."""
+    import metalblas_b200 as mb
+    gen = torch.Generator().manual_seed(9)
+    ca = rand((512, 640), torch.complex32, gen)
+    cb = rand((640, 384), torch.complex32, gen)
+    cref = orc.product(to_np(ca), to_np(cb), "complex32")
+    x = rand((1, 8192), torch.bfloat16, gen)
+    w = rand((8192, 4096), torch.bfloat16, gen)
+    gref = orc.product(to_np(x), to_np(w), "bfloat16")
+    a = rand((128, 8192), torch.bfloat16, gen)
+    b = rand((8192, 512), torch.bfloat16, gen)
+    sref = orc.product(to_np(a), to_np(b), "bfloat16")
+    for _ in range(3):
+        ok, err = orc.check(to_np(mb.matmul(ca, cb)), cref, "complex32")
+        assert ok, f"complex32 {err}"
+        ok, err = orc.check(to_np(mb.matmul(x, w)), gref, "bfloat16")   # K-split GEMV
+        assert ok, f"gemv after complex32 {err}"
+        ok, err = orc.check(to_np(_run(a, b, 128, 4, -1)), sref, "bfloat16")  # split-K tensor-core
+        assert ok, f"split-K after complex32 {err}"
+
+
 def test_no_device_timeouts():
     from metalblas_b200 import kernels
     assert kernels.device_status() == 0
