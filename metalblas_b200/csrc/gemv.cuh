@@ -31,10 +31,10 @@ struct GemvParams {
   int conj_w, conj_x;
   int x_vec;             // rows kernel: x is unit-stride and 16-byte aligned in every batch
   EpiScalars epi;
-  int ksplit;            // cols kernel: CTAs along K
-  int64_t kchunk;        // cols kernel: rows of W per CTA
+  int ksplit;            // cols and staged-x rows kernels: CTAs along K
+  int64_t kchunk;        // K elements per CTA (a multiple of 16 bytes of W for the rows kernel)
   void *ws;              // ksplit*batch*R accumulators
-  unsigned *tickets;     // batch * ceil(R / cols_per_cta) counters, zero on entry and exit
+  unsigned *tickets;     // batch * (CTAs along R) counters, zero on entry and exit
 };
 
 template <class T, int VEC>
@@ -48,7 +48,46 @@ struct VecLoad {
 #pragma unroll
     for (int i = 0; i < VEC; ++i) out[i] = x.v[i];
   }
+  __device__ static __forceinline__ uint4 raw(const T *p) {
+    uint4 q;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(q.x), "=r"(q.y), "=r"(q.z), "=r"(q.w) : "l"(p));
+    return q;
+  }
 };
+
+// acc += dot(w, x) over one 16-byte vector of each.  Generic form: unpack and
+// multiply in the accumulator type.
+template <class T, int VEC>
+struct Dot16 {
+  __device__ static __forceinline__ void run(typename Elem<T>::acc &acc, const uint4 &w, const uint4 &x, int cw, int cx) {
+    union { uint4 q; T v[VEC]; } wu, xu;
+    wu.q = w;
+    xu.q = x;
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) Elem<T>::mad(acc, Elem<T>::load(wu.v[i], cw), Elem<T>::load(xu.v[i], cx));
+  }
+};
+// 16-bit floats: the sm_100 mixed-precision FMA (fp16/bf16 inputs, fp32 addend
+// and result, one rounding) takes the packed halves directly, so no conversion
+// instructions are issued; the result equals fmaf(float(w), float(x), acc).
+#define MB_DOT16_MIXED(TYPE, PTXT)                                                                      \
+  template <>                                                                                           \
+  struct Dot16<TYPE, 8> {                                                                               \
+    __device__ static __forceinline__ void run(float &acc, const uint4 &w, const uint4 &x, int, int) {  \
+      const unsigned wv[4] = {w.x, w.y, w.z, w.w}, xv[4] = {x.x, x.y, x.z, x.w};                        \
+      _Pragma("unroll") for (int i = 0; i < 4; ++i)                                                     \
+        asm("{.reg .b16 wl, wh, xl, xh;\n\t"                                                            \
+            "mov.b32 {wl, wh}, %1;\n\t"                                                                 \
+            "mov.b32 {xl, xh}, %2;\n\t"                                                                 \
+            "fma.rn.f32." PTXT " %0, wl, xl, %0;\n\t"                                                   \
+            "fma.rn.f32." PTXT " %0, wh, xh, %0;}"                                                      \
+            : "+f"(acc) : "r"(wv[i]), "r"(xv[i]));                                                      \
+    }                                                                                                   \
+  };
+MB_DOT16_MIXED(__nv_bfloat16, "bf16")
+MB_DOT16_MIXED(__half, "f16")
+#undef MB_DOT16_MIXED
 
 template <class Acc> __device__ __forceinline__ void acc_add(Acc &a, const Acc &b) { a += b; }
 template <> __device__ __forceinline__ void acc_add<cf32>(cf32 &a, const cf32 &b) { a.re += b.re; a.im += b.im; }
@@ -242,6 +281,124 @@ __global__ void __launch_bounds__(NW * 32) gemv_rows_kernel(const GemvParams p) 
 #pragma unroll
   for (int m = 16; m >= 1; m >>= 1) acc_add(acc, shfl_xor(acc, m));
   if (lane == 0) gemv_store<T>(p, b, r, acc);
+}
+
+// ---------------------------------------------------------------------------
+// gemv_rows with x staged in shared memory: W rows contiguous along K, x unit
+// stride and 16-byte aligned.  Each warp owns RPW rows; x is read from global
+// memory once per CTA (in 16 KB chunks) instead of once per row, so the only
+// streamed global traffic is W.  grid (ceil(R / (NW * RPW)), ksplit, batch):
+// CTA (x, y) covers rows [x*NW*RPW, +NW*RPW) over K range [y*kchunk, +kchunk).
+// Splitting K keeps every CTA short, so the last partial wave of a long row
+// sweep does not leave most SMs idle; partials are summed in split order by
+// the CTA that draws the last ticket, as in gemv_cols.
+template <class T, int VEC, int NW, int RPW>
+__global__ void __launch_bounds__(NW * 32, sizeof(typename Elem<T>::acc) == 8 ? 2 : 3)
+gemv_rows_smem_kernel(const GemvParams p) {
+  using E = Elem<T>;
+  using Acc = typename E::acc;
+  constexpr int KC = 16384 / (int)sizeof(T);  // x elements per staged chunk
+  constexpr int U = 4;                        // K vectors in flight per row and lane
+  constexpr int STEP = 32 * VEC;
+  __shared__ __align__(16) T xs[KC];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t b = blockIdx.z;
+  const int64_t r0 = ((int64_t)blockIdx.x * NW + warp) * RPW;
+  const T *X = (const T *)p.X + b * p.sX;
+  const T *W = (const T *)p.W + b * p.sW;
+  Acc acc[RPW];
+#pragma unroll
+  for (int r = 0; r < RPW; ++r) acc[r] = E::zero();
+  const T *wrow[RPW];
+  bool live[RPW];
+#pragma unroll
+  for (int r = 0; r < RPW; ++r) {
+    live[r] = r0 + r < p.R;
+    wrow[r] = W + (live[r] ? (r0 + r) : 0) * p.w_ld;
+  }
+
+  const int64_t kbeg = (int64_t)blockIdx.y * p.kchunk;
+  const int64_t kend = min(p.K, kbeg + p.kchunk);
+  for (int64_t kc = kbeg; kc < kend; kc += KC) {
+    const int kn = (int)min((int64_t)KC, kend - kc);
+    __syncthreads();  // previous chunk fully consumed
+    for (int i = threadIdx.x * VEC; i < kn; i += NW * 32 * VEC) {
+      if (i + VEC <= kn) {
+        *reinterpret_cast<uint4 *>(&xs[i]) = __ldg(reinterpret_cast<const uint4 *>(X + kc + i));
+      } else {
+        for (int j = 0; j < VEC && i + j < kn; ++j) xs[i + j] = X[kc + i + j];
+      }
+    }
+    __syncthreads();
+    const int kvec = (kn / VEC) * VEC;
+    int k = lane * VEC;
+    for (; k + (U - 1) * STEP + VEC <= kvec; k += U * STEP) {
+      uint4 w[RPW][U];
+#pragma unroll
+      for (int r = 0; r < RPW; ++r)
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+          w[r][u] = live[r] ? VecLoad<T, VEC>::raw(wrow[r] + kc + k + u * STEP) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const uint4 xq = *reinterpret_cast<const uint4 *>(&xs[k + u * STEP]);
+#pragma unroll
+        for (int r = 0; r < RPW; ++r)
+          if (live[r]) Dot16<T, VEC>::run(acc[r], w[r][u], xq, p.conj_w, p.conj_x);
+      }
+    }
+    for (; k + VEC <= kvec; k += STEP) {
+      const uint4 xq = *reinterpret_cast<const uint4 *>(&xs[k]);
+#pragma unroll
+      for (int r = 0; r < RPW; ++r)
+        if (live[r]) Dot16<T, VEC>::run(acc[r], VecLoad<T, VEC>::raw(wrow[r] + kc + k), xq, p.conj_w, p.conj_x);
+    }
+    for (int kk = kvec + lane; kk < kn; kk += 32)
+#pragma unroll
+      for (int r = 0; r < RPW; ++r)
+        if (live[r]) E::mad(acc[r], E::load(wrow[r][kc + kk], p.conj_w), E::load(xs[kk], p.conj_x));
+  }
+#pragma unroll
+  for (int r = 0; r < RPW; ++r)
+#pragma unroll
+    for (int m = 16; m >= 1; m >>= 1) acc_add(acc[r], shfl_xor(acc[r], m));
+  if (p.ksplit == 1) {
+#pragma unroll
+    for (int r = 0; r < RPW; ++r)
+      if (lane == 0 && live[r]) gemv_store<T>(p, b, r0 + r, acc[r]);
+    return;
+  }
+  Acc *ws = (Acc *)p.ws + (b * p.ksplit + blockIdx.y) * p.R;
+#pragma unroll
+  for (int r = 0; r < RPW; ++r)
+    if (lane == 0 && live[r]) ws[r0 + r] = acc[r];
+  __shared__ unsigned s_ticket;
+  __threadfence();
+  __syncthreads();
+  unsigned *ticket = p.tickets + b * gridDim.x + blockIdx.x;
+  if (threadIdx.x == 0) s_ticket = atomicAdd(ticket, 1u);
+  __syncthreads();
+  if (s_ticket != (unsigned)(p.ksplit - 1)) return;
+  __threadfence();
+  const Acc *ws0 = (const Acc *)p.ws + b * p.ksplit * p.R;
+  if (threadIdx.x < NW * RPW) {
+    const int64_t r = (int64_t)blockIdx.x * NW * RPW + threadIdx.x;
+    if (r < p.R) {
+      Acc s = E::zero();
+      for (int sp = 0; sp < p.ksplit; ++sp) {
+        Acc v;
+        if constexpr (sizeof(Acc) == 8 && !E::is_int) {
+          float2 f = __ldcg((const float2 *)(ws0 + sp * p.R + r));
+          v = *reinterpret_cast<Acc *>(&f);
+        } else {
+          v = __ldcg(ws0 + sp * p.R + r);
+        }
+        acc_add(s, v);
+      }
+      gemv_store<T>(p, b, r, s);
+    }
+  }
+  if (threadIdx.x == 0) *ticket = 0u;
 }
 
 }  // namespace mb

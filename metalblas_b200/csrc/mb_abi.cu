@@ -123,6 +123,9 @@ void normalize(int64_t rows, int64_t cols, int64_t &rs, int64_t &cs) {
 // plan reads; each kernel returns the counters it used to zero.
 constexpr int64_t kTicketBytes = 256 * 1024;
 constexpr int64_t kMaxTickets = kTicketBytes / 4;
+constexpr int kGemvWarps = 8;         // warps per GEMV CTA
+constexpr int kGemvRowsPerWarp = 2;   // staged-x rows kernel
+constexpr int64_t kGemvRowsPerCta = kGemvWarps * kGemvRowsPerWarp;
 
 enum PlanKind { PK_EMPTY = 0, PK_GEMV_COLS, PK_GEMV_ROWS, PK_TC, PK_SIMT, PK_TC_C32 };
 
@@ -424,6 +427,32 @@ bool plan_gemv(const Op &o, int sms, const mb_gemm_desc *d, bool have_ws, Plan &
       const int64_t accb = acc_is_8byte(o.dt) ? 8 : 4;
       pl.ws_bytes = kTicketBytes + ks * o.batch * g.R * accb;
     }
+  } else if (pl.vec > 1 && g.x_vec) {
+    // Staged-x rows kernel: CTAs of kGemvRowsPerCta rows.  A short CTA pays a
+    // fixed cost of about two memory round trips (x staging, launch, ticket),
+    // so K is split only when rows are long (>= 32 KB) and there are enough
+    // row groups to fill the machine; each split CTA then streams 8 KB per
+    // row (four unrolled steps of a warp).  Measured on B200 over K in
+    // {4096, 8192, 16384} x R in {4096, 14336, 28672} for fp32/fp16/bf16.
+    const int64_t rg = ceil_div(g.R, kGemvRowsPerCta);
+    const int64_t slots = (int64_t)sms * (acc_is_8byte(o.dt) ? 2 : 3);  // launch-bounds minimum
+    const int64_t align = 2048 / esz;  // one unrolled step of a warp: 4 x 32 lanes x 16 bytes
+    const int64_t row_bytes = g.K * esz;
+    int64_t best_ks = 1;
+    if (row_bytes >= 32768 && rg * o.batch >= slots) best_ks = std::min<int64_t>(64, row_bytes / 8192);
+    if (!have_ws || o.batch * rg > kMaxTickets) best_ks = 1;
+    int64_t ks = best_ks;
+    if (d->split_k > 0 && have_ws && o.batch * rg <= kMaxTickets)
+      ks = std::min<int64_t>(d->split_k, std::max<int64_t>(1, g.K / align));
+    if (ks > 1) {
+      g.kchunk = ceil_div(ceil_div(g.K, ks), align) * align;
+      ks = ceil_div(g.K, g.kchunk);
+    }
+    g.ksplit = (int)ks;
+    if (ks > 1) {
+      const int64_t accb = acc_is_8byte(o.dt) ? 8 : 4;
+      pl.ws_bytes = kTicketBytes + ks * o.batch * g.R * accb;
+    }
   }
   pl.kind = kind;
   pl.g = g;
@@ -521,7 +550,7 @@ int launch_simt(const Op &o, const EpiScalars &e, cudaStream_t st) {
     constexpr int BM = 64, BN = 64;
     dim3 grid((unsigned)ceil_div(o.N, BN), (unsigned)ceil_div(o.M, BM), (unsigned)std::min<int64_t>(o.batch, 65535));
     if (grid.y > 65535) return fail(MB_ERR_INVALID, "M too large for the CUDA-core kernel");
-    simt_gemm_kernel<T, BM, BN, 16, 4, 4><<<grid, 256, 0, st>>>(p);
+    simt_gemm_kernel<T, BM, BN, 16, 4, 4><<<grid, 256, 0, st>>>(p);  // 64 x 16 = 4 x 256 runs
   }
   return cuda_check(cudaGetLastError(), "simt_gemm launch");
 }
@@ -530,7 +559,7 @@ template <class T>
 int launch_gemv(const Plan &pl, const EpiScalars &e, void *ws, cudaStream_t st) {
   GemvParams g = pl.g;
   g.epi = e;
-  constexpr int NW = 8;
+  constexpr int NW = kGemvWarps;
   constexpr int V = 16 / sizeof(T);
   if (g.ksplit > 1) {
     g.tickets = reinterpret_cast<unsigned *>(ws);
@@ -543,10 +572,15 @@ int launch_gemv(const Plan &pl, const EpiScalars &e, void *ws, cudaStream_t st) 
     if (pl.vec > 1) gemv_cols_kernel<T, V, NW><<<grid, NW * 32, 0, st>>>(g);
     else gemv_cols_kernel<T, 1, NW><<<dim3((unsigned)ceil_div(g.R, 32), (unsigned)g.ksplit, gz), NW * 32, 0, st>>>(g);
   } else {
-    dim3 grid((unsigned)ceil_div(g.R, NW), 1, gz);
-    if (grid.x > 2147483647u) return fail(MB_ERR_INVALID, "too many rows");
-    if (pl.vec > 1) gemv_rows_kernel<T, V, NW><<<grid, NW * 32, 0, st>>>(g);
-    else gemv_rows_kernel<T, 1, NW><<<grid, NW * 32, 0, st>>>(g);
+    if (pl.vec > 1 && g.x_vec) {
+      constexpr int RPW = kGemvRowsPerWarp;  // x staged in shared memory
+      dim3 grid((unsigned)ceil_div(g.R, NW * RPW), (unsigned)g.ksplit, gz);
+      gemv_rows_smem_kernel<T, V, NW, RPW><<<grid, NW * 32, 0, st>>>(g);
+    } else {
+      dim3 grid((unsigned)ceil_div(g.R, NW), 1, gz);
+      if (pl.vec > 1) gemv_rows_kernel<T, V, NW><<<grid, NW * 32, 0, st>>>(g);
+      else gemv_rows_kernel<T, 1, NW><<<grid, NW * 32, 0, st>>>(g);
+    }
   }
   return cuda_check(cudaGetLastError(), "gemv launch");
 }
@@ -787,7 +821,10 @@ int mb_plan_query(const mb_gemm_desc *d, char *buf, int buflen) {
   switch (pl.kind) {
     case PK_EMPTY: snprintf(tmp, sizeof(tmp), "empty"); break;
     case PK_GEMV_COLS: snprintf(tmp, sizeof(tmp), "gemv_cols vec=%d ksplit=%d", pl.vec, pl.g.ksplit); break;
-    case PK_GEMV_ROWS: snprintf(tmp, sizeof(tmp), "gemv_rows vec=%d", pl.vec); break;
+    case PK_GEMV_ROWS:
+      snprintf(tmp, sizeof(tmp), "gemv_rows vec=%d x_smem=%d ksplit=%d", pl.vec, (pl.vec > 1 && pl.g.x_vec) ? 1 : 0,
+               pl.g.ksplit);
+      break;
     case PK_TC:
       snprintf(tmp, sizeof(tmp),
                "tc bn=%d split=%d dp=%lld half=%d pair=%d swap=%d a_mn=%d b_mn=%d tiles=%lldx%lld ws=%lld", pl.bn,

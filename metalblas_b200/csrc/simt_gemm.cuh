@@ -33,30 +33,41 @@ struct SimtParams {
 };
 
 template <class T, int BM, int BN, int BK, int TM, int TN>
-__global__ void __launch_bounds__(256) simt_gemm_kernel(const SimtParams p) {
+__global__ void __launch_bounds__(256, 2) simt_gemm_kernel(const SimtParams p) {
   using E = Elem<T>;
   using Acc = typename E::acc;
   constexpr int NT = 256;
   constexpr int TX = BN / TN, TY = BM / TM;
   static_assert(TX * TY == NT, "micro-tile grid must cover 256 threads");
-  constexpr int A_PER = BM * BK / NT, B_PER = BK * BN / NT;
-  static_assert(A_PER * NT == BM * BK && B_PER * NT == BK * BN, "tile/thread mismatch");
+  // Staging: every thread moves one run of 4 consecutive elements of A and of B
+  // per K slice, along that operand's contiguous dimension.
+  static_assert(BM * BK == 4 * NT && BK * BN == 4 * NT, "one 4-element run per thread and operand");
   constexpr int PAD = (sizeof(Acc) == 4) ? 4 : 2;
 
-  __shared__ Acc As[2][BK][BM + PAD];
-  __shared__ Acc Bs[2][BK][BN + PAD];
+  __shared__ __align__(16) Acc As[2][BK][BM + PAD];
+  __shared__ __align__(16) Acc Bs[2][BK][BN + PAD];
 
   const int tid = threadIdx.x;
   const int tx = tid % TX, ty = tid / TX;
   const int64_t m0 = (int64_t)blockIdx.y * BM, n0 = (int64_t)blockIdx.x * BN;
-  // Stage the contiguous dimension fastest so global loads coalesce.
+  // A: k contiguous (row-major) -> run along k; otherwise run along m.
   const bool a_kfast = p.a_cs == 1 || (p.a_rs != 1 && (p.a_cs < 0 ? -p.a_cs : p.a_cs) <= (p.a_rs < 0 ? -p.a_rs : p.a_rs));
+  // B: n contiguous (row-major) -> run along n; otherwise run along k.
   const bool b_nfast = p.b_cs == 1 || (p.b_rs != 1 && (p.b_cs < 0 ? -p.b_cs : p.b_cs) <= (p.b_rs < 0 ? -p.b_rs : p.b_rs));
+  // this thread's run: (row or column, first k) inside the tile
+  const int a_m = a_kfast ? tid % BM : (tid % (BM / 4)) * 4;
+  const int a_k = a_kfast ? (tid / BM) * 4 : tid / (BM / 4);
+  const int b_n = b_nfast ? (tid % (BN / 4)) * 4 : tid % BN;
+  const int b_k = b_nfast ? tid / (BN / 4) : (tid / BN) * 4;
+  const int64_t a_step = a_kfast ? p.a_cs : p.a_rs;   // stride along the run
+  const int64_t b_step = b_nfast ? p.b_cs : p.b_rs;
   const int64_t num_kt = (p.K + BK - 1) / BK;
 
   for (int64_t bz = blockIdx.z; bz < p.batch; bz += gridDim.z) {
-    const T *A = (const T *)p.A + bz * p.sA;
-    const T *B = (const T *)p.B + bz * p.sB;
+    // run bases for k0 = 0
+    const T *Ab = (const T *)p.A + bz * p.sA + (m0 + a_m) * p.a_rs + (int64_t)a_k * p.a_cs;
+    const T *Bb = (const T *)p.B + bz * p.sB + (int64_t)b_k * p.b_rs + (n0 + b_n) * p.b_cs;
+    const int64_t a_kt_step = (int64_t)BK * p.a_cs, b_kt_step = (int64_t)BK * p.b_rs;
 
     Acc acc[TM][TN];
 #pragma unroll
@@ -64,40 +75,32 @@ __global__ void __launch_bounds__(256) simt_gemm_kernel(const SimtParams p) {
 #pragma unroll
       for (int j = 0; j < TN; ++j) acc[i][j] = E::zero();
 
-    Acc ra[A_PER], rb[B_PER];
+    Acc ra[4], rb[4];
     auto load_tile = [&](int64_t kt) {
       const int64_t k0 = kt * BK;
+      const T *ap = Ab + kt * a_kt_step;
+      const T *bp = Bb + kt * b_kt_step;
 #pragma unroll
-      for (int q = 0; q < A_PER; ++q) {
-        const int idx = tid + q * NT;
-        const int mm = a_kfast ? idx / BK : idx % BM;
-        const int kk = a_kfast ? idx % BK : idx / BM;
-        const int64_t gm = m0 + mm, gk = k0 + kk;
-        ra[q] = (gm < p.M && gk < p.K) ? E::load(A[gm * p.a_rs + gk * p.a_cs], p.conj_a) : E::zero();
+      for (int j = 0; j < 4; ++j) {
+        const int64_t gm = m0 + a_m + (a_kfast ? 0 : j), gk = k0 + a_k + (a_kfast ? j : 0);
+        ra[j] = (gm < p.M && gk < p.K) ? E::load(ap[j * a_step], p.conj_a) : E::zero();
       }
 #pragma unroll
-      for (int q = 0; q < B_PER; ++q) {
-        const int idx = tid + q * NT;
-        const int nn = b_nfast ? idx % BN : idx / BK;
-        const int kk = b_nfast ? idx / BN : idx % BK;
-        const int64_t gn = n0 + nn, gk = k0 + kk;
-        rb[q] = (gn < p.N && gk < p.K) ? E::load(B[gk * p.b_rs + gn * p.b_cs], p.conj_b) : E::zero();
+      for (int j = 0; j < 4; ++j) {
+        const int64_t gn = n0 + b_n + (b_nfast ? j : 0), gk = k0 + b_k + (b_nfast ? 0 : j);
+        rb[j] = (gn < p.N && gk < p.K) ? E::load(bp[j * b_step], p.conj_b) : E::zero();
       }
     };
     auto store_tile = [&](int buf) {
 #pragma unroll
-      for (int q = 0; q < A_PER; ++q) {
-        const int idx = tid + q * NT;
-        const int mm = a_kfast ? idx / BK : idx % BM;
-        const int kk = a_kfast ? idx % BK : idx / BM;
-        As[buf][kk][mm] = ra[q];
+      for (int j = 0; j < 4; ++j) {
+        if (a_kfast) As[buf][a_k + j][a_m] = ra[j];
+        else As[buf][a_k][a_m + j] = ra[j];
       }
 #pragma unroll
-      for (int q = 0; q < B_PER; ++q) {
-        const int idx = tid + q * NT;
-        const int nn = b_nfast ? idx % BN : idx / BK;
-        const int kk = b_nfast ? idx / BN : idx % BK;
-        Bs[buf][kk][nn] = rb[q];
+      for (int j = 0; j < 4; ++j) {
+        if (b_nfast) Bs[buf][b_k][b_n + j] = rb[j];
+        else Bs[buf][b_k + j][b_n] = rb[j];
       }
     };
 

@@ -102,6 +102,39 @@ def test_complex32_workspace_does_not_clobber_tickets():
         assert ok, f"split-K after complex32 {err}"
 
 
+def _gemv_rows(x, w, split, epilogue=None):
+    """y[b] = W[b] x[b] with W rows contiguous along K (the x @ W^T layout),
+    through the GEMV backend with a forced K split."""
+    B, N, K = w.shape
+    c = torch.empty(B, 1, N, dtype=x.dtype, device=x.device)
+    dispatch._launch(x, w, c, 1, N, K, B, (K, 1, K), (1, K, N * K), (N, 1, N), epilogue=epilogue,
+                     backend=_lib.MB_BACKEND_GEMV, split_k=split, autotune=False)
+    return c
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32, torch.complex64,
+                                   torch.int32], ids=NAME.get)
+def test_gemv_rows_k_split(dtype):
+    """The staged-x rows GEMV split along K: ragged K (not a multiple of the
+    chunk), batches, the alpha/beta epilogue, and two calls in a row with the
+    same tickets."""
+    gen = torch.Generator().manual_seed(10)
+    for (B, N, K) in [(1, 1000, 5000), (3, 77, 12288), (2, 4096, 3000)]:
+        x = rand((B, 1, K), dtype, gen)
+        w = rand((B, N, K), dtype, gen)
+        bias = rand((B, 1, N), dtype, gen)
+        ref = orc.product(to_np(x), to_np(w).transpose(0, 2, 1), NAME[dtype])
+        fref = orc.fused(to_np(bias), to_np(x), to_np(w).transpose(0, 2, 1), 2, 3, NAME[dtype])
+        for split in (1, 2, 3, 7):
+            for _ in range(2):
+                got = _gemv_rows(x, w, split)
+                ok, err = orc.check(to_np(got), ref, NAME[dtype])
+                assert ok, f"{(B, N, K)} split={split} err={err}"
+            got = _gemv_rows(x, w, split, epilogue=(bias, (N, 1, N), 2, 3, True, True))
+            ok, err = orc.check(to_np(got), fref, NAME[dtype])
+            assert ok, f"{(B, N, K)} split={split} addmv err={err}"
+
+
 def test_no_device_timeouts():
     from metalblas_b200 import kernels
     assert kernels.device_status() == 0
