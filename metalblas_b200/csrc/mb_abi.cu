@@ -540,17 +540,34 @@ int launch_simt(const Op &o, const EpiScalars &e, cudaStream_t st) {
   p.c_rs = o.c_rs; p.c_cs = o.c_cs; p.sC = o.sC;
   p.bias_rs = o.bias_rs; p.bias_cs = o.bias_cs; p.bias_bs = o.bias_bs;
   p.conj_a = o.conj_a; p.conj_b = o.conj_b; p.epi = e;
+  // A 4-element run along the contiguous dimension is one aligned vector when
+  // the base, the other stride and the batch stride keep 4-element alignment
+  // (runs start at multiples of 4 along the contiguous dimension).
+  const int64_t run_bytes = 4 * (int64_t)sizeof(T);
+  auto vec_ok = [&](const void *base, int64_t rs, int64_t cs, int64_t bs) {
+    const int64_t lead = (cs == 1) ? rs : (rs == 1 ? cs : -1);
+    if (lead < 0 || reinterpret_cast<uintptr_t>(base) % run_bytes) return 0;
+    if (lead % 4 || (o.batch > 1 && bs % 4)) return 0;
+    return 1;
+  };
+  {
+    // the kernel's choice of run direction (see simt_gemm_kernel)
+    const bool a_kfast = o.a_cs == 1 || (o.a_rs != 1 && std::llabs(o.a_cs) <= std::llabs(o.a_rs));
+    const bool b_nfast = o.b_cs == 1 || (o.b_rs != 1 && std::llabs(o.b_cs) <= std::llabs(o.b_rs));
+    p.a_vec = (a_kfast ? o.a_cs == 1 : o.a_rs == 1) ? vec_ok(o.A, o.a_rs, o.a_cs, o.sA) : 0;
+    p.b_vec = (b_nfast ? o.b_cs == 1 : o.b_rs == 1) ? vec_ok(o.B, o.b_rs, o.b_cs, o.sB) : 0;
+  }
   using Acc = typename Elem<T>::acc;
   if constexpr (sizeof(Acc) == 4) {
     constexpr int BM = 128, BN = 128;
     dim3 grid((unsigned)ceil_div(o.N, BN), (unsigned)ceil_div(o.M, BM), (unsigned)std::min<int64_t>(o.batch, 65535));
     if (grid.y > 65535) return fail(MB_ERR_INVALID, "M too large for the CUDA-core kernel");
-    simt_gemm_kernel<T, BM, BN, 8, 8, 8><<<grid, 256, 0, st>>>(p);
+    simt_gemm_kernel<T, BM, BN, 16, 8, 8><<<grid, 256, 0, st>>>(p);
   } else {
     constexpr int BM = 64, BN = 64;
     dim3 grid((unsigned)ceil_div(o.N, BN), (unsigned)ceil_div(o.M, BM), (unsigned)std::min<int64_t>(o.batch, 65535));
     if (grid.y > 65535) return fail(MB_ERR_INVALID, "M too large for the CUDA-core kernel");
-    simt_gemm_kernel<T, BM, BN, 16, 4, 4><<<grid, 256, 0, st>>>(p);  // 64 x 16 = 4 x 256 runs
+    simt_gemm_kernel<T, BM, BN, 16, 4, 4><<<grid, 256, 0, st>>>(p);
   }
   return cuda_check(cudaGetLastError(), "simt_gemm launch");
 }

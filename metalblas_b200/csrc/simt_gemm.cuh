@@ -13,10 +13,15 @@
 // reference copies with .contiguous() in metalblas/dispatch.py:33-35 and which
 // we read in place).
 //
-// Layout: 256 threads, a BM x BN tile per CTA, a TM x TN micro-tile per thread,
-// BK-deep K slices double-buffered in shared memory with a register prefetch of
-// the next slice.  Operands are converted to the accumulator type when they are
-// staged, so the inner loop is pure FFMA / IMAD.
+// Layout: 256 threads, a BM x BN tile per CTA, a TM x TN micro-tile per thread
+// made of two TM/2 x TN/2 quadrant pairs (rows ty*TM/2 and BM/2 + ty*TM/2, and
+// likewise for columns) so that a warp's shared-memory reads of a K row are
+// contiguous 16-byte vectors.  BK-deep K slices are double-buffered in shared
+// memory with a register prefetch of the next slice; every thread stages runs
+// of 4 elements along each operand's contiguous dimension, with one aligned
+// vector load per run when the layout allows it.  Operands are converted to
+// the accumulator type when they are staged, so the inner loop is pure FFMA /
+// IMAD.
 #pragma once
 #include "mb_common.cuh"
 
@@ -29,8 +34,48 @@ struct SimtParams {
   int64_t a_rs, a_cs, sA, b_rs, b_cs, sB, c_rs, c_cs, sC;
   int64_t bias_rs, bias_cs, bias_bs;
   int conj_a, conj_b;
+  int a_vec, b_vec;  // 4-element runs along the contiguous dimension are aligned vectors
   EpiScalars epi;
 };
+
+// Four consecutive elements from an address aligned to 4 * sizeof(T).
+template <class T>
+__device__ __forceinline__ void load_run4(const T *p, T (&v)[4]) {
+  constexpr int B = 4 * (int)sizeof(T);
+  if constexpr (B == 32) {
+    union { uint4 q[2]; T t[4]; } u;
+    u.q[0] = __ldg(reinterpret_cast<const uint4 *>(p));
+    u.q[1] = __ldg(reinterpret_cast<const uint4 *>(p) + 1);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = u.t[i];
+  } else if constexpr (B == 16) {
+    union { uint4 q; T t[4]; } u;
+    u.q = __ldg(reinterpret_cast<const uint4 *>(p));
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = u.t[i];
+  } else if constexpr (B == 8) {
+    union { uint2 q; T t[4]; } u;
+    u.q = __ldg(reinterpret_cast<const uint2 *>(p));
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = u.t[i];
+  } else {
+    static_assert(B == 4, "element size");
+    union { unsigned q; T t[4]; } u;
+    u.q = __ldg(reinterpret_cast<const unsigned *>(p));
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = u.t[i];
+  }
+}
+
+// Four accumulators to a 16-byte aligned shared-memory address as vectors.
+template <class Acc>
+__device__ __forceinline__ void sts_run4(Acc *dst, const Acc (&v)[4]) {
+  struct alignas(16) V4 { Acc a[4]; };
+  V4 t;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) t.a[i] = v[i];
+  *reinterpret_cast<V4 *>(dst) = t;
+}
 
 template <class T, int BM, int BN, int BK, int TM, int TN>
 __global__ void __launch_bounds__(256, 2) simt_gemm_kernel(const SimtParams p) {
@@ -39,10 +84,12 @@ __global__ void __launch_bounds__(256, 2) simt_gemm_kernel(const SimtParams p) {
   constexpr int NT = 256;
   constexpr int TX = BN / TN, TY = BM / TM;
   static_assert(TX * TY == NT, "micro-tile grid must cover 256 threads");
-  // Staging: every thread moves one run of 4 consecutive elements of A and of B
-  // per K slice, along that operand's contiguous dimension.
-  static_assert(BM * BK == 4 * NT && BK * BN == 4 * NT, "one 4-element run per thread and operand");
-  constexpr int PAD = (sizeof(Acc) == 4) ? 4 : 2;
+  constexpr int HM = TM / 2, HN = TN / 2;
+  static_assert(HM * (int)sizeof(Acc) % 16 == 0 && HN * (int)sizeof(Acc) % 16 == 0, "16-byte fragment reads");
+  // runs of 4 elements per thread and operand per K slice
+  constexpr int RA = BM * BK / (4 * NT), RB = BK * BN / (4 * NT);
+  static_assert(RA * 4 * NT == BM * BK && RB * 4 * NT == BK * BN && RA >= 1 && RB >= 1, "run tiling");
+  constexpr int PAD = 16 / (int)sizeof(Acc);  // keeps rows 16-byte aligned
 
   __shared__ __align__(16) Acc As[2][BK][BM + PAD];
   __shared__ __align__(16) Acc Bs[2][BK][BN + PAD];
@@ -50,24 +97,24 @@ __global__ void __launch_bounds__(256, 2) simt_gemm_kernel(const SimtParams p) {
   const int tid = threadIdx.x;
   const int tx = tid % TX, ty = tid / TX;
   const int64_t m0 = (int64_t)blockIdx.y * BM, n0 = (int64_t)blockIdx.x * BN;
-  // A: k contiguous (row-major) -> run along k; otherwise run along m.
+  // A: k contiguous (row-major) -> runs along k; otherwise runs along m.
   const bool a_kfast = p.a_cs == 1 || (p.a_rs != 1 && (p.a_cs < 0 ? -p.a_cs : p.a_cs) <= (p.a_rs < 0 ? -p.a_rs : p.a_rs));
-  // B: n contiguous (row-major) -> run along n; otherwise run along k.
+  // B: n contiguous (row-major) -> runs along n; otherwise runs along k.
   const bool b_nfast = p.b_cs == 1 || (p.b_rs != 1 && (p.b_cs < 0 ? -p.b_cs : p.b_cs) <= (p.b_rs < 0 ? -p.b_rs : p.b_rs));
-  // this thread's run: (row or column, first k) inside the tile
-  const int a_m = a_kfast ? tid % BM : (tid % (BM / 4)) * 4;
-  const int a_k = a_kfast ? (tid / BM) * 4 : tid / (BM / 4);
-  const int b_n = b_nfast ? (tid % (BN / 4)) * 4 : tid % BN;
-  const int b_k = b_nfast ? tid / (BN / 4) : (tid / BN) * 4;
-  const int64_t a_step = a_kfast ? p.a_cs : p.a_rs;   // stride along the run
+  const bool a_vec = p.a_vec != 0, b_vec = p.b_vec != 0;
+  // this thread's run r: (row or column, first k) inside the tile; recomputed
+  // where used (a few integer ops) rather than held in registers
+  auto a_m = [&](int r) { const int q = tid + r * NT; return a_kfast ? q % BM : (q % (BM / 4)) * 4; };
+  auto a_k = [&](int r) { const int q = tid + r * NT; return a_kfast ? (q / BM) * 4 : q / (BM / 4); };
+  auto b_n = [&](int r) { const int q = tid + r * NT; return b_nfast ? (q % (BN / 4)) * 4 : q % BN; };
+  auto b_k = [&](int r) { const int q = tid + r * NT; return b_nfast ? q / (BN / 4) : (q / BN) * 4; };
+  const int64_t a_step = a_kfast ? p.a_cs : p.a_rs;  // stride along a run
   const int64_t b_step = b_nfast ? p.b_cs : p.b_rs;
   const int64_t num_kt = (p.K + BK - 1) / BK;
 
   for (int64_t bz = blockIdx.z; bz < p.batch; bz += gridDim.z) {
-    // run bases for k0 = 0
-    const T *Ab = (const T *)p.A + bz * p.sA + (m0 + a_m) * p.a_rs + (int64_t)a_k * p.a_cs;
-    const T *Bb = (const T *)p.B + bz * p.sB + (int64_t)b_k * p.b_rs + (n0 + b_n) * p.b_cs;
-    const int64_t a_kt_step = (int64_t)BK * p.a_cs, b_kt_step = (int64_t)BK * p.b_rs;
+    const T *A0 = (const T *)p.A + bz * p.sA;
+    const T *B0 = (const T *)p.B + bz * p.sB;
 
     Acc acc[TM][TN];
 #pragma unroll
@@ -75,32 +122,64 @@ __global__ void __launch_bounds__(256, 2) simt_gemm_kernel(const SimtParams p) {
 #pragma unroll
       for (int j = 0; j < TN; ++j) acc[i][j] = E::zero();
 
-    Acc ra[4], rb[4];
+    Acc ra[RA][4], rb[RB][4];
     auto load_tile = [&](int64_t kt) {
       const int64_t k0 = kt * BK;
-      const T *ap = Ab + kt * a_kt_step;
-      const T *bp = Bb + kt * b_kt_step;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int64_t gm = m0 + a_m + (a_kfast ? 0 : j), gk = k0 + a_k + (a_kfast ? j : 0);
-        ra[j] = (gm < p.M && gk < p.K) ? E::load(ap[j * a_step], p.conj_a) : E::zero();
+      for (int r = 0; r < RA; ++r) {
+        const int64_t gm = m0 + a_m(r), gk = k0 + a_k(r);
+        const T *ap = A0 + gm * p.a_rs + gk * p.a_cs;
+        const bool full = a_kfast ? (gm < p.M && gk + 3 < p.K) : (gm + 3 < p.M && gk < p.K);
+        if (a_vec && full) {
+          T v[4];
+          load_run4<T>(ap, v);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) ra[r][j] = E::load(v[j], p.conj_a);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const bool in = a_kfast ? (gm < p.M && gk + j < p.K) : (gm + j < p.M && gk < p.K);
+            ra[r][j] = in ? E::load(ap[j * a_step], p.conj_a) : E::zero();
+          }
+        }
       }
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int64_t gn = n0 + b_n + (b_nfast ? j : 0), gk = k0 + b_k + (b_nfast ? 0 : j);
-        rb[j] = (gn < p.N && gk < p.K) ? E::load(bp[j * b_step], p.conj_b) : E::zero();
+      for (int r = 0; r < RB; ++r) {
+        const int64_t gn = n0 + b_n(r), gk = k0 + b_k(r);
+        const T *bp = B0 + gk * p.b_rs + gn * p.b_cs;
+        const bool full = b_nfast ? (gn + 3 < p.N && gk < p.K) : (gn < p.N && gk + 3 < p.K);
+        if (b_vec && full) {
+          T v[4];
+          load_run4<T>(bp, v);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) rb[r][j] = E::load(v[j], p.conj_b);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const bool in = b_nfast ? (gn + j < p.N && gk < p.K) : (gn < p.N && gk + j < p.K);
+            rb[r][j] = in ? E::load(bp[j * b_step], p.conj_b) : E::zero();
+          }
+        }
       }
     };
     auto store_tile = [&](int buf) {
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        if (a_kfast) As[buf][a_k + j][a_m] = ra[j];
-        else As[buf][a_k][a_m + j] = ra[j];
+      for (int r = 0; r < RA; ++r) {
+        if (a_kfast) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) As[buf][a_k(r) + j][a_m(r)] = ra[r][j];
+        } else {
+          sts_run4<Acc>(&As[buf][a_k(r)][a_m(r)], ra[r]);
+        }
       }
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        if (b_nfast) Bs[buf][b_k][b_n + j] = rb[j];
-        else Bs[buf][b_k + j][b_n] = rb[j];
+      for (int r = 0; r < RB; ++r) {
+        if (b_nfast) {
+          sts_run4<Acc>(&Bs[buf][b_k(r)][b_n(r)], rb[r]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) Bs[buf][b_k(r) + j][b_n(r)] = rb[r][j];
+        }
       }
     };
 
@@ -116,9 +195,15 @@ __global__ void __launch_bounds__(256, 2) simt_gemm_kernel(const SimtParams p) {
       for (int kk = 0; kk < BK; ++kk) {
         Acc av[TM], bv[TN];
 #pragma unroll
-        for (int i = 0; i < TM; ++i) av[i] = As[cur][kk][ty * TM + i];
+        for (int i = 0; i < HM; ++i) {
+          av[i] = As[cur][kk][ty * HM + i];
+          av[HM + i] = As[cur][kk][BM / 2 + ty * HM + i];
+        }
 #pragma unroll
-        for (int j = 0; j < TN; ++j) bv[j] = Bs[cur][kk][tx * TN + j];
+        for (int j = 0; j < HN; ++j) {
+          bv[j] = Bs[cur][kk][tx * HN + j];
+          bv[HN + j] = Bs[cur][kk][BN / 2 + tx * HN + j];
+        }
 #pragma unroll
         for (int i = 0; i < TM; ++i)
 #pragma unroll
@@ -132,11 +217,11 @@ __global__ void __launch_bounds__(256, 2) simt_gemm_kernel(const SimtParams p) {
     const T *bias = (const T *)p.bias + (p.epi.enabled ? bz * p.bias_bs : 0);
 #pragma unroll
     for (int i = 0; i < TM; ++i) {
-      const int64_t gm = m0 + ty * TM + i;
+      const int64_t gm = m0 + (i < HM ? ty * HM + i : BM / 2 + ty * HM + (i - HM));
       if (gm >= p.M) continue;
 #pragma unroll
       for (int j = 0; j < TN; ++j) {
-        const int64_t gn = n0 + tx * TN + j;
+        const int64_t gn = n0 + (j < HN ? tx * HN + j : BN / 2 + tx * HN + (j - HN));
         if (gn >= p.N) continue;
         Acc v = acc[i][j];
         if (p.epi.enabled) v = EpiOps<T>::apply(v, bias + gm * p.bias_rs + gn * p.bias_cs, p.epi);
