@@ -92,7 +92,7 @@ typedef struct mb_gemm_desc {
     /* epilogue */
     int32_t epilogue;       /* 0: plain product; 1: alpha/beta/bias epilogue */
     int32_t alpha_nz, beta_nz;
-    int32_t _pad0;
+    int32_t stream_k;       /* plan override, TC: 0 planner decides, 1 no stream-K tail, 2 stream-K tail */
     const void *bias;       /* same dtype as C */
     int64_t bias_rs, bias_cs, bias_bs;
     double alpha_re, alpha_im, beta_re, beta_im;   /* float / complex scalars */

@@ -51,7 +51,7 @@ class GemmDesc(ctypes.Structure):
         ("c_rs", ctypes.c_int64), ("c_cs", ctypes.c_int64), ("sC", ctypes.c_int64),
         ("conj_a", ctypes.c_int32), ("conj_b", ctypes.c_int32),
         ("epilogue", ctypes.c_int32), ("alpha_nz", ctypes.c_int32), ("beta_nz", ctypes.c_int32),
-        ("_pad0", ctypes.c_int32),
+        ("stream_k", ctypes.c_int32),
         ("bias", ctypes.c_void_p),
         ("bias_rs", ctypes.c_int64), ("bias_cs", ctypes.c_int64), ("bias_bs", ctypes.c_int64),
         ("alpha_re", ctypes.c_double), ("alpha_im", ctypes.c_double),

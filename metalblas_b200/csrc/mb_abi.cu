@@ -141,6 +141,8 @@ struct Plan {
   int64_t dp_tiles = 0;  // whole tiles; tiles after them are split `splits` ways along K,
   int tail_half = 0;     // or (tail_half) into two half-width units each
   int pair = 1;          // 2: CTA-pair kernel (cta_group::2, 256-row tiles)
+  int sk = 0;            // tail tiles stream-K over sk_ctas CTAs (splits = partial slots per tile)
+  int64_t sk_ctas = 0;
   // complex32 as one real fp16 GEMM C' = A' B' (PK_TC_C32); the TC fields above
   // describe that real GEMM
   int c32_pack_a = 0;               // A' is a packed copy (else A's own storage)
@@ -229,8 +231,21 @@ const bool g_pair_enabled = [] {
 
 // HBM bytes per clock per SM when every SM streams (6537 GB/s / 148 / 1.965 GHz).
 constexpr double kHbmBytesPerClkPerSm = 22.4;
+// Operand bytes one SM's TMA pipeline sustains per clock (B200, 4-8 stage ring).
+constexpr double kSmFillBytesPerClk = 45.0;
 
-void choose_tc_tile(const Op &o, int sms, int force_bn, int force_split, int force_pair, bool have_ws, Plan &pl) {
+// Stream-K partition of `tail` tiles of kb K-blocks over G CTAs: the most
+// pieces any tile is cut into (CTA g owns iterations [g*I/G, (g+1)*I/G)).
+int sk_max_parts(int64_t tail, int64_t kb, int64_t G) {
+  const int64_t I = tail * kb;
+  auto owner = [&](int64_t i) { return ((i + 1) * G - 1) / I; };
+  int64_t mx = 0;
+  for (int64_t t = 0; t < tail; ++t) mx = std::max(mx, owner((t + 1) * kb - 1) - owner(t * kb) + 1);
+  return (int)mx;
+}
+
+void choose_tc_tile(const Op &o, int sms, int force_bn, int force_split, int force_pair, int force_sk, bool have_ws,
+                    Plan &pl) {
   const int esz = elem_size(o.dt);
   const int64_t BK = 128 / esz;
   const int64_t kb_total = ceil_div(o.K, BK);
@@ -240,10 +255,14 @@ void choose_tc_tile(const Op &o, int sms, int force_bn, int force_split, int for
       (double)(o.M * o.K * (o.sA ? o.batch : 1) + o.N * o.K * (o.sB ? o.batch : 1)) * esz +
       (double)(o.M * o.N * o.batch) * esz;
   auto consider = [&](double compute, double units, double waves, double extra_bytes, int bn, int am, int bm,
-                      int seff, int64_t kbp, int64_t dp, int half, int pair = 1) {
-    // HBM floor, streamed by the SMs busy on average across the waves
+                      int seff, int64_t kbp, int64_t dp, int half, int pair = 1, int sk = 0) {
+    // HBM floor: the whole chip's bandwidth, or what the SMs busy on average
+    // across the waves can pull (about 45 B/clk each through TMA), if lower.
+    // Stream-K CTAs stream B rows at unrelated K offsets at the same time,
+    // which measured ~15% below the same bytes read by K-aligned splits.
     const double avg_active = units / std::max(1.0, waves);
-    const double mem = (opnd_bytes + extra_bytes) / (kHbmBytesPerClkPerSm * avg_active);
+    const double rate = std::min(kHbmBytesPerClkPerSm * sms, kSmFillBytesPerClk * avg_active);
+    const double mem = (opnd_bytes + extra_bytes) / rate * (sk ? 1.15 : 1.0);
     const double t = std::max(compute, mem) * (1.0 + 0.002 * seff);
     if (t < best) {
       best = t;
@@ -251,6 +270,7 @@ void choose_tc_tile(const Op &o, int sms, int force_bn, int force_split, int for
       pl.tiles_m = ceil_div(o.M, 128 * pair); pl.tiles_n = ceil_div(o.N, bn);
       pl.kb_total = kb_total; pl.kb_per_split = kbp;
       pl.dp_tiles = dp; pl.tail_half = half; pl.pair = pair;
+      pl.sk = sk; pl.sk_ctas = sk ? sms : 0;
     }
   };
   for (int bn : bns) {
@@ -260,7 +280,7 @@ void choose_tc_tile(const Op &o, int sms, int force_bn, int force_split, int for
     if (!force_bn && bn > 16 && round_up(o.N, 16) <= bn / 2) continue;  // a smaller tile already covers N
     const int64_t tiles = o.batch * ceil_div(o.M, 128) * ceil_div(o.N, bn);
     const double unit_full = kb_total * kblock_cycles(bn) + 4.0 * bn;
-    if ((!force_split || force_split == 1) && force_pair != 2) {
+    if ((!force_split || force_split == 1) && force_pair != 2 && force_sk != 2) {
       // whole tiles
       const int64_t w = ceil_div(tiles, sms);
       consider(w * unit_full, (double)tiles, (double)w, 0.0, bn, am, bm, 1, kb_total, tiles, 0);
@@ -281,7 +301,7 @@ void choose_tc_tile(const Op &o, int sms, int force_bn, int force_split, int for
     // Pairs pay a cross-CTA handshake per tile (both epilogues must drain an
     // accumulator before the next MMA): only worth it with enough K per tile.
     const bool want_pair = force_pair == 2 || (force_pair == 0 && g_pair_enabled && o.M > 128 && kb_total >= 8);
-    if ((bn == 128 || bn == 256) && pair_fits && want_pair && (!force_split || force_split == 1)) {
+    if ((bn == 128 || bn == 256) && pair_fits && want_pair && (!force_split || force_split == 1) && force_sk != 2) {
       const int pairs = sms / 2;
       const int64_t ptiles = o.batch * ceil_div(o.M, 256) * ceil_div(o.N, bn);
       const double punit = kb_total * kblock_cycles_pair(bn) + 4.0 * bn;
@@ -297,6 +317,25 @@ void choose_tc_tile(const Op &o, int sms, int force_bn, int force_split, int for
                  0.0, bn, am, bm, 1, kb_total, dp, 1, 2);
       }
     }
+    // stream-K tail: whole tiles for the full waves, the tiles left over cut
+    // into equal K-block ranges, one per CTA (every CTA busy to the end)
+    if (have_ws && force_pair != 2 && force_sk != 1 && !force_split && tiles % sms) {
+      const int64_t dp = (tiles / sms) * sms;
+      const int64_t tail = tiles - dp;
+      const int64_t iters = tail * kb_total;
+      if (iters >= 4 * (int64_t)sms || (force_sk == 2 && iters >= sms)) {
+        const int maxp = sk_max_parts(tail, kb_total, sms);
+        if (tail * tc::NUM_EPI_WARPS <= kMaxTickets) {
+          const double share = (double)ceil_div(iters, sms) * kblock_cycles(bn);
+          // the fixup: the last piece of a tile re-reads every partial of it
+          const double fix = maxp > 1 ? 8.0 * 4.0 * bn + 8.0 * maxp * bn : 4.0 * bn;
+          const double extra = maxp > 1 ? (double)tail * maxp * 128.0 * bn * 8.0 : 0.0;
+          consider((dp / sms) * unit_full + share + fix, (double)(dp + sms), (double)(dp / sms + 1), extra, bn, am,
+                   bm, maxp, kb_total, dp, 0, 1, 1);
+        }
+      }
+    }
+    if (force_sk == 2) continue;
     // every tile split along K (long-K, few tiles: skinny and thin shapes)
     int max_split = have_ws && force_pair != 2 ? (int)std::min<int64_t>(kb_total, 64) : 1;
     if (tiles * tc::NUM_EPI_WARPS > kMaxTickets) max_split = 1;  // ticket counters
@@ -320,7 +359,7 @@ void choose_tc_tile(const Op &o, int sms, int force_bn, int force_split, int for
 // Fill pl for the TC path on operands o (possibly swapped); false if TMA can't.
 bool plan_tc(const Op &o, int sms, const mb_gemm_desc *d, bool have_ws, Plan &pl) {
   pl.bn = 0;
-  choose_tc_tile(o, sms, d->tile_n, d->split_k, d->cta_pair, have_ws, pl);
+  choose_tc_tile(o, sms, d->tile_n, d->split_k, d->cta_pair, d->stream_k, have_ws, pl);
   if (!pl.bn) return false;
   pl.kind = PK_TC;
   const int64_t tiles = o.batch * pl.tiles_m * pl.tiles_n;
@@ -329,6 +368,7 @@ bool plan_tc(const Op &o, int sms, const mb_gemm_desc *d, bool have_ws, Plan &pl
   } else if (!pl.tail_half) {
     pl.splits = 1;
     pl.dp_tiles = tiles;
+    pl.sk = 0;
   }
   return true;
 }
@@ -665,11 +705,16 @@ int launch_tc_bn(const Op &o, const Plan &pl, const EpiScalars &e, void *ws, int
   p.tiles_m = (int)pl.tiles_m; p.tiles_n = (int)pl.tiles_n;
   p.splits = pl.splits; p.kb_total = (int)pl.kb_total; p.kb_per_split = (int)pl.kb_per_split;
   const int64_t tiles = o.batch * pl.tiles_m * pl.tiles_n;
-  const int64_t units = pl.dp_tiles + (tiles - pl.dp_tiles) * (pl.tail_half ? 2 : pl.splits);
+  const int64_t units = pl.dp_tiles + (pl.sk ? 0 : (tiles - pl.dp_tiles) * (pl.tail_half ? 2 : pl.splits));
   if (units >= (1ll << 31)) return fail(MB_ERR_INVALID, "too many tiles");
   p.dp_tiles = (int)pl.dp_tiles;
   p.tail_half = pl.tail_half;
   p.num_units = (int)units;
+  if (pl.sk) {
+    if constexpr (PAIR != 1) return fail(MB_ERR_INVALID, "stream-K needs single-CTA tiles");
+    p.sk = 1;
+    p.sk_iters = (long long)(tiles - pl.dp_tiles) * pl.kb_total;
+  }
   p.group_m = 16;
   p.C = o.C; p.c_rs = o.c_rs; p.c_cs = o.c_cs; p.sC = o.sC;
   p.bias = o.bias; p.bias_rs = o.bias_rs; p.bias_cs = o.bias_cs; p.bias_bs = o.bias_bs;
@@ -698,7 +743,8 @@ int launch_tc_bn(const Op &o, const Plan &pl, const EpiScalars &e, void *ws, int
     attr_done[dev] = 1;
   }
   if constexpr (PAIR == 1) {
-    const int grid = (int)std::min<int64_t>(units, sms);
+    // stream-K ranges are cut for exactly sk_ctas CTAs
+    const int grid = pl.sk ? (int)pl.sk_ctas : (int)std::min<int64_t>(units, sms);
     kern<<<grid, tc::NUM_THREADS, C_::SMEM_BYTES, st>>>(p);
   } else {
     // one cluster (CTA pair) per unit slot; the pair shares each 256-row tile
@@ -844,8 +890,8 @@ int mb_plan_query(const mb_gemm_desc *d, char *buf, int buflen) {
       break;
     case PK_TC:
       snprintf(tmp, sizeof(tmp),
-               "tc bn=%d split=%d dp=%lld half=%d pair=%d swap=%d a_mn=%d b_mn=%d tiles=%lldx%lld ws=%lld", pl.bn,
-               pl.splits, (long long)pl.dp_tiles, pl.tail_half, pl.pair, pl.swap, pl.a_mn, pl.b_mn,
+               "tc bn=%d split=%d dp=%lld half=%d pair=%d sk=%d swap=%d a_mn=%d b_mn=%d tiles=%lldx%lld ws=%lld",
+               pl.bn, pl.splits, (long long)pl.dp_tiles, pl.tail_half, pl.pair, pl.sk, pl.swap, pl.a_mn, pl.b_mn,
                (long long)pl.tiles_m, (long long)pl.tiles_n, (long long)pl.ws_bytes);
       break;
     case PK_TC_C32:

@@ -27,9 +27,17 @@
 // tile i+1.
 //
 // Schedule: units are whole output tiles, except that when the tiles do not
-// fill the last wave of the grid, the leftover tiles ("tail") are split along K
-// so the last wave is full as well (dp_tiles whole tiles first, then
-// (tiles - dp_tiles) * splits split units).
+// fill the last wave of the grid, the leftover tiles ("tail") are cut so the
+// last wave is full as well: dp_tiles whole tiles first, then either
+//  * half-width units (two per tail tile),
+//  * fixed K splits ((tiles - dp_tiles) * splits split units), or
+//  * stream-K: the tail's tiles x K-blocks iterations are divided into equal
+//    contiguous ranges, one per CTA; a range is cut at tile boundaries into
+//    pieces, and a tile's pieces (at most `splits`) are summed in K order by
+//    the warp that draws the last ticket.  Every CTA does the same number of
+//    K-blocks, whatever the tile count.
+// Partials are stored lane-interleaved (a warp's 32 rows of 4 columns form one
+// 512-byte run) so both the writes and the reduction are coalesced.
 //
 // Operand layouts: each operand may be K-major or MN-major in global memory;
 // TMA copies it into the matching canonical SWIZZLE_128B layout and the UMMA
@@ -78,6 +86,8 @@ struct TcParams {
   int c_tma;             // write C through tmC
   void *ws;              // split-K partials: tail_tiles * splits * BM * BN * 4 bytes
   unsigned *tickets;     // NUM_EPI_WARPS per tail tile, zero on entry and exit
+  int sk;                // tail tiles partitioned stream-K (splits = partial slots per tile)
+  long long sk_iters;    // tail tiles * kb_total: the K-block iterations shared out
   unsigned long long timeout_ns;
 };
 
@@ -404,15 +414,17 @@ __device__ __forceinline__ uint32_t make_idesc(int a_mn, int b_mn) {
 struct Unit {
   int b, tm, tn;
   int tile;          // raster index over all output tiles
-  int s;             // split index (0 unless a K-split unit)
+  int s;             // split / piece index (0 unless a K-split unit)
+  int nparts;        // partial sums of this tile (split units)
   int kb0, kb1;      // K-blocks of this unit
   bool split;        // partial-sum unit (tail tile split along K)
   int half;          // -1: whole tile; 0/1: which half-width (BN/2 columns) of the tile
   int tail;          // tile - dp_tiles (valid for tail units)
 };
+__device__ __forceinline__ void tile_coords(const TcParams &p, Unit &r);
 __device__ __forceinline__ Unit decode_unit(const TcParams &p, int u) {
   Unit r;
-  r.s = 0; r.split = false; r.half = -1; r.tail = 0;
+  r.s = 0; r.split = false; r.half = -1; r.tail = 0; r.nparts = 1;
   r.kb0 = 0; r.kb1 = p.kb_total;
   if (u < p.dp_tiles) {
     r.tile = u;
@@ -427,9 +439,16 @@ __device__ __forceinline__ Unit decode_unit(const TcParams &p, int u) {
     r.tile = p.dp_tiles + r.tail;
     r.s = v % p.splits;
     r.split = true;
+    r.nparts = p.splits;
     r.kb0 = r.s * p.kb_per_split;
     r.kb1 = min(p.kb_total, r.kb0 + p.kb_per_split);
   }
+  tile_coords(p, r);
+  return r;
+}
+// (batch, tile row, tile column) of r.tile: grouped raster, group_m tile rows
+// per group so that concurrently running tiles share A and B panels in L2.
+__device__ __forceinline__ void tile_coords(const TcParams &p, Unit &r) {
   const int per_batch = p.tiles_m * p.tiles_n;
   r.b = r.tile / per_batch;
   const int q = r.tile % per_batch;
@@ -440,7 +459,52 @@ __device__ __forceinline__ Unit decode_unit(const TcParams &p, int u) {
   const int w = q % per_group;
   r.tm = first_m + w % gsz;
   r.tn = w / gsz;
-  return r;
+}
+
+// The stream-K CTA that owns iteration i of the tail (ranges [g*I/G, (g+1)*I/G)).
+__device__ __forceinline__ long long sk_owner(long long i, long long I, int G) {
+  return ((i + 1) * (long long)G - 1) / I;
+}
+
+// The sequence of units one CTA (or CTA pair) works through; every role of the
+// CTA walks the same sequence.
+struct UnitIter {
+  int u;                // next strided unit
+  long long i, iend;    // remaining stream-K range
+};
+__device__ __forceinline__ UnitIter unit_iter(const TcParams &p, int id, int n) {
+  UnitIter it;
+  it.u = id;
+  it.i = it.iend = 0;
+  if (p.sk) {
+    it.i = (long long)id * p.sk_iters / n;
+    it.iend = (long long)(id + 1) * p.sk_iters / n;
+  }
+  return it;
+}
+__device__ __forceinline__ bool unit_next(const TcParams &p, UnitIter &it, int n, Unit &r) {
+  if (it.u < p.num_units) {
+    r = decode_unit(p, it.u);
+    it.u += n;
+    return true;
+  }
+  if (it.i >= it.iend) return false;
+  const long long KB = p.kb_total;
+  const int tail = (int)(it.i / KB);
+  const long long t0 = (long long)tail * KB, t1 = t0 + KB;
+  const long long end = min(it.iend, t1);
+  r.tail = tail;
+  r.tile = p.dp_tiles + tail;
+  r.half = -1;
+  r.kb0 = (int)(it.i - t0);
+  r.kb1 = (int)(end - t0);
+  const long long first = sk_owner(t0, p.sk_iters, n);
+  r.s = (int)(sk_owner(it.i, p.sk_iters, n) - first);
+  r.nparts = (int)(sk_owner(t1 - 1, p.sk_iters, n) - first) + 1;
+  r.split = r.nparts > 1;
+  it.i = end;
+  tile_coords(p, r);
+  return true;
 }
 
 template <class T>
@@ -621,8 +685,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
       uint32_t phase = 0;
       int issued_stage = -1;
       uint32_t issued_phase = 0;
-      for (int u = pair_id; u < p.num_units; u += npairs) {
-        const Unit w = decode_unit(p, u);
+      UnitIter it = unit_iter(p, pair_id, npairs);
+      Unit w;
+      while (unit_next(p, it, npairs, w)) {
         const int ba = p.a_bcast ? 0 : w.b, bb = p.b_bcast ? 0 : w.b;
         // This CTA's columns of B: its share (1/PAIR) of the unit's columns.  A
         // half-width unit loads only its BN/2 columns of an MN-major B; a
@@ -683,8 +748,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
       int abuf = 0;
       uint32_t aphase = 0;
       bool issued_any = false;
-      for (int u = pair_id; u < p.num_units; u += npairs) {
-        const Unit w = decode_unit(p, u);
+      UnitIter it = unit_iter(p, pair_id, npairs);
+      Unit w;
+      while (unit_next(p, it, npairs, w)) {
         const uint32_t idesc = w.half >= 0 ? idesc_half : idesc_full;
         // K-major B holds the whole tile: a half-width unit starts BN/2 rows in.
         const uint32_t b_off = (w.half > 0 && !p.b_mn) ? (uint32_t)(BN / 2) * 128u : 0u;
@@ -732,8 +798,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
     int sbuf = 0;                         // staging buffer to fill next
     int abuf = 0;
     uint32_t aphase = 0;
-    for (int u = pair_id; u < p.num_units; u += npairs) {
-      const Unit w = decode_unit(p, u);
+    UnitIter it = unit_iter(p, pair_id, npairs);
+    Unit w;
+    while (unit_next(p, it, npairs, w)) {
       if (!wait_x(tfull_bar(abuf), aphase)) break;
       tc_fence_after();
       const int m0 = w.tm * TM_ROWS + (int)rank * BM;  // this CTA's first output row of the tile
@@ -813,9 +880,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
         __syncwarp();
         if (lane == 0) release_tmem(abuf);
       } else {
-        // Split-K: publish raw accumulators (tile-local row-major, 4 B each).
-        uint32_t *part = reinterpret_cast<uint32_t *>(p.ws) +
-                         ((int64_t)w.tail * p.splits + w.s) * (int64_t)(BM * BN) + (int64_t)row * BN + col0;
+        // Split-K: publish raw accumulators.  Slot (tail, s) holds BM x BN
+        // 4-byte values; warp ew's 32 rows x wcols columns are stored as
+        // uint4 runs indexed (column / 4) * 32 + lane.
+        const int64_t slot_words = (int64_t)BM * BN;
+        const int64_t warp_off = (int64_t)ew * 32 * wcols;
+        uint4 *part = reinterpret_cast<uint4 *>(reinterpret_cast<uint32_t *>(p.ws) +
+                                                ((int64_t)w.tail * p.splits + w.s) * slot_words + warp_off) + lane;
 #pragma unroll 1
         for (int c = 0; c < wcols; c += RCH) {
           uint32_t r[32];
@@ -823,7 +894,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
           tmem_wait_ld();
 #pragma unroll
           for (int j = 0; j < RCH; j += 4)
-            __stcg(reinterpret_cast<uint4 *>(part + c + j), make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]));
+            __stcg(part + ((c + j) >> 2) * 32, make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]));
         }
         tc_fence_before();
         __syncwarp();
@@ -837,27 +908,42 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
         unsigned *ticket = p.tickets + (int64_t)w.tail * NUM_EPI_WARPS + ew;
         if (lane == 0) tk = atomicAdd(ticket, 1u);
         tk = __shfl_sync(0xffffffffu, tk, 0);
-        if (tk == (unsigned)(p.splits - 1)) {
+        if (tk == (unsigned)(w.nparts - 1)) {
           __threadfence();
-          const uint32_t *base = reinterpret_cast<const uint32_t *>(p.ws) +
-                                 (int64_t)w.tail * p.splits * (int64_t)(BM * BN) + (int64_t)row * BN + col0;
+          const uint4 *base = reinterpret_cast<const uint4 *>(reinterpret_cast<const uint32_t *>(p.ws) +
+                                                              (int64_t)w.tail * p.splits * slot_words + warp_off) + lane;
+          const int64_t slot_vec = slot_words / 4;
+          constexpr int NV = RCH / 4;                  // uint4 per lane per partial and chunk
+          constexpr int PB = NV >= 8 ? 2 : (NV >= 4 ? 4 : 8);  // partials in flight: 16 loads per lane
 #pragma unroll 1
           for (int c = 0; c < wcols; c += RCH) {
             uint32_t r[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) r[j] = 0;
-            for (int s = 0; s < p.splits; ++s) {
-              const uint32_t *src = base + (int64_t)s * (BM * BN) + c;
+            const uint4 *src = base + (c >> 2) * 32;
+#pragma unroll 1
+            for (int s0 = 0; s0 < w.nparts; s0 += PB) {
+              uint4 v[PB][NV];
 #pragma unroll
-              for (int j = 0; j < RCH; j += 4) {
-                const uint4 v = __ldcg(reinterpret_cast<const uint4 *>(src + j));
-                if constexpr (Elem<T>::is_int) {
-                  r[j] += v.x; r[j + 1] += v.y; r[j + 2] += v.z; r[j + 3] += v.w;
-                } else {
-                  r[j] = __float_as_uint(__uint_as_float(r[j]) + __uint_as_float(v.x));
-                  r[j + 1] = __float_as_uint(__uint_as_float(r[j + 1]) + __uint_as_float(v.y));
-                  r[j + 2] = __float_as_uint(__uint_as_float(r[j + 2]) + __uint_as_float(v.z));
-                  r[j + 3] = __float_as_uint(__uint_as_float(r[j + 3]) + __uint_as_float(v.w));
+              for (int b = 0; b < PB; ++b)
+#pragma unroll
+                for (int q = 0; q < NV; ++q)
+                  v[b][q] = (s0 + b < w.nparts) ? __ldcg(src + (int64_t)(s0 + b) * slot_vec + q * 32) : make_uint4(0, 0, 0, 0);
+              // summed in K order: partial s0, s0+1, ...
+#pragma unroll
+              for (int b = 0; b < PB; ++b) {
+                if (s0 + b >= w.nparts) break;
+#pragma unroll
+                for (int q = 0; q < NV; ++q) {
+                  const uint4 x = v[b][q];
+                  if constexpr (Elem<T>::is_int) {
+                    r[4 * q] += x.x; r[4 * q + 1] += x.y; r[4 * q + 2] += x.z; r[4 * q + 3] += x.w;
+                  } else {
+                    r[4 * q] = __float_as_uint(__uint_as_float(r[4 * q]) + __uint_as_float(x.x));
+                    r[4 * q + 1] = __float_as_uint(__uint_as_float(r[4 * q + 1]) + __uint_as_float(x.y));
+                    r[4 * q + 2] = __float_as_uint(__uint_as_float(r[4 * q + 2]) + __uint_as_float(x.z));
+                    r[4 * q + 3] = __float_as_uint(__uint_as_float(r[4 * q + 3]) + __uint_as_float(x.w));
+                  }
                 }
               }
             }

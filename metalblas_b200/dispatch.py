@@ -97,7 +97,7 @@ _BACKENDS = {None: _lib.MB_BACKEND_AUTO, "auto": _lib.MB_BACKEND_AUTO, "gemv": _
 
 
 def _launch(A, B, C, M, N, K, batch, a3, b3, c3, *, epilogue=None, backend=_lib.MB_BACKEND_AUTO,
-            tile_n=0, split_k=0, swap_ab=0, cta_pair=0, autotune=True):
+            tile_n=0, split_k=0, swap_ab=0, cta_pair=0, stream_k=0, autotune=True):
     """Fill an mb_gemm_desc and call mb_gemm on the current stream of C's device.
 
     a3/b3/c3 are (row stride, col stride, batch stride) in elements.
@@ -129,13 +129,15 @@ def _launch(A, B, C, M, N, K, batch, a3, b3, c3, *, epilogue=None, backend=_lib.
             d.alpha_re, d.alpha_im = float(complex(alpha).real), float(complex(alpha).imag)
             d.beta_re, d.beta_im = float(complex(beta).real), float(complex(beta).imag)
     d.tile_n, d.split_k, d.swap_ab, d.cta_pair = int(tile_n), int(split_k), int(swap_ab), int(cta_pair)
+    d.stream_k = int(stream_k)
     dev = C.device
     if torch.cuda.current_device() != dev.index:
         with torch.cuda.device(dev):
             return _launch(A, B, C, M, N, K, batch, a3, b3, c3, epilogue=epilogue, backend=backend,
-                           tile_n=tile_n, split_k=split_k, swap_ab=swap_ab, cta_pair=cta_pair, autotune=autotune)
+                           tile_n=tile_n, split_k=split_k, swap_ab=swap_ab, cta_pair=cta_pair, stream_k=stream_k,
+                           autotune=autotune)
     stream = torch.cuda.current_stream(dev).cuda_stream
-    if autotune and backend == _lib.MB_BACKEND_AUTO and not (tile_n or split_k or swap_ab or cta_pair):
+    if autotune and backend == _lib.MB_BACKEND_AUTO and not (tile_n or split_k or swap_ab or cta_pair or stream_k):
         choice = _plan.choose(d, A, B, C, stream)
         if choice is not None:
             d.backend, d.tile_n, d.split_k, d.swap_ab = choice

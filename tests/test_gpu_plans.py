@@ -25,17 +25,19 @@ SHAPES = [(128, 8192, 4096), (64, 2048, 8192), (256, 512, 16384), (4, 4096, 4096
 # (tile_n, split_k, swap_ab, cta_pair)
 VARIANTS = [(0, 0, 0, 0), (64, 1, -1, 1), (64, 4, -1, 0), (128, 2, -1, 0), (256, 4, -1, 0), (256, 8, -1, 0),
             (128, 3, -1, 0), (0, 0, 1, 0), (32, 4, 1, 0), (16, 2, 1, 0), (64, 1, 1, 0),
-            (256, 1, -1, 2), (128, 1, -1, 2), (256, 0, -1, 2)]
+            (256, 1, -1, 2), (128, 1, -1, 2), (256, 0, -1, 2),
+            # stream-K tail (forced), plain and swapped
+            (0, 0, -1, 0, 2), (64, 0, -1, 0, 2), (256, 0, -1, 0, 2), (16, 0, 1, 0, 2), (128, 0, 1, 0, 2)]
 
 
-def _run(a, b, tile_n, split, swap, pair=0, epilogue=None):
+def _run(a, b, tile_n, split, swap, pair=0, sk=0, epilogue=None):
     M, K = a.shape
     N = b.shape[1]
     c = torch.empty(M, N, dtype=a.dtype, device=a.device)
     try:
         dispatch._launch(a, b, c, M, N, K, 1, (a.stride(0), a.stride(1), 0), (b.stride(0), b.stride(1), 0),
                          (c.stride(0), c.stride(1), 0), epilogue=epilogue, backend=_lib.MB_BACKEND_TC,
-                         tile_n=tile_n, split_k=split, swap_ab=swap, cta_pair=pair, autotune=False)
+                         tile_n=tile_n, split_k=split, swap_ab=swap, cta_pair=pair, stream_k=sk, autotune=False)
     except NotImplementedError:
         return None  # this layout cannot take the forced variant (e.g. MN-major B with a narrow tile)
     return c
@@ -72,11 +74,42 @@ def test_split_k_epilogue_int8_wraps():
         ref = orc.fused(to_np(bias), to_np(a), to_np(b), 3, -7, "int8")
         ok, _ = orc.check(to_np(c), ref, "int8")
         assert ok, f"split={split}"
+    for bn in (64, 128):  # stream-K tail: 3..6 K-ordered partials per tile
+        c = _run(a, b, bn, 0, -1, sk=2, epilogue=(bias, (0, 1, 0), 3, -7, True, True))
+        ref = orc.fused(to_np(bias), to_np(a), to_np(b), 3, -7, "int8")
+        ok, _ = orc.check(to_np(c), ref, "int8")
+        assert ok, f"stream-K bn={bn}"
     for pair in (1, 2):
         c = _run(a, b, 256, 1, -1, pair=pair, epilogue=(bias, (0, 1, 0), 3, -7, True, True))
         ref = orc.fused(to_np(bias), to_np(a), to_np(b), 3, -7, "int8")
         ok, _ = orc.check(to_np(c), ref, "int8")
         assert ok, f"pair={pair}"
+
+
+def test_stream_k_many_parts_and_repeat():
+    """One tile cut into one piece per SM (its last piece sums ~148 partials),
+    run twice so the tickets must have been returned to zero, plus a batched
+    bf16 case with an alpha/beta epilogue."""
+    from metalblas_b200 import kernels
+    gen = torch.Generator().manual_seed(11)
+    a = rand((128, 65536), torch.bfloat16, gen)
+    b = rand((65536, 128), torch.bfloat16, gen)
+    ref = orc.product(to_np(a), to_np(b), "bfloat16")
+    for _ in range(2):
+        c = _run(a, b, 128, 0, -1, sk=2)
+        ok, err = orc.check(to_np(c), ref, "bfloat16")
+        assert ok, f"many parts err={err}"
+    A = rand((3, 200, 3000), torch.float16, gen)
+    B = rand((3, 3000, 72), torch.float16, gen)
+    bias = rand((3, 200, 72), torch.float16, gen)
+    C = torch.empty(3, 200, 72, dtype=torch.float16, device="cuda")
+    dispatch._launch(A, B, C, 200, 72, 3000, 3, (3000, 1, 200 * 3000), (72, 1, 3000 * 72), (72, 1, 200 * 72),
+                     epilogue=(bias, (72, 1, 200 * 72), 0.5, 2.0, True, True), backend=_lib.MB_BACKEND_TC,
+                     tile_n=32, stream_k=2, autotune=False)
+    fref = orc.fused(to_np(bias), to_np(A), to_np(B), 0.5, 2.0, "float16")
+    ok, err = orc.check(to_np(C), fref, "float16")
+    assert ok, f"batched stream-K baddbmm err={err}"
+    assert kernels.device_status() == 0
 
 
 def test_complex32_workspace_does_not_clobber_tickets():
