@@ -149,6 +149,44 @@ int64_t mb_gemm_workspace_size(const mb_gemm_desc *d);
  * tile that _gemm_plan returns). Returns the string length written. */
 int mb_plan_query(const mb_gemm_desc *d, char *buf, int buflen);
 
+/* y = op(W) x for a unit-stride matrix W (rows x cols, element (r, c) at
+ * W[r*ldw + c]): trans == 0 gives y[r] = sum_c W(r,c) x[c] (rows outputs),
+ * trans == 1 gives y[c] = sum_r W(r,c) x[r] (cols outputs).  x and y are
+ * strided by incx / incy elements; y has W's dtype.  Replaces the GEMV routing
+ * of _dispatch_gemv (metalblas/dispatch.py:49-70) onto the gemv_t / gemv_nt
+ * kernels (metalblas/shaders/gemv_t.h:15-99, gemv_nt.h:16-101) and the
+ * integer / complex GEMVs (metalblas/integer_dispatch.py:92-105,
+ * complex_dispatch.py:33-66).  A workspace (size from mb_gemm_workspace_size
+ * of the equivalent mb_gemm descriptor) lets long reductions split across
+ * CTAs; with workspace == NULL the reduction stays in one CTA per output
+ * block. */
+int mb_gemv(int32_t dtype, int32_t trans, int64_t rows, int64_t cols, const void *W, int64_t ldw,
+            const void *x, int64_t incx, void *y, int64_t incy, void *workspace, int64_t workspace_bytes,
+            void *stream);
+
+/* Per-shape plan overrides: the autotune cache, kept in the library so that
+ * every caller of mb_gemm gets tuned plans.  The reference caches autotune
+ * winners in module dicts keyed by shape (metalblas/float_dispatch.py:154,
+ * 484-505, 977-1045); here the key is the device name, dtype, M, N, K, batch,
+ * broadcast flags, layout/alignment class and epilogue flag of a descriptor.
+ * mb_gemm consults the table only for descriptors with backend AUTO and no
+ * plan override of their own.  keep == 1 records "tuned: the tile table's
+ * choice stands".  All functions are thread-safe. */
+typedef struct mb_plan_override {
+    int32_t keep;
+    int32_t backend, tile_n, split_k, swap_ab, cta_pair, stream_k;
+} mb_plan_override;
+int mb_autotune_record(const mb_gemm_desc *d, const mb_plan_override *ov);
+/* 1 and *ov filled on a hit, 0 on a miss, negative mb_status on error. */
+int mb_autotune_lookup(const mb_gemm_desc *d, mb_plan_override *ov);
+/* Text file, one entry per line; save writes `path` atomically (via a
+ * temporary file).  load replaces nothing on a missing or malformed file
+ * (returns MB_ERR_INVALID) and otherwise merges the file's entries. */
+int mb_autotune_cache_load(const char *path);
+int mb_autotune_cache_save(const char *path);
+void mb_autotune_cache_clear(void);
+int64_t mb_autotune_cache_size(void);
+
 /* Text of the last error raised on this thread. */
 const char *mb_last_error_string(void);
 

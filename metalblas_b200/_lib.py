@@ -35,7 +35,9 @@ DTYPE_CODE = {
 EXPORTS = (
     "mb_gemm_desc_init", "mb_gemm", "mb_gemm_noalloc", "mb_gemm_workspace_size", "mb_plan_query",
     "mb_last_error_string", "mb_device_status", "mb_device_status_clear",
-    "mb_debug_wait_timeout", "mb_abi_version", "mb_built_sm",
+    "mb_debug_wait_timeout", "mb_abi_version", "mb_built_sm", "mb_gemv",
+    "mb_autotune_record", "mb_autotune_lookup", "mb_autotune_cache_load", "mb_autotune_cache_save",
+    "mb_autotune_cache_clear", "mb_autotune_cache_size",
 )
 
 
@@ -61,6 +63,13 @@ class GemmDesc(ctypes.Structure):
         ("cta_pair", ctypes.c_int32),
         ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_int64),
     ]
+
+
+class PlanOverride(ctypes.Structure):
+    """Mirror of ``mb_plan_override``."""
+
+    _fields_ = [(n, ctypes.c_int32) for n in
+                ("keep", "backend", "tile_n", "split_k", "swap_ab", "cta_pair", "stream_k")]
 
 
 _lib = None
@@ -102,6 +111,22 @@ def load():
         lib.mb_abi_version.restype = ctypes.c_int
         lib.mb_built_sm.argtypes = []
         lib.mb_built_sm.restype = ctypes.c_int
+        V, I64, I32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32
+        lib.mb_gemv.argtypes = [I32, I32, I64, I64, V, I64, V, I64, V, I64, V, I64, V]
+        lib.mb_gemv.restype = ctypes.c_int
+        PO = ctypes.POINTER(PlanOverride)
+        lib.mb_autotune_record.argtypes = [P, PO]
+        lib.mb_autotune_record.restype = ctypes.c_int
+        lib.mb_autotune_lookup.argtypes = [P, PO]
+        lib.mb_autotune_lookup.restype = ctypes.c_int
+        lib.mb_autotune_cache_load.argtypes = [ctypes.c_char_p]
+        lib.mb_autotune_cache_load.restype = ctypes.c_int
+        lib.mb_autotune_cache_save.argtypes = [ctypes.c_char_p]
+        lib.mb_autotune_cache_save.restype = ctypes.c_int
+        lib.mb_autotune_cache_clear.argtypes = []
+        lib.mb_autotune_cache_clear.restype = None
+        lib.mb_autotune_cache_size.argtypes = []
+        lib.mb_autotune_cache_size.restype = ctypes.c_int64
         _lib = lib
         return lib
 
@@ -144,3 +169,28 @@ def device_status() -> int:
 
 def device_status_clear() -> None:
     load().mb_device_status_clear()
+
+
+def autotune_lookup(d: GemmDesc):
+    """The library's cached plan override for d's shape: None on a miss, "keep"
+    when tuning kept the tile table's choice, else (backend, tile_n, split_k,
+    swap_ab)."""
+    ov = PlanOverride()
+    rc = load().mb_autotune_lookup(ctypes.byref(d), ctypes.byref(ov))
+    if rc < 0:
+        raise_for(-rc, "mb_autotune_lookup")
+    if rc == 0:
+        return None
+    if ov.keep:
+        return "keep"
+    return (ov.backend, ov.tile_n, ov.split_k, ov.swap_ab)
+
+
+def autotune_record(d: GemmDesc, choice) -> None:
+    """Record choice (None = keep the table's plan) for d's shape."""
+    ov = PlanOverride()
+    if choice is None:
+        ov.keep = 1
+    else:
+        ov.backend, ov.tile_n, ov.split_k, ov.swap_ab = (int(x) for x in choice)
+    raise_for(load().mb_autotune_record(ctypes.byref(d), ctypes.byref(ov)), "mb_autotune_record")

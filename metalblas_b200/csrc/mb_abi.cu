@@ -25,8 +25,10 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 #include <string>
+#include <unordered_map>
 
 #include "../../include/metalblas_b200.h"
 #include "mb_common.cuh"
@@ -79,6 +81,7 @@ bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 
 struct DevInfo {
   int sms = 148;
   bool ok = false;
+  char name[128] = {0};
 };
 DevInfo g_dev[64];
 std::mutex g_dev_mu;
@@ -92,9 +95,49 @@ int num_sms(int dev) {
   if (!g_dev[dev].ok) {
     int n = 0;
     if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && n > 0) g_dev[dev].sms = n;
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, dev) == cudaSuccess) {
+      snprintf(g_dev[dev].name, sizeof(g_dev[dev].name), "%s", prop.name);
+      for (char *c = g_dev[dev].name; *c; ++c)
+        if (*c == '\t' || *c == '\n' || *c == '|') *c = ' ';
+    }
     g_dev[dev].ok = true;
   }
   return g_dev[dev].sms;
+}
+// Device name for autotune keys ("none" without a device).
+std::string device_name() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    cudaGetLastError();
+    return "none";
+  }
+  num_sms(dev);
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  return g_dev[dev].name[0] ? std::string(g_dev[dev].name) : std::string("unknown");
+}
+
+// ------------------------------------------------------------ autotune cache
+struct Override {
+  int keep, backend, tile_n, split_k, swap_ab, cta_pair, stream_k;
+};
+std::mutex g_tune_mu;
+std::unordered_map<std::string, Override> g_tune;
+std::atomic<int64_t> g_tune_size{0};
+
+std::string tune_key(const mb_gemm_desc *d) {
+  char buf[512];
+  const std::string name = device_name();
+  auto m8 = [](int64_t v) { return (long long)(((v % 8) + 8) % 8); };
+  snprintf(buf, sizeof(buf), "%s|%d|%lld|%lld|%lld|%lld|%d%d|%d%d%d|%lld%lld%lld%lld|%d%d%d|%d", name.c_str(),
+           d->dtype, (long long)d->M, (long long)d->N, (long long)d->K, (long long)d->batch, d->sA == 0, d->sB == 0,
+           d->a_rs == 1, d->b_rs == 1, d->c_cs == 1, m8(d->a_rs), m8(d->a_cs), m8(d->b_rs), m8(d->b_cs),
+           aligned16(d->A), aligned16(d->B), aligned16(d->C), d->epilogue);
+  return buf;
+}
+
+bool has_overrides(const mb_gemm_desc *d) {
+  return d->backend != MB_BACKEND_AUTO || d->tile_n || d->split_k || d->swap_ab || d->cta_pair || d->stream_k;
 }
 
 unsigned long long wait_timeout_ns() {
@@ -847,8 +890,26 @@ int plan_for(const mb_gemm_desc *d, Plan &pl, Op &o, int &sms, bool query = fals
   rc = current_device(&dev);
   if (rc && !query) return rc;
   sms = rc ? 148 : num_sms(dev);
+  if (rc) cudaGetLastError();
   o = make_op(d);
   const bool have_ws = d->workspace != nullptr || d->workspace_bytes < 0;  // <0: size query
+  if (g_tune_size.load(std::memory_order_relaxed) > 0 && !has_overrides(d)) {
+    Override ov{};
+    bool hit = false;
+    {
+      const std::string key = tune_key(d);
+      std::lock_guard<std::mutex> lk(g_tune_mu);
+      auto it = g_tune.find(key);
+      if (it != g_tune.end()) { ov = it->second; hit = true; }
+    }
+    if (hit && !ov.keep) {
+      mb_gemm_desc q = *d;
+      q.backend = ov.backend; q.tile_n = ov.tile_n; q.split_k = ov.split_k; q.swap_ab = ov.swap_ab;
+      q.cta_pair = ov.cta_pair; q.stream_k = ov.stream_k;
+      if (validate(&q) == MB_OK && make_plan(&q, o, sms, have_ws, pl) == MB_OK) return MB_OK;
+      pl = Plan{};  // a stale entry that no longer plans: fall back to the table
+    }
+  }
   return make_plan(d, o, sms, have_ws, pl);
 }
 
@@ -930,6 +991,109 @@ int mb_gemm(const mb_gemm_desc *d, void *stream) {
     }
   });
 }
+
+int mb_gemv(int32_t dtype, int32_t trans, int64_t rows, int64_t cols, const void *W, int64_t ldw, const void *x,
+            int64_t incx, void *y, int64_t incy, void *workspace, int64_t workspace_bytes, void *stream) {
+  if (rows < 0 || cols < 0) return fail(MB_ERR_INVALID, "negative extent");
+  if (trans != 0 && trans != 1) return fail(MB_ERR_INVALID, "trans must be 0 or 1");
+  if (ldw < std::max<int64_t>(cols, 1)) return fail(MB_ERR_INVALID, "ldw %lld < cols %lld", (long long)ldw, (long long)cols);
+  mb_gemm_desc d;
+  mb_gemm_desc_init(&d);
+  d.dtype = dtype;
+  d.backend = MB_BACKEND_GEMV;
+  d.A = nullptr; d.B = nullptr; d.C = y;
+  if (trans == 0) {
+    // y (rows x 1) = W (rows x cols) @ x (cols x 1)
+    d.M = rows; d.N = 1; d.K = cols;
+    d.A = W; d.a_rs = ldw; d.a_cs = 1;
+    d.B = x; d.b_rs = incx; d.b_cs = 1;
+    d.c_rs = incy; d.c_cs = 1;
+  } else {
+    // y (1 x cols) = x (1 x rows) @ W (rows x cols)
+    d.M = 1; d.N = cols; d.K = rows;
+    d.A = x; d.a_rs = 1; d.a_cs = incx;
+    d.B = W; d.b_rs = ldw; d.b_cs = 1;
+    d.c_rs = 1; d.c_cs = incy;
+  }
+  d.workspace = workspace;
+  d.workspace_bytes = workspace ? workspace_bytes : 0;
+  if (!workspace) d.split_k = 1;
+  return mb_gemm(&d, stream);
+}
+
+int mb_autotune_record(const mb_gemm_desc *d, const mb_plan_override *ov) {
+  if (!d || !ov) return fail(MB_ERR_INVALID, "null argument");
+  const std::string key = tune_key(d);
+  std::lock_guard<std::mutex> lk(g_tune_mu);
+  g_tune[key] = Override{ov->keep ? 1 : 0, ov->backend, ov->tile_n, ov->split_k, ov->swap_ab, ov->cta_pair,
+                         ov->stream_k};
+  g_tune_size.store((int64_t)g_tune.size());
+  return MB_OK;
+}
+
+int mb_autotune_lookup(const mb_gemm_desc *d, mb_plan_override *ov) {
+  if (!d || !ov) return -fail(MB_ERR_INVALID, "null argument");
+  const std::string key = tune_key(d);
+  std::lock_guard<std::mutex> lk(g_tune_mu);
+  auto it = g_tune.find(key);
+  if (it == g_tune.end()) return 0;
+  const Override &o = it->second;
+  ov->keep = o.keep; ov->backend = o.backend; ov->tile_n = o.tile_n; ov->split_k = o.split_k;
+  ov->swap_ab = o.swap_ab; ov->cta_pair = o.cta_pair; ov->stream_k = o.stream_k;
+  return 1;
+}
+
+static const char kTuneHeader[] = "metalblas_b200 autotune v1";
+
+int mb_autotune_cache_load(const char *path) {
+  if (!path) return fail(MB_ERR_INVALID, "null path");
+  FILE *f = fopen(path, "r");
+  if (!f) return fail(MB_ERR_INVALID, "cannot open %s", path);
+  std::unordered_map<std::string, Override> add;
+  char line[1024];
+  bool ok = fgets(line, sizeof(line), f) && strncmp(line, kTuneHeader, sizeof(kTuneHeader) - 1) == 0;
+  while (ok && fgets(line, sizeof(line), f)) {
+    char *tab = strchr(line, '\t');
+    if (!tab) { ok = line[0] == '\n' || line[0] == 0; continue; }
+    *tab = 0;
+    Override o{};
+    if (sscanf(tab + 1, "%d %d %d %d %d %d %d", &o.keep, &o.backend, &o.tile_n, &o.split_k, &o.swap_ab, &o.cta_pair,
+               &o.stream_k) != 7) { ok = false; break; }
+    add[line] = o;
+  }
+  fclose(f);
+  if (!ok) return fail(MB_ERR_INVALID, "malformed autotune cache %s", path);
+  std::lock_guard<std::mutex> lk(g_tune_mu);
+  for (auto &kv : add) g_tune[kv.first] = kv.second;
+  g_tune_size.store((int64_t)g_tune.size());
+  return MB_OK;
+}
+
+int mb_autotune_cache_save(const char *path) {
+  if (!path) return fail(MB_ERR_INVALID, "null path");
+  const std::string tmp = std::string(path) + ".tmp";
+  FILE *f = fopen(tmp.c_str(), "w");
+  if (!f) return fail(MB_ERR_INVALID, "cannot write %s", tmp.c_str());
+  fprintf(f, "%s\n", kTuneHeader);
+  {
+    std::lock_guard<std::mutex> lk(g_tune_mu);
+    for (auto &kv : g_tune) {
+      const Override &o = kv.second;
+      fprintf(f, "%s\t%d %d %d %d %d %d %d\n", kv.first.c_str(), o.keep, o.backend, o.tile_n, o.split_k, o.swap_ab,
+              o.cta_pair, o.stream_k);
+    }
+  }
+  if (fclose(f) != 0 || rename(tmp.c_str(), path) != 0) return fail(MB_ERR_INVALID, "cannot write %s", path);
+  return MB_OK;
+}
+
+void mb_autotune_cache_clear(void) {
+  std::lock_guard<std::mutex> lk(g_tune_mu);
+  g_tune.clear();
+  g_tune_size.store(0);
+}
+
+int64_t mb_autotune_cache_size(void) { return g_tune_size.load(); }
 
 }  // extern "C"
 

@@ -11,15 +11,16 @@ This module keeps the reference's autotuning contract on top of it
   tall/narrow shapes) — ``_fastest``, metalblas/float_dispatch.py:421-436;
 * a rival is accepted only if it agrees with the primary within
   0.02 * max|ref| (bit-exact for integers) — metalblas/float_dispatch.py:464-468;
-* results are cached per shape; with ``METALBLAS_AUTOTUNE_CACHE=<file.json>``
-  the cache persists across processes, keyed by GPU name, dtype, M, N, K,
-  batch, layout and alignment class.  A missing or unreadable file means
-  re-tune.
+* results are cached per shape in the library's table (mb_autotune_record /
+  mb_autotune_lookup, so C callers of mb_gemm get the tuned plans too), keyed
+  by GPU name, dtype, M, N, K, batch, broadcast flags, layout and alignment
+  class and epilogue flag; with ``METALBLAS_AUTOTUNE_CACHE=<file>`` the table
+  persists across processes (mb_autotune_cache_load / _save).  A missing or
+  unreadable file means re-tune.
 """
 from __future__ import annotations
 
 import ctypes
-import json
 import os
 import threading
 
@@ -33,7 +34,6 @@ TALL_NARROW_MARGIN = 0.01
 MIN_FLOPS = 4e9          # below this the table's choice stands (launch-bound)
 _TC_CODES = (_lib.MB_BF16, _lib.MB_F16, _lib.MB_I8, _lib.MB_U8)
 
-_cache: dict = {}
 _lock = threading.Lock()
 _loaded = False
 
@@ -43,39 +43,21 @@ def _cache_path():
 
 
 def _load_cache():
+    """Merge the cache file into the library's table once per process; a
+    missing or unreadable file means re-tune."""
     global _loaded
     if _loaded:
         return
     _loaded = True
     path = _cache_path()
-    if not path or not os.path.exists(path):
-        return
-    try:
-        with open(path) as f:
-            data = json.load(f)
-        for k, v in data.items():
-            _cache[k] = tuple(v) if v is not None else None
-    except (OSError, ValueError):
-        _cache.clear()
+    if path and os.path.exists(path):
+        _lib.load().mb_autotune_cache_load(path.encode())
 
 
 def _save_cache():
     path = _cache_path()
-    if not path:
-        return
-    tmp = path + ".tmp"
-    try:
-        with open(tmp, "w") as f:
-            json.dump(_cache, f, indent=0, sort_keys=True)
-        os.replace(tmp, path)
-    except OSError:
-        pass
-
-
-def _key(d, dev) -> str:
-    align = (d.a_rs == 1, d.b_rs == 1, d.c_cs == 1, d.a_rs % 8, d.a_cs % 8, d.b_rs % 8, d.b_cs % 8)
-    return "|".join(map(str, (torch.cuda.get_device_name(dev), d.dtype, d.M, d.N, d.K, d.batch,
-                              d.sA == 0, d.sB == 0, align, d.epilogue)))
+    if path:
+        _lib.load().mb_autotune_cache_save(path.encode())
 
 
 def _candidates(primary: str, d):
@@ -199,19 +181,19 @@ def choose(d, A, B, C, stream):
         return None
     if torch.cuda.is_current_stream_capturing():
         return None
-    dev = C.device
-    key = _key(d, dev)
     with _lock:
         _load_cache()
-        if key in _cache:
-            return _cache[key]
+        hit = _lib.autotune_lookup(d)
+    if hit is not None:
+        return None if hit == "keep" else hit
     choice = _tune(d, C, stream)
     with _lock:
-        _cache[key] = choice
+        _lib.autotune_record(d, choice)
         _save_cache()
     return choice
 
 
 def clear():
+    """Forget every tuned shape (the library's table)."""
     with _lock:
-        _cache.clear()
+        _lib.load().mb_autotune_cache_clear()
