@@ -201,6 +201,14 @@ void mb_device_status_clear(void);
  * kernel must give up, record MB_ERR_DEVICE_TIMEOUT and return. */
 int mb_debug_wait_timeout(int64_t limit_us, void *stream);
 
+/* Measured CUDA-core multiply-add throughput of the current device, in 1e12
+ * operations per second (a multiply-add counts 2, as in 2*M*N*K): kind 0 fp32
+ * FFMA, 1 int32 IMAD, 2 int64 multiply-add.  These are the roofline
+ * denominators of the CUDA-core GEMM (complex64/fp32, int16/int32, int64),
+ * for which no published B200 figure exists; the reference has no
+ * counterpart.  Runs for about 20 ms and synchronises its own stream. */
+int mb_peak_probe(int32_t kind, double *tops);
+
 /* Library ABI version (MB_ABI_VERSION) and the SM arch it was built for (100). */
 int mb_abi_version(void);
 int mb_built_sm(void);

@@ -37,7 +37,7 @@ EXPORTS = (
     "mb_last_error_string", "mb_device_status", "mb_device_status_clear",
     "mb_debug_wait_timeout", "mb_abi_version", "mb_built_sm", "mb_gemv",
     "mb_autotune_record", "mb_autotune_lookup", "mb_autotune_cache_load", "mb_autotune_cache_save",
-    "mb_autotune_cache_clear", "mb_autotune_cache_size",
+    "mb_autotune_cache_clear", "mb_autotune_cache_size", "mb_peak_probe",
 )
 
 
@@ -127,6 +127,8 @@ def load():
         lib.mb_autotune_cache_clear.restype = None
         lib.mb_autotune_cache_size.argtypes = []
         lib.mb_autotune_cache_size.restype = ctypes.c_int64
+        lib.mb_peak_probe.argtypes = [I32, ctypes.POINTER(ctypes.c_double)]
+        lib.mb_peak_probe.restype = ctypes.c_int
         _lib = lib
         return lib
 
@@ -194,3 +196,10 @@ def autotune_record(d: GemmDesc, choice) -> None:
     else:
         ov.backend, ov.tile_n, ov.split_k, ov.swap_ab = (int(x) for x in choice)
     raise_for(load().mb_autotune_record(ctypes.byref(d), ctypes.byref(ov)), "mb_autotune_record")
+
+
+def peak_probe(kind: int) -> float:
+    """Measured CUDA-core multiply-add rate in 1e12 ops/s (0 fp32, 1 int32, 2 int64)."""
+    v = ctypes.c_double()
+    raise_for(load().mb_peak_probe(int(kind), ctypes.byref(v)), "mb_peak_probe")
+    return v.value

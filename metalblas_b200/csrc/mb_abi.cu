@@ -36,6 +36,7 @@
 #include "gemv.cuh"
 #include "tc_gemm.cuh"
 #include "c32.cuh"
+#include "peaks.cuh"
 
 using namespace mb;
 
@@ -1209,6 +1210,53 @@ int mb_debug_wait_timeout(int64_t limit_us, void *stream) {
   if (limit_us <= 0 || limit_us > 10000000) return fail(MB_ERR_INVALID, "limit_us out of range");
   tc::wait_timeout_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>((unsigned long long)limit_us * 1000ull);
   return cuda_check(cudaGetLastError(), "wait_timeout launch");
+}
+
+int mb_peak_probe(int32_t kind, double *tops) {
+  if (!tops) return fail(MB_ERR_INVALID, "null output");
+  if (kind < 0 || kind > 2) return fail(MB_ERR_INVALID, "probe kind must be 0 (fp32), 1 (int32) or 2 (int64)");
+  int dev = 0;
+  int rc = current_device(&dev);
+  if (rc) return rc;
+  const int sms = num_sms(dev);
+  const dim3 grid((unsigned)(4 * sms)), block(256);
+  void *out = nullptr;
+  rc = cuda_check(cudaMalloc(&out, (size_t)grid.x * block.x * 8), "probe buffer");
+  if (rc) return rc;
+  cudaStream_t st = nullptr;
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  float ms = 0.f;
+  long long iters = 4096;
+  auto launch = [&](long long n) {
+    if (kind == 0) peak_mad_kernel<float><<<grid, block, 0, st>>>((float *)out, 1.0001f, n);
+    else if (kind == 1) peak_mad_kernel<uint32_t><<<grid, block, 0, st>>>((uint32_t *)out, 3u, n);
+    else peak_mad_kernel<unsigned long long><<<grid, block, 0, st>>>((unsigned long long *)out, 3ull, n);
+  };
+  rc = cuda_check(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking), "probe stream");
+  if (!rc) rc = cuda_check(cudaEventCreate(&e0), "probe event");
+  if (!rc) rc = cuda_check(cudaEventCreate(&e1), "probe event");
+  if (!rc) {
+    launch(64);  // warm-up
+    // grow the step count until one launch takes at least 20 ms
+    for (int tries = 0; tries < 8 && !rc; ++tries) {
+      cudaEventRecord(e0, st);
+      launch(iters);
+      cudaEventRecord(e1, st);
+      rc = cuda_check(cudaEventSynchronize(e1), "probe run");
+      if (!rc) rc = cuda_check(cudaEventElapsedTime(&ms, e0, e1), "probe timing");
+      if (rc || ms >= 20.f) break;
+      iters *= 4;
+    }
+  }
+  if (!rc) rc = cuda_check(cudaGetLastError(), "probe launch");
+  if (e0) cudaEventDestroy(e0);
+  if (e1) cudaEventDestroy(e1);
+  if (st) cudaStreamDestroy(st);
+  cudaFree(out);
+  if (rc) return rc;
+  const double ops = 2.0 * kPeakChains * 16.0 * (double)iters * grid.x * block.x;
+  *tops = ops / (ms * 1e-3) / 1e12;
+  return MB_OK;
 }
 
 int mb_abi_version(void) { return MB_ABI_VERSION; }

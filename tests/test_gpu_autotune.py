@@ -85,3 +85,15 @@ def test_mb_gemv_both_orientations(dtype):
                 ok, err = orc.check(to_np(y), ref, NAME[dtype])
                 assert ok, f"trans={trans} inc={inc} ws={w is not None} err={err}"
                 assert not to_np(ybuf[1::2]).any(), "wrote between strided outputs"
+
+
+def test_peak_probe_rates_are_plausible():
+    """The CUDA-core roofline denominators: B200 fp32 FFMA is 148 SMs x 128
+    lanes x 2 ops x ~1.9 GHz ~ 72e12 op/s nominal; IMAD and the emulated int64
+    multiply-add are slower."""
+    f32 = _lib.peak_probe(0)
+    i32 = _lib.peak_probe(1)
+    i64 = _lib.peak_probe(2)
+    assert 30.0 < f32 < 120.0, f32
+    assert 5.0 < i32 <= f32 * 1.05, i32
+    assert 0.5 < i64 < i32, i64
