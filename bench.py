@@ -357,6 +357,413 @@ def run_reference(args, w, rank, world):
     }
 
 
+# --------------------------------------------------------------------------- suite
+# `bench.py --suite`: every BASELINE.json config (C1-C5) on one GPU, one JSON
+# line per case: the value, its roofline fraction against the bound that
+# applies (dense tensor peak, CUDA-core multiply-add peak measured by
+# mb_peak_probe, or HBM), an oracle check on a row or column sample, and where
+# stated a host-CPU torch timing of a bounded sample of the same product.
+L2_BYTES = 126 * 2 ** 20
+
+
+def _suite_time(fn, nsets, min_ms=150.0, max_iters=2000):
+    """Average device time of fn(i) (i cycles over nsets input sets), CUDA
+    events on the current stream after 3 warm-up calls."""
+    for i in range(3):
+        fn(i % nsets)
+    torch.cuda.synchronize()
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    fn(0)
+    e1.record(s)
+    e1.synchronize()
+    one = max(e0.elapsed_time(e1), 1e-3)
+    n = int(max(5, min(max_iters, min_ms / one)))
+    e0.record(s)
+    for i in range(n):
+        fn(i % nsets)
+    e1.record(s)
+    e1.synchronize()
+    return e0.elapsed_time(e1) / n
+
+
+def _nsets(bytes_per_set, cap=32):
+    """Input sets to rotate so that one pass over them exceeds 2 x L2."""
+    return int(max(1, min(cap, -(-int(2.2 * L2_BYTES) // max(1, int(bytes_per_set))))))
+
+
+def _copies(t, n):
+    return [t] + [t.clone() for _ in range(n - 1)]
+
+
+def _int_range(dt):
+    info = torch.iinfo(dt)
+    return info.min, info.max + 1
+
+
+def _cpu_rows(fn_rows, rows_total, seconds=1.0):
+    """Host time of a bounded row sample: fn_rows(r) computes the first r rows.
+    Returns (seconds per call, rows)."""
+    r = max(1, min(rows_total, 16))
+    t0 = time.perf_counter()
+    fn_rows(r)
+    t = max(time.perf_counter() - t0, 1e-6)
+    r = int(max(1, min(rows_total, r * seconds / t)))
+    fn_rows(r)
+    t0 = time.perf_counter()
+    fn_rows(r)
+    return time.perf_counter() - t0, r
+
+
+class _Suite:
+    def __init__(self, args):
+        import metalblas_b200 as mb
+        from metalblas_b200 import _lib
+        from oracle import oracle as orc
+        self.mb, self.lib, self.orc = mb, _lib, orc
+        self.args = args
+        self.dev = torch.device("cuda", 0)
+        self.bf16_peak, self.hbm, self.peak_src = _peaks()
+        self.ffma = _lib.peak_probe(0)
+        self.imad = _lib.peak_probe(1)
+        self.imad64 = _lib.peak_probe(2)
+        self.int8_peak = self._int8_peak()
+        self.threads = torch.get_num_threads()
+        self.emit({"suite": "peaks", "bf16_dense_tflops": self.bf16_peak, "bf16_source": self.peak_src,
+                   "hbm_gbs": self.hbm, "int8_dense_tops_cublaslt": self.int8_peak,
+                   "ffma_tflops_probe": self.ffma, "imad32_tops_probe": self.imad,
+                   "mad64_tops_probe": self.imad64, "host_threads": self.threads,
+                   "gpu": torch.cuda.get_device_name(0)})
+
+    @staticmethod
+    def emit(d):
+        print(json.dumps(d), flush=True)
+
+    def _int8_peak(self):
+        """Dense int8 rate of cuBLASLt (torch._int_mm, 8192^3, best of 5): the
+        measured counterpart of MEASURED_PEAKS.json's bf16 figure."""
+        try:
+            a = torch.randint(-128, 128, (8192, 8192), dtype=torch.int8, device=self.dev)
+            b = torch.randint(-128, 128, (8192, 8192), dtype=torch.int8, device=self.dev)
+            best = min(_suite_time(lambda i: torch._int_mm(a, b), 1, min_ms=50) for _ in range(5))
+            return 2.0 * 8192 ** 3 / (best * 1e-3) / 1e12
+        except RuntimeError:
+            return 4500.0
+
+    def check_rows(self, got, a_h, b_h, name, rows=64, bias=None, beta=None, alpha=None):
+        """Oracle on a sample of output rows (2-D product a_h @ b_h)."""
+        orc = self.orc
+        M = a_h.shape[0]
+        idx = torch.arange(0, M, max(1, M // rows))
+        a_s = _to_np(a_h[idx])
+        ref = (orc.product(a_s, _to_np(b_h), name) if bias is None else
+               orc.fused(_to_np(bias)[idx] if bias.dim() == 2 else _to_np(bias), a_s, _to_np(b_h), beta, alpha, name))
+        ok, err = orc.check(_to_np(got[idx.to(got.device)]), ref, name)
+        return {"ok": bool(ok), "err": float(err), "rows": int(len(idx))}
+
+    # ------------------------------------------------------------------ GEMM
+    def gemm_case(self, suite, case, a_h, b_h, name, peak, peak_name, *, bias_h=None, beta=1.0, alpha=1.0,
+                  a_view=None, b_view=None, make_a=None, flops_mult=2.0, cpu=True, check_name=None):
+        """a_h/b_h: logical host operands (what the product means; a_h may be a
+        conj or transposed view); a_view / b_view map a device copy of the
+        logical operand to the tested layout; make_a builds the device A
+        operand directly (for conj / transposed storage)."""
+        mb = self.mb
+        dt = a_h.dtype
+        M, K = a_h.shape
+        N = b_h.shape[1]
+        set_bytes = (M * K + K * N + M * N) * a_h.element_size()
+        n = _nsets(set_bytes, cap=8)
+        if make_a is None:
+            make_a = lambda: (a_view(a_h.to(self.dev)) if a_view else a_h.to(self.dev))
+        make_b = lambda: (b_view(b_h.to(self.dev)) if b_view else b_h.to(self.dev))
+        As = [make_a() for _ in range(n)]
+        Bs = [make_b() for _ in range(n)]
+        Cs = [torch.empty(M, N, dtype=dt, device=self.dev) for _ in range(n)]
+        bias = bias_h.to(self.dev) if bias_h is not None else None
+        if bias is None:
+            fn = lambda i: mb.matmul(As[i], Bs[i], out=Cs[i])
+        else:
+            fn = lambda i: mb.addmm(bias, As[i], Bs[i], beta=beta, alpha=alpha, out=Cs[i])
+        ms = _suite_time(fn, n)
+        fn(0)
+        torch.cuda.synchronize()
+        flops = flops_mult * M * N * K
+        value = flops / (ms * 1e-3) / 1e12
+        chk = self.check_rows(Cs[0], a_h, b_h, check_name or {torch.bfloat16: "bfloat16"}.get(dt, str(dt)[6:]),
+                              bias=bias_h, beta=beta, alpha=alpha)
+        line = {"suite": suite, "case": case, "metric": "TFLOP/s" if dt.is_floating_point or dt.is_complex else "TOPS",
+                "value": value, "ms": ms, "roofline": {"bound": peak_name, "peak": peak, "frac": value / peak},
+                "check": chk, "plan": mb.kernels.plan(As[0], Bs[0]), "l2": f"{n} rotating input sets"}
+        if cpu:
+            line["cpu"] = self.cpu_gemm(a_h, b_h, flops_mult)
+        self.emit(line)
+
+    def cpu_gemm(self, a_h, b_h, flops_mult=2.0):
+        a, b = a_h, b_h
+        label = ""
+        if a.dtype is torch.complex32:
+            a, b = a.to(torch.complex64), b.to(torch.complex64)
+            label = " (complex64 upcast: CPU has no complex32 matmul)"
+        N, K = b.shape[1], b.shape[0]
+        sec, rows = _cpu_rows(lambda r: torch.matmul(a[:r].contiguous(), b), a.shape[0], self.args.cpu_seconds)
+        v = flops_mult * rows * N * K / sec / 1e12
+        return {"value": v, "unit": "TFLOP/s" if a.dtype.is_floating_point or a.dtype.is_complex else "TOPS",
+                "cores": self.threads, "kind": "port", "sample": f"host torch.matmul A[:{rows}] @ B{label}"}
+
+    # ------------------------------------------------------------------ suites
+    def c1(self):
+        g = torch.Generator().manual_seed(0)
+        a = torch.randn(2048, 4096, generator=g).to(torch.bfloat16)
+        b = torch.randn(4096, 2048, generator=g).to(torch.bfloat16)
+        bias = torch.randn(2048, generator=g).to(torch.bfloat16)
+        self.gemm_case("C1", "bf16 matmul A[2048,4096]@B[4096,2048]", a, b, "bfloat16", self.bf16_peak,
+                       "tensor bf16 dense")
+        self.gemm_case("C1", "bf16 addmm bias[2048] beta=0.5 alpha=2", a, b, "bfloat16", self.bf16_peak,
+                       "tensor bf16 dense", bias_h=bias, beta=0.5, alpha=2.0, cpu=False)
+        g = torch.Generator().manual_seed(0)
+        a = torch.randn(4096, 4096, generator=g).to(torch.bfloat16)
+        b = torch.randn(4096, 4096, generator=g).to(torch.bfloat16)
+        self.gemm_case("headline", "bf16 4096^3", a, b, "bfloat16", self.bf16_peak, "tensor bf16 dense")
+
+    def c2(self):
+        """GEMV / thin-matrix sweep: bytes 2(KN + MK + MN) against HBM."""
+        mb, orc = self.mb, self.orc
+        for K in (4096, 8192, 16384):
+            for N in (4096, 14336, 28672):
+                g = torch.Generator().manual_seed(1)
+                w32 = torch.randn(K, N, generator=g) * 0.02
+                xs32 = {M: torch.randn(M, K, generator=g) for M in (1, 4, 16)}
+                cols = torch.randperm(N, generator=g)[:256].sort().values
+                for dt, name in ((torch.bfloat16, "bfloat16"), (torch.float16, "float16")):
+                    w_h = w32.to(dt)
+                    W = w_h.to(self.dev)
+                    Wt = W.t().contiguous()   # [N, K] storage, used as its transpose
+                    nW = _nsets(W.numel() * W.element_size(), cap=16)
+                    for layout in ("x@W", "x@Wt"):
+                        base = W if layout == "x@W" else Wt.t()
+                        ops = [base] + [(W.clone() if layout == "x@W" else Wt.clone().t()) for _ in range(nW - 1)]
+                        for M in (1, 4, 16):
+                            x_h = xs32[M].to(dt)
+                            X = [x_h.to(self.dev) for _ in range(nW)]
+                            Y = [torch.empty(M, N, dtype=dt, device=self.dev) for _ in range(nW)]
+                            ms = _suite_time(lambda i: mb.matmul(X[i], ops[i], out=Y[i]), nW, min_ms=60)
+                            byts = 2.0 * (K * N + M * K + M * N)
+                            gbs = byts / (ms * 1e-3) / 1e9
+                            ref = orc.product(_to_np(x_h), _to_np(w_h[:, cols]), name)
+                            ok, err = orc.check(_to_np(Y[0][:, cols.to(self.dev)]), ref, name)
+                            line = {"suite": "C2", "case": f"{name} M={M} K={K} N={N} {layout}", "metric": "GB/s",
+                                    "value": gbs, "ms": ms,
+                                    "roofline": {"bound": "hbm", "peak": self.hbm, "frac": gbs / self.hbm},
+                                    "check": {"ok": bool(ok), "err": float(err), "cols": 256},
+                                    "plan": mb.kernels.plan(X[0], ops[0]), "l2": f"{nW} rotating weight copies"}
+                            if M == 1 and dt is torch.bfloat16 and layout == "x@W":
+                                x1 = x_h.contiguous()
+                                t0 = time.perf_counter()
+                                torch.matmul(x1, w_h)
+                                reps = 3
+                                t0 = time.perf_counter()
+                                for _ in range(reps):
+                                    torch.matmul(x1, w_h)
+                                sec = (time.perf_counter() - t0) / reps
+                                line["cpu"] = {"value": byts / sec / 1e9, "unit": "GB/s", "cores": self.threads,
+                                               "kind": "port", "sample": "host torch.matmul, whole product"}
+                            self.emit(line)
+                        del ops
+                    del W, Wt
+
+    def c3(self):
+        """Batched / broadcast bmm: roofline time = max(FLOP / tensor peak, bytes / HBM)."""
+        mb, orc = self.mb, self.orc
+        for dt, name in ((torch.float16, "float16"), (torch.bfloat16, "bfloat16")):
+            cases = [("[8,512,256]@[8,256,512]", (8, 512, 256), (8, 256, 512), None),
+                     ("[64,2048,128]@[64,128,2048]", (64, 2048, 128), (64, 128, 2048), None),
+                     ("[256,1024,1024]@[256,1024,1024]", (256, 1024, 1024), (256, 1024, 1024), None),
+                     ("broadcast [64,2048,128]@[1,128,2048]", (64, 2048, 128), (1, 128, 2048), None),
+                     ("transposed A^T: [64,128,2048]^T@[64,128,2048]", (64, 128, 2048), (64, 128, 2048), "at"),
+                     ("sliced A[:, :, :128] of [64,2048,256] (lda=2K)", (64, 2048, 256), (64, 128, 2048), "slice"),
+                     ("offset A[:, 1:, 1:] of [64,2049,129]", (64, 2049, 129), (64, 128, 2048), "offset")]
+            for label, sa, sb, kind in cases:
+                g = torch.Generator().manual_seed(2)
+                a_h = torch.randn(*sa, generator=g).to(dt)
+                b_h = torch.randn(*sb, generator=g).to(dt)
+                if kind == "at":
+                    view = lambda t: t.transpose(1, 2)
+                elif kind == "slice":
+                    view = lambda t: t[:, :, :128]
+                elif kind == "offset":
+                    view = lambda t: t[:, 1:, 1:]
+                else:
+                    view = lambda t: t
+                A_log = view(a_h)
+                Bt, M, K = sb[0], A_log.shape[1], A_log.shape[2]
+                Bsz, N = A_log.shape[0], sb[2]
+                set_bytes = (a_h.numel() + b_h.numel() + Bsz * M * N) * a_h.element_size()
+                n = _nsets(set_bytes, cap=64)
+                As = [view(a_h.to(self.dev)) for _ in range(n)]
+                Bs = [b_h.to(self.dev) for _ in range(n)]
+                Cs = [torch.empty(Bsz, M, N, dtype=dt, device=self.dev) for _ in range(n)]
+                if Bt == 1:
+                    fn = lambda i: mb.matmul(As[i], Bs[i], out=Cs[i])  # broadcast batch, written in place
+                else:
+                    fn = lambda i: mb.bmm(As[i], Bs[i], out=Cs[i])
+                ms = _suite_time(fn, n)
+                flops = 2.0 * Bsz * M * N * K
+                byts = (Bsz * M * K + Bt * K * N + Bsz * M * N) * a_h.element_size()
+                t_roof = max(flops / (self.bf16_peak * 1e12), byts / (self.hbm * 1e9))
+                fn(0)
+                torch.cuda.synchronize()
+                bi = [0, Bsz - 1]
+                ref = orc.product(_to_np(A_log[bi]), _to_np(b_h[[0, 0]] if Bt == 1 else b_h[bi]), name)
+                ok, err = orc.check(_to_np(Cs[0][bi]), ref, name)
+                sec, nb = _cpu_rows(lambda r: torch.matmul(A_log[:r], b_h if Bt == 1 else b_h[:r]), Bsz,
+                                    self.args.cpu_seconds)
+                self.emit({"suite": "C3", "case": f"{name} {label}", "metric": "TFLOP/s",
+                           "value": flops / (ms * 1e-3) / 1e12, "ms": ms,
+                           "roofline": {"bound": "max(tensor, hbm)", "roofline_ms": t_roof * 1e3,
+                                        "frac": t_roof * 1e3 / ms,
+                                        "tensor_frac": flops / (ms * 1e-3) / 1e12 / self.bf16_peak,
+                                        "hbm_frac": byts / (ms * 1e-3) / 1e9 / self.hbm},
+                           "check": {"ok": bool(ok), "err": float(err), "batches": bi},
+                           "plan": mb.kernels.plan(As[0][0], Bs[0][0]), "l2": f"{n} rotating input sets",
+                           "cpu": {"value": 2.0 * nb * M * N * K / sec / 1e12, "unit": "TFLOP/s",
+                                   "cores": self.threads, "kind": "port",
+                                   "sample": f"host torch.matmul, {nb} of {Bsz} batches"}})
+
+    def c4(self):
+        """Integers, bit-exact: 8-bit on the int8 tensor cores, 16/32/64-bit on IMAD."""
+        mb = self.mb
+        layouts = {
+            "rm_rm": (None, None),
+            "rm_cm": (None, lambda t: t.t().contiguous().t()),
+            "cm_cm": (lambda t: t.t().contiguous().t(), lambda t: t.t().contiguous().t()),
+            "offset": (lambda t: _offset_view(t), lambda t: _offset_view(t)),
+        }
+        for n in (4096, 8192):
+            for dt, name in ((torch.int8, "int8"), (torch.uint8, "uint8")):
+                g = torch.Generator().manual_seed(3)
+                lo, hi = _int_range(dt)
+                a = torch.randint(lo, hi, (n, n), dtype=dt, generator=g)
+                b = torch.randint(lo, hi, (n, n), dtype=dt, generator=g)
+                lays = ("rm_rm", "rm_cm", "cm_cm", "offset") if (n == 4096 and dt is torch.int8) else ("rm_rm",)
+                for lay in lays:
+                    av, bv = layouts[lay]
+                    self.gemm_case("C4", f"{name} {n}^3 {lay} full range", a, b, name, self.int8_peak,
+                                   "tensor int8 dense (cuBLASLt measured)", a_view=av, b_view=bv,
+                                   cpu=(lay == "rm_rm" and n == 4096), check_name=name)
+        for dt, name, peak, pname in ((torch.int16, "int16", self.imad, "IMAD probe"),
+                                      (torch.int32, "int32", self.imad, "IMAD probe"),
+                                      (torch.int64, "int64", self.imad64, "int64 mul-add probe")):
+            g = torch.Generator().manual_seed(4)
+            a = torch.randint(-1000, 1000, (2048, 2048), dtype=dt, generator=g)
+            b = torch.randint(-1000, 1000, (2048, 2048), dtype=dt, generator=g)
+            lays = ("rm_rm", "rm_cm", "cm_cm", "offset") if dt is torch.int32 else ("rm_rm",)
+            for lay in lays:
+                av, bv = layouts[lay]
+                self.gemm_case("C4", f"{name} 2048^3 {lay}", a, b, name, peak, pname, a_view=av, b_view=bv,
+                               cpu=(lay == "rm_rm"), check_name=name)
+        # int32 GEMV 1 x 8192 x 8192
+        g = torch.Generator().manual_seed(4)
+        w = torch.randint(-1000, 1000, (8192, 8192), dtype=torch.int32, generator=g)
+        x = torch.randint(-1000, 1000, (1, 8192), dtype=torch.int32, generator=g)
+        self.gemv_case("C4", "int32 GEMV 1x8192x8192 x@W", x, w, "int32")
+
+    def gemv_case(self, suite, case, x_h, w_h, name):
+        mb, orc = self.mb, self.orc
+        M, K = x_h.shape
+        N = w_h.shape[1]
+        elt = w_h.element_size()
+        n = _nsets(K * N * elt, cap=16)
+        W = [w_h.to(self.dev) for _ in range(n)]
+        X = [x_h.to(self.dev) for _ in range(n)]
+        Y = [torch.empty(M, N, dtype=w_h.dtype, device=self.dev) for _ in range(n)]
+        ms = _suite_time(lambda i: mb.matmul(X[i], W[i], out=Y[i]), n)
+        byts = elt * (K * N + M * K + M * N)
+        gbs = byts / (ms * 1e-3) / 1e9
+        ok, err = orc.check(_to_np(Y[0]), orc.product(_to_np(x_h), _to_np(w_h), name), name)
+        self.emit({"suite": suite, "case": case, "metric": "GB/s", "value": gbs, "ms": ms,
+                   "roofline": {"bound": "hbm", "peak": self.hbm, "frac": gbs / self.hbm},
+                   "check": {"ok": bool(ok), "err": float(err)}, "plan": mb.kernels.plan(X[0], W[0]),
+                   "l2": f"{n} rotating weight copies"})
+
+    def c5(self):
+        mb = self.mb
+        for dt, name, peak, pname in ((torch.complex64, "complex64", self.ffma, "FFMA probe (8MNK real ops)"),
+                                      (torch.complex32, "complex32", self.bf16_peak, "tensor fp16 dense")):
+            g = torch.Generator().manual_seed(5)
+            a = torch.complex(torch.randn(4096, 4096, generator=g), torch.randn(4096, 4096, generator=g)).to(dt)
+            b = torch.complex(torch.randn(4096, 4096, generator=g), torch.randn(4096, 4096, generator=g)).to(dt)
+            self.gemm_case("C5", f"{name} 4096^3", a, b, name, peak, pname, flops_mult=8.0, check_name=name)
+            # conj(A) @ B: A passed as a lazy conj view (conj bit, read in place)
+            self.gemm_case("C5", f"{name} conj(A)@B 4096^3", a.conj(), b, name, peak, pname,
+                           make_a=lambda: a.to(self.dev).conj(), flops_mult=8.0, cpu=False, check_name=name)
+            # A^T @ B: A stored row-major, passed transposed (column-major read)
+            self.gemm_case("C5", f"{name} A^T@B 4096^3", a.t(), b, name, peak, pname,
+                           make_a=lambda: a.to(self.dev).t(), flops_mult=8.0, cpu=False, check_name=name)
+            x = torch.complex(torch.randn(1, 8192, generator=g), torch.randn(1, 8192, generator=g)).to(dt)
+            w = torch.complex(torch.randn(8192, 8192, generator=g), torch.randn(8192, 8192, generator=g)).to(dt)
+            self.gemv_case("C5", f"{name} GEMV 1x8192x8192 x@W", x, w, name)
+        g = torch.Generator().manual_seed(6)
+        a = torch.randn(16384, 16384, generator=g).to(torch.bfloat16)
+        b = torch.randn(16384, 16384, generator=g).to(torch.bfloat16)
+        self.gemm_case("C5", "bf16 16384^3", a, b, "bfloat16", self.bf16_peak, "tensor bf16 dense")
+        del a, b
+        g = torch.Generator().manual_seed(6)
+        a = torch.randn(128, 65536, generator=g).to(torch.bfloat16)
+        b = torch.randn(65536, 8192, generator=g).to(torch.bfloat16)
+        self._skinny(a, b)
+
+    def _skinny(self, a_h, b_h):
+        """128 x 8192 x 65536 bf16: HBM-bound (reads B once)."""
+        mb = self.mb
+        M, K = a_h.shape
+        N = b_h.shape[1]
+        As = [a_h.to(self.dev) for _ in range(2)]
+        Bs = [b_h.to(self.dev) for _ in range(2)]
+        Cs = [torch.empty(M, N, dtype=torch.bfloat16, device=self.dev) for _ in range(2)]
+        ms = _suite_time(lambda i: mb.matmul(As[i], Bs[i], out=Cs[i]), 2)
+        byts = 2.0 * (M * K + K * N + M * N)
+        gbs = byts / (ms * 1e-3) / 1e9
+        chk = self.check_rows(Cs[0], a_h, b_h, "bfloat16", rows=16)
+        self.emit({"suite": "C5", "case": "bf16 skinny split-K 128x8192x65536", "metric": "GB/s", "value": gbs,
+                   "ms": ms, "tflops": 2.0 * M * N * K / (ms * 1e-3) / 1e12,
+                   "roofline": {"bound": "hbm", "peak": self.hbm, "frac": gbs / self.hbm}, "check": chk,
+                   "plan": mb.kernels.plan(As[0], Bs[0]), "l2": "inputs 1.1 GB > L2",
+                   "cpu": self.cpu_gemm(a_h, b_h)})
+
+
+def _to_np(t):
+    """Values of a (possibly conj / strided / cuda) tensor as numpy, exactly."""
+    t = t.detach()
+    if t.dtype is torch.complex32:
+        t = t.to(torch.complex64)
+    if t.is_conj():
+        t = t.resolve_conj()
+    if t.is_neg():
+        t = t.resolve_neg()
+    t = t.cpu()
+    if t.dtype is torch.bfloat16:
+        t = t.float()
+    return t.numpy()
+
+
+def _offset_view(t):
+    """The reference's "offset" layout: [1:, 1:] of a (rows+1) x (cols+1) buffer
+    (lda = cols + 1, storage offset > 0)."""
+    big = torch.zeros(t.shape[0] + 1, t.shape[1] + 1, dtype=t.dtype, device=t.device)
+    big[1:, 1:] = t
+    return big[1:, 1:]
+
+
+def run_suite(args):
+    assert torch.cuda.is_available(), "bench.py --suite needs a CUDA device"
+    torch.cuda.set_device(0)
+    s = _Suite(args)
+    for c in args.configs.split(","):
+        getattr(s, c.lower())()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -365,7 +772,14 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="bf16_gemm_4096", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--suite", action="store_true",
+                    help="measure every BASELINE config on one GPU, one JSON line per case")
+    ap.add_argument("--configs", default="C1,C2,C3,C4,C5")
+    ap.add_argument("--cpu-seconds", type=float, default=1.0, help="host time per CPU-baseline sample")
     args = ap.parse_args()
+    if args.suite:
+        run_suite(args)
+        return
     w = dict(WORKLOADS[args.workload])
     w["name"] = args.workload
     w["dtype_name"] = {torch.bfloat16: "bf16", torch.float16: "fp16", torch.int8: "int8"}[w["dtype"]]

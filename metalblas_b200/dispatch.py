@@ -232,6 +232,10 @@ def _matmul_nd(a, b, out=None):
         size = prod(batch)
         a3 = a.expand(*batch, M, K).reshape(size, M, K)
         b3 = b.expand(*batch, K, N).reshape(size, K, N)
+        if (out is not None and not (a_vec or b_vec) and out.shape == (*batch, M, N) and out.dtype == a.dtype
+                and out.is_contiguous()):
+            bmm(a3, b3, out=out.view(size, M, N))  # written in place, no temporary
+            return out
         result = bmm(a3, b3).reshape(*batch, M, N)
     else:
         result = matmul(a, b)
