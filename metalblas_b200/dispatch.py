@@ -17,6 +17,7 @@ CUDA tensors and every product runs through one C-ABI call, ``mb_gemm``
 from __future__ import annotations
 
 import ctypes
+import threading
 from math import prod
 
 import torch
@@ -96,6 +97,44 @@ _BACKENDS = {None: _lib.MB_BACKEND_AUTO, "auto": _lib.MB_BACKEND_AUTO, "gemv": _
              "mpp_tensor": _lib.MB_BACKEND_TC, "mpp": _lib.MB_BACKEND_TC, "simd": _lib.MB_BACKEND_SIMT}
 
 
+# Per-thread cache of filled descriptors: a call whose shapes, strides, dtype,
+# flags, pointer alignment, plan overrides, epilogue scalars, device and stream
+# match an earlier successful call reuses that call's descriptor (including the
+# autotuner's verdict and the workspace) and only sets the data pointers.
+_TLS = threading.local()
+_FAST_MAX = 4096
+_GEN = [0]   # bumped by reset_caches: entries of every thread go stale
+_c_void_p = ctypes.c_void_p
+_byref = ctypes.byref
+
+
+def _fast_cache() -> dict:
+    c = getattr(_TLS, "fast", None)
+    if c is None:
+        c = _TLS.fast = {}
+    return c
+
+
+def reset_caches() -> None:
+    """Forget cached descriptors and workspaces (after a device error or when the
+    autotune table changes)."""
+    _WS.clear()
+    _GEN[0] += 1
+    _fast_cache().clear()
+
+
+try:
+    _raw_stream = torch._C._cuda_getCurrentRawStream
+except AttributeError:  # pragma: no cover - older torch
+    _raw_stream = None
+
+
+def _stream_of(dev) -> int:
+    if _raw_stream is not None:
+        return _raw_stream(dev.index)
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
 def _launch(A, B, C, M, N, K, batch, a3, b3, c3, *, epilogue=None, backend=_lib.MB_BACKEND_AUTO,
             tile_n=0, split_k=0, swap_ab=0, cta_pair=0, stream_k=0, autotune=True):
     """Fill an mb_gemm_desc and call mb_gemm on the current stream of C's device.
@@ -103,26 +142,53 @@ def _launch(A, B, C, M, N, K, batch, a3, b3, c3, *, epilogue=None, backend=_lib.
     a3/b3/c3 are (row stride, col stride, batch stride) in elements.
     epilogue: (bias, (rs, cs, bs), beta, alpha, beta_nz, alpha_nz) or None.
     """
+    dev = C.device
+    if torch.cuda.current_device() != dev.index:
+        with torch.cuda.device(dev):
+            return _launch(A, B, C, M, N, K, batch, a3, b3, c3, epilogue=epilogue, backend=backend,
+                           tile_n=tile_n, split_k=split_k, swap_ab=swap_ab, cta_pair=cta_pair, stream_k=stream_k,
+                           autotune=autotune)
+    stream = _stream_of(dev)
+    pa = A.data_ptr() if A is not None else 0
+    pb = B.data_ptr() if B is not None else 0
+    pc = C.data_ptr()
+    ca = A is not None and A.is_conj()
+    cb = B is not None and B.is_conj()
+    if epilogue is not None:
+        bias, bstr, beta, alpha, bnz, anz = epilogue
+        pbias = bias.data_ptr() if bnz else 0
+        ekey = (bstr, beta, alpha, bool(bnz), bool(anz), pbias & 15)
+    else:
+        ekey = None
+    key = (C.dtype, M, N, K, batch, a3, b3, c3, backend, tile_n, split_k, swap_ab, cta_pair, stream_k,
+           autotune and _plan.AUTOTUNE, ca, cb, pa & 15, pb & 15, pc & 15, ekey, dev.index, stream, _GEN[0])
+    cache = _fast_cache()
+    hit = cache.get(key)
+    if hit is not None:
+        d = hit[0]
+        d.A, d.B, d.C = pa or None, pb or None, pc
+        if ekey is not None:
+            d.bias = pbias or None
+        if _lib._lib.mb_gemm(_byref(d), _c_void_p(stream)) == _lib.MB_OK:
+            return C
+        cache.pop(key, None)  # rerun through the full path, which raises the error
+
     lib = _lib.load()
     dtype = C.dtype
     d = _lib.new_desc()
     d.dtype = _lib.DTYPE_CODE[dtype]
     d.backend = backend
     d.M, d.N, d.K, d.batch = int(M), int(N), int(K), int(batch)
-    d.A = A.data_ptr() if A is not None else None
-    d.B = B.data_ptr() if B is not None else None
-    d.C = C.data_ptr()
+    d.A, d.B, d.C = pa or None, pb or None, pc
     d.a_rs, d.a_cs, d.sA = a3
     d.b_rs, d.b_cs, d.sB = b3
     d.c_rs, d.c_cs, d.sC = c3
-    d.conj_a = int(A is not None and A.is_conj())
-    d.conj_b = int(B is not None and B.is_conj())
+    d.conj_a, d.conj_b = int(ca), int(cb)
     if epilogue is not None:
-        bias, (brs, bcs, bbs), beta, alpha, bnz, anz = epilogue
         d.epilogue = 1
         d.alpha_nz, d.beta_nz = int(bool(anz)), int(bool(bnz))
-        d.bias = bias.data_ptr() if bnz else None
-        d.bias_rs, d.bias_cs, d.bias_bs = brs, bcs, bbs
+        d.bias = pbias or None
+        d.bias_rs, d.bias_cs, d.bias_bs = bstr
         if dtype in INTS:
             d.ialpha, d.ibeta = _int64(alpha), _int64(beta)
         else:
@@ -130,18 +196,14 @@ def _launch(A, B, C, M, N, K, batch, a3, b3, c3, *, epilogue=None, backend=_lib.
             d.beta_re, d.beta_im = float(complex(beta).real), float(complex(beta).imag)
     d.tile_n, d.split_k, d.swap_ab, d.cta_pair = int(tile_n), int(split_k), int(swap_ab), int(cta_pair)
     d.stream_k = int(stream_k)
-    dev = C.device
-    if torch.cuda.current_device() != dev.index:
-        with torch.cuda.device(dev):
-            return _launch(A, B, C, M, N, K, batch, a3, b3, c3, epilogue=epilogue, backend=backend,
-                           tile_n=tile_n, split_k=split_k, swap_ab=swap_ab, cta_pair=cta_pair, stream_k=stream_k,
-                           autotune=autotune)
-    stream = torch.cuda.current_stream(dev).cuda_stream
+    tuned = False
     if autotune and backend == _lib.MB_BACKEND_AUTO and not (tile_n or split_k or swap_ab or cta_pair or stream_k):
         choice = _plan.choose(d, A, B, C, stream)
+        tuned = _plan.AUTOTUNE
         if choice is not None:
             d.backend, d.tile_n, d.split_k, d.swap_ab = choice
     nbytes = int(lib.mb_gemm_workspace_size(ctypes.byref(d)))
+    ws = None
     if nbytes > 0:
         ws = _workspace(dev, stream, nbytes)
         d.workspace, d.workspace_bytes = ws.data_ptr(), ws.numel()
@@ -151,6 +213,12 @@ def _launch(A, B, C, M, N, K, batch, a3, b3, c3, *, epilogue=None, backend=_lib.
         d.backend = _lib.MB_BACKEND_SIMT
         rc = lib.mb_gemm(ctypes.byref(d), ctypes.c_void_p(stream))
     _lib.raise_for(rc)
+    # Cache unless the autotuner has yet to decide this shape (it skips shapes
+    # below its size floor and during stream capture, and those stay untuned).
+    if not tuned or _lib.autotune_lookup(d) is not None or not _plan.wants(d):
+        if len(cache) >= _FAST_MAX:
+            cache.clear()
+        cache[key] = (d, ws)
     return C
 
 

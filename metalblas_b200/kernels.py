@@ -57,7 +57,7 @@ def device_status_clear() -> None:
     allocated on the next call."""
     from . import dispatch
     _lib.device_status_clear()
-    dispatch._WS.clear()
+    dispatch.reset_caches()
 
 
 def debug_wait_timeout(limit_us: int) -> None:

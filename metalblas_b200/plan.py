@@ -173,11 +173,16 @@ def _tune(d, C, stream):
     return None
 
 
+def wants(d) -> bool:
+    """Whether the autotuner would time rivals for this descriptor's shape."""
+    if not AUTOTUNE or d.dtype not in _TC_CODES or d.M <= 1 or d.N <= 1 or d.K == 0:
+        return False
+    return 2.0 * d.M * d.N * d.K * max(d.batch, 1) >= MIN_FLOPS
+
+
 def choose(d, A, B, C, stream):
     """Return (backend, tile_n, split_k, swap_ab) to override the table, or None."""
-    if not AUTOTUNE or d.dtype not in _TC_CODES or d.M <= 1 or d.N <= 1 or d.K == 0:
-        return None
-    if 2.0 * d.M * d.N * d.K * max(d.batch, 1) < MIN_FLOPS:
+    if not wants(d):
         return None
     if torch.cuda.is_current_stream_capturing():
         return None
@@ -194,6 +199,9 @@ def choose(d, A, B, C, stream):
 
 
 def clear():
-    """Forget every tuned shape (the library's table)."""
+    """Forget every tuned shape (the library's table, and this thread's cached
+    descriptors that carry a tuned plan)."""
     with _lock:
         _lib.load().mb_autotune_cache_clear()
+    from . import dispatch
+    dispatch._fast_cache().clear()
