@@ -110,7 +110,9 @@ struct Cfg {
   static constexpr int ACC_COLS = BN;           // fp32/s32: one column per N
   static constexpr int TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
   static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + STAGING_BYTES + BAR_BYTES;
-  static constexpr int RCH = QUART < 32 ? (QUART < 8 ? 8 : QUART) : 32;  // columns per tcgen05.ld, direct path
+  // columns per tcgen05.ld on the direct-store and split-K paths (16 for 16-bit
+  // outputs keeps the epilogue within the register budget of 320 threads)
+  static constexpr int RCH = QUART < (ESZ == 2 ? 16 : 32) ? (QUART < 8 ? 8 : QUART) : (ESZ == 2 ? 16 : 32);
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N for M=128");
   static_assert(STAGES >= 2, "need a pipeline");
   static_assert(SMEM_BYTES <= SMEM_LIMIT, "shared memory");
@@ -560,12 +562,58 @@ __device__ __forceinline__ void epi_values(const TcParams &p, int b, int m, int 
   for (int j = 0; j < NC; ++j) out[j] = epi_value<T>(p, b, m, n0 + j, r[j]);
 }
 
-// Direct stores of NC (<= 32) consecutive columns of one output row.
+// Real epilogue on NC (<= 32) consecutive columns n0.. of row m, in place: the
+// raw accumulator bits in v become the bits of alpha * acc + beta * bias in the
+// accumulator type (fp32 or wrapping u32), mb_epi semantics.  The row's bias values are fetched with
+// 16-byte vector loads when they are contiguous and aligned (the usual bias[N]
+// broadcast of addmm, or a row-major bias matrix), else one load per element.
 template <class T, int NC>
-__device__ __forceinline__ void store_row_chunk(const TcParams &p, int b, int m, int n0, const uint32_t (&r)[32]) {
+__device__ __forceinline__ void epi_real(const TcParams &p, int b, int m, int n0, uint32_t (&v)[32]) {
+  using E = Elem<T>;
+  using Acc = typename E::acc;
+  constexpr int BYTES = NC * (int)sizeof(T);
+  constexpr int NQ = BYTES / 16 > 0 ? BYTES / 16 : 1;
+  union { uint4 q[NQ]; T t[NQ * 16 / sizeof(T)]; } u;  // the bias values, packed
+  const bool use_bias = p.epi.beta_nz && m < p.M;
+  if (use_bias) {
+    const T *row = (const T *)p.bias + (int64_t)b * p.bias_bs + (int64_t)m * p.bias_rs;
+    if (BYTES % 16 == 0 && p.bias_cs == 1 && n0 + NC <= p.N && (reinterpret_cast<uintptr_t>(row + n0) & 15) == 0) {
+#pragma unroll
+      for (int i = 0; i < NQ; ++i) u.q[i] = __ldg(reinterpret_cast<const uint4 *>(row + n0) + i);
+    } else {
+#pragma unroll
+      for (int j = 0; j < NC; ++j) u.t[j] = (n0 + j < p.N) ? row[(int64_t)(n0 + j) * p.bias_cs] : T();
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < NC; ++j) {
+    if constexpr (E::is_int) {
+      Acc x = p.epi.alpha_nz ? (Acc)p.epi.ialpha * v[j] : Acc(0);
+      if (use_bias) x += (Acc)p.epi.ibeta * E::load(u.t[j], false);
+      v[j] = x;
+    } else {
+      float x = p.epi.alpha_nz ? p.epi.alpha_re * __uint_as_float(v[j]) : 0.f;
+      if (use_bias) x = fmaf(p.epi.beta_re, E::load(u.t[j], false), x);
+      v[j] = __float_as_uint(x);
+    }
+  }
+}
+
+// Direct stores of NC (<= 32) consecutive columns of one output row (r is
+// consumed: the epilogue is applied to it in place).
+template <class T, int NC>
+__device__ __forceinline__ void store_row_chunk(const TcParams &p, int b, int m, int n0, uint32_t (&r)[32]) {
   T *C = (T *)p.C + (int64_t)b * p.sC;
   T out[NC];
-  epi_values<T, NC>(p, b, m, n0, r, out);
+  bool cplx = false;
+  if constexpr (std::is_same_v<T, __half>) cplx = p.epi.cplx != 0;
+  if (p.epi.enabled && !cplx) {
+    epi_real<T, NC>(p, b, m, n0, r);
+#pragma unroll
+    for (int j = 0; j < NC; ++j) out[j] = Elem<T>::store(acc_from_bits<T>(r[j]));
+  } else {
+    epi_values<T, NC>(p, b, m, n0, r, out);
+  }
   constexpr int PER16 = 16 / sizeof(T);
   if (NC % PER16 == 0 && p.c_vec && n0 + NC <= p.N) {
     uint4 *dst = reinterpret_cast<uint4 *>(C + (int64_t)m * p.c_rs + n0);
@@ -583,28 +631,41 @@ __device__ __forceinline__ void store_row_chunk(const TcParams &p, int b, int m,
 // pairs of fp32 round with one cvt to bf16x2 / f16x2, 8-bit outputs keep the
 // low byte of each s32 (two's-complement wrap) via byte permutes.
 template <class T>
-__device__ __forceinline__ void pack32(const TcParams &p, int b, int m, int n0, const uint32_t (&r)[32],
-                                       uint32_t (&pk)[32 * sizeof(T) / 4]) {
-  if (!p.epi.enabled) {
-    if constexpr (sizeof(T) == 2) {
+__device__ __forceinline__ void pack_bits32(const uint32_t (&r)[32], uint32_t (&pk)[32 * sizeof(T) / 4]) {
+  if constexpr (sizeof(T) == 2) {
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        if constexpr (std::is_same_v<T, __nv_bfloat16>) {
-          __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
-          pk[j] = *reinterpret_cast<uint32_t *>(&h);
-        } else {
-          __half2 h = __floats2half2_rn(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
-          pk[j] = *reinterpret_cast<uint32_t *>(&h);
-        }
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const uint32_t lo = __byte_perm(r[4 * j], r[4 * j + 1], 0x0040);
-        const uint32_t hi = __byte_perm(r[4 * j + 2], r[4 * j + 3], 0x0040);
-        pk[j] = __byte_perm(lo, hi, 0x5410);
+    for (int j = 0; j < 16; ++j) {
+      if constexpr (std::is_same_v<T, __nv_bfloat16>) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
+        pk[j] = *reinterpret_cast<uint32_t *>(&h);
+      } else {
+        __half2 h = __floats2half2_rn(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
+        pk[j] = *reinterpret_cast<uint32_t *>(&h);
       }
     }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t lo = __byte_perm(r[4 * j], r[4 * j + 1], 0x0040);
+      const uint32_t hi = __byte_perm(r[4 * j + 2], r[4 * j + 3], 0x0040);
+      pk[j] = __byte_perm(lo, hi, 0x5410);
+    }
+  }
+}
+
+// (r is consumed: the epilogue is applied to it in place.)
+template <class T>
+__device__ __forceinline__ void pack32(const TcParams &p, int b, int m, int n0, uint32_t (&r)[32],
+                                       uint32_t (&pk)[32 * sizeof(T) / 4]) {
+  if (!p.epi.enabled) {
+    pack_bits32<T>(r, pk);
+    return;
+  }
+  bool cplx = false;
+  if constexpr (std::is_same_v<T, __half>) cplx = p.epi.cplx != 0;
+  if (!cplx) {
+    epi_real<T, 32>(p, b, m, n0, r);
+    pack_bits32<T>(r, pk);
     return;
   }
   T out[32];
