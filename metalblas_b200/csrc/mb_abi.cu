@@ -37,6 +37,7 @@
 #include "tc_gemm.cuh"
 #include "c32.cuh"
 #include "peaks.cuh"
+#include "pack.cuh"
 
 using namespace mb;
 
@@ -171,7 +172,7 @@ constexpr int kGemvWarps = 8;         // warps per GEMV CTA
 constexpr int kGemvRowsPerWarp = 2;   // staged-x rows kernel
 constexpr int64_t kGemvRowsPerCta = kGemvWarps * kGemvRowsPerWarp;
 
-enum PlanKind { PK_EMPTY = 0, PK_GEMV_COLS, PK_GEMV_ROWS, PK_TC, PK_SIMT, PK_TC_C32 };
+enum PlanKind { PK_EMPTY = 0, PK_GEMV_COLS, PK_GEMV_ROWS, PK_TC, PK_SIMT, PK_TC_C32, PK_TC_PACKED };
 
 struct Plan {
   int kind = PK_EMPTY;
@@ -193,6 +194,10 @@ struct Plan {
   int64_t c32_lda = 0, c32_ldb = 0; // row pitch of packed A' / of B', in half2 pairs
   int64_t c32_a_off = 0, c32_b_off = 0, c32_a_batches = 1, c32_b_batches = 1;
   int a_mn = 0, b_mn = 0;
+  // PK_TC_PACKED: operands TMA cannot address are first copied into the
+  // workspace as dense row-major matrices (A' M x lda', B' K x ldb')
+  int pk_a = 0, pk_b = 0;
+  int64_t pk_lda = 0, pk_ldb = 0, pk_a_off = 0, pk_b_off = 0, pk_a_batches = 1, pk_b_batches = 1;
   // shared
   int64_t ws_bytes = 0;
   std::string why;
@@ -467,6 +472,58 @@ bool plan_c32(const Op &o, int sms, const mb_gemm_desc *d, bool have_ws, Plan &p
   return true;
 }
 
+// TMA can load this operand (rows x cols, strides rs / cs, batch stride bs) in
+// place: 16-byte aligned base, a unit stride, and the other stride and the
+// batch stride multiples of 16 bytes.
+bool operand_tma_ok(const void *ptr, int64_t rows, int64_t cols, int64_t rs, int64_t cs, int64_t bs, int64_t batch,
+                    int esz) {
+  if (!aligned16(ptr)) return false;
+  if (batch > 1 && (bs < 0 || (bs * esz) % 16)) return false;
+  if (cs == 1 && rs >= cols && (rs * esz) % 16 == 0) return true;
+  if (rs == 1 && cs >= rows && (cs * esz) % 16 == 0) return true;
+  return false;
+}
+
+// The TC GEMM on operands of which at least one TMA cannot address (the
+// reference's "offset" view A[1:, 1:] with lda = K+1, odd pitches, no unit
+// stride): those are copied into the workspace first.  The reference copies
+// such views with .contiguous() (metalblas/dispatch.py:33-35); here the copy
+// goes to aligned scratch and the product still runs on the tensor cores.
+Op packed_op(const Op &o, const Plan &t, const void *a, const void *b) {
+  Op r = o;
+  if (t.pk_a) { r.A = a; r.a_rs = t.pk_lda; r.a_cs = 1; r.sA = o.sA ? o.M * t.pk_lda : 0; }
+  if (t.pk_b) { r.B = b; r.b_rs = t.pk_ldb; r.b_cs = 1; r.sB = o.sB ? o.K * t.pk_ldb : 0; }
+  return r;
+}
+
+bool plan_tc_any(const Op &o, int sms, const mb_gemm_desc *d, bool have_ws, Plan &pl);
+
+bool plan_packed(const Op &o, int sms, const mb_gemm_desc *d, bool have_ws, Plan &pl) {
+  if (!is_tc_dtype(o.dt) || !have_ws || o.M < 1 || o.N < 1 || o.K < 1) return false;
+  if (o.M >= (1ll << 31) || o.N >= (1ll << 31) || o.K >= (1ll << 31)) return false;
+  const int esz = elem_size(o.dt);
+  Plan t;
+  t.pk_a = !operand_tma_ok(o.A, o.M, o.K, o.a_rs, o.a_cs, o.sA, o.batch, esz);
+  t.pk_b = !operand_tma_ok(o.B, o.K, o.N, o.b_rs, o.b_cs, o.sB, o.batch, esz);
+  if (!t.pk_a && !t.pk_b) return false;
+  t.pk_lda = round_up(o.K, 16 / esz);
+  t.pk_ldb = round_up(o.N, 16 / esz);
+  t.pk_a_batches = o.sA ? o.batch : 1;
+  t.pk_b_batches = o.sB ? o.batch : 1;
+  const void *ph = reinterpret_cast<const void *>(uintptr_t(1) << 20);  // aligned placeholder
+  const Op r = packed_op(o, t, ph, ph);
+  if (!plan_tc_any(r, sms, d, have_ws, t)) return false;
+  const int64_t base = std::max<int64_t>(t.ws_bytes, kTicketBytes);
+  const int64_t a_bytes = t.pk_a ? t.pk_a_batches * o.M * t.pk_lda * esz : 0;
+  const int64_t b_bytes = t.pk_b ? t.pk_b_batches * o.K * t.pk_ldb * esz : 0;
+  t.pk_a_off = round_up(base, 256);
+  t.pk_b_off = round_up(t.pk_a_off + a_bytes, 256);
+  t.ws_bytes = t.pk_b_off + b_bytes;
+  t.kind = PK_TC_PACKED;
+  pl = t;
+  return true;
+}
+
 bool plan_gemv(const Op &o, int sms, const mb_gemm_desc *d, bool have_ws, Plan &pl) {
   GemvParams g{};
   int kind = 0;
@@ -560,28 +617,34 @@ int make_plan(const mb_gemm_desc *d, const Op &o, int sms, bool have_ws, Plan &p
   }
   if (be == MB_BACKEND_TC) {
     if (!is_tc_dtype(o.dt)) return fail(MB_ERR_UNSUPPORTED, "tensor-core backend supports bf16/fp16/int8/uint8 only");
-    const bool want_swap = d->swap_ab == 1 || (d->swap_ab == 0 && o.M < 128 && o.N > o.M);
-    if (want_swap && d->swap_ab != -1) {
-      Op s = swapped(o);
-      if (plan_tc(s, sms, d, have_ws, pl)) { pl.swap = 1; return MB_OK; }
-    }
-    if (d->swap_ab != 1 && plan_tc(o, sms, d, have_ws, pl)) { pl.swap = 0; return MB_OK; }
+    if (plan_tc_any(o, sms, d, have_ws, pl)) return MB_OK;
+    if (plan_packed(o, sms, d, have_ws, pl)) return MB_OK;
     return fail(MB_ERR_UNSUPPORTED, "tensor-core backend: operands not TMA-addressable (need a unit stride, "
-                                    "16-byte aligned base and leading/batch strides)");
+                                    "16-byte aligned base and leading/batch strides) and no workspace to pack them");
   }
   // AUTO
   if ((o.M == 1 || o.N == 1) && plan_gemv(o, sms, d, have_ws, pl)) return MB_OK;
   if (o.dt == MB_C32 && plan_c32(o, sms, d, have_ws, pl)) return MB_OK;
   if (is_tc_dtype(o.dt)) {
-    const bool want_swap = d->swap_ab == 1 || (d->swap_ab == 0 && o.M < 128 && o.N > o.M);
-    if (want_swap && d->swap_ab != -1) {
-      Op s = swapped(o);
-      if (plan_tc(s, sms, d, have_ws, pl)) { pl.swap = 1; return MB_OK; }
-    }
-    if (d->swap_ab != 1 && plan_tc(o, sms, d, have_ws, pl)) { pl.swap = 0; return MB_OK; }
+    if (plan_tc_any(o, sms, d, have_ws, pl)) return MB_OK;
+    // worth a copy when the product is large enough for the tensor cores to
+    // win it back (the CUDA-core kernel reads any layout in place)
+    if ((double)o.M * o.N * o.K * std::max<int64_t>(o.batch, 1) >= 1.0e8 && plan_packed(o, sms, d, have_ws, pl))
+      return MB_OK;
   }
   pl.kind = PK_SIMT;
   return MB_OK;
+}
+
+// The TC plan on o as given or, for thin M, as Cᵀ = Bᵀ·Aᵀ.
+bool plan_tc_any(const Op &o, int sms, const mb_gemm_desc *d, bool have_ws, Plan &pl) {
+  const bool want_swap = d->swap_ab == 1 || (d->swap_ab == 0 && o.M < 128 && o.N > o.M);
+  if (want_swap && d->swap_ab != -1) {
+    Op s = swapped(o);
+    if (plan_tc(s, sms, d, have_ws, pl)) { pl.swap = 1; return true; }
+  }
+  if (d->swap_ab != 1 && plan_tc(o, sms, d, have_ws, pl)) { pl.swap = 0; return true; }
+  return false;
 }
 
 int validate(const mb_gemm_desc *d) {
@@ -859,6 +922,28 @@ int launch_c32(const Op &o, const Plan &pl, EpiScalars e, void *ws, int sms, cud
   return launch_tc<__half>(c32_inner(o, pl, ap, bp), pl, e, ws, sms, st);
 }
 
+template <class T>
+int launch_packed(const Op &o, const Plan &pl, const EpiScalars &e, void *ws, int sms, cudaStream_t st) {
+  char *w = reinterpret_cast<char *>(ws);
+  void *ap = w + pl.pk_a_off, *bp = w + pl.pk_b_off;
+  using U = std::conditional_t<sizeof(T) == 1, uint8_t, uint16_t>;
+  const int grid_cap = sms * 16;
+  auto pack = [&](const void *src, void *dst, int64_t rows, int64_t cols, int64_t rs, int64_t cs, int64_t bs,
+                  int64_t batches, int64_t ld, const char *what) {
+    PackArgs a{src, dst, rows, cols, rs, cs, bs, batches, ld};
+    const int64_t n = batches * rows * cols;
+    pack_matrix_kernel<U><<<(unsigned)std::max<int64_t>(1, std::min<int64_t>(ceil_div(n, 256), grid_cap)), 256, 0,
+                            st>>>(a);
+    return cuda_check(cudaGetLastError(), what);
+  };
+  int rc = MB_OK;
+  if (pl.pk_a) rc = pack(o.A, ap, o.M, o.K, o.a_rs, o.a_cs, o.sA, pl.pk_a_batches, pl.pk_lda, "pack A");
+  if (!rc && pl.pk_b) rc = pack(o.B, bp, o.K, o.N, o.b_rs, o.b_cs, o.sB, pl.pk_b_batches, pl.pk_ldb, "pack B");
+  if (rc) return rc;
+  const Op r = packed_op(o, pl, ap, bp);
+  return launch_tc<T>(pl.swap ? swapped(r) : r, pl, e, ws, sms, st);
+}
+
 template <class F>
 int by_dtype(int dt, F &&f) {
   switch (dt) {
@@ -960,6 +1045,11 @@ int mb_plan_query(const mb_gemm_desc *d, char *buf, int buflen) {
       snprintf(tmp, sizeof(tmp), "tc_c32 pack_a=%d bn=%d split=%d pair=%d tiles=%lldx%lld ws=%lld", pl.c32_pack_a,
                pl.bn, pl.splits, pl.pair, (long long)pl.tiles_m, (long long)pl.tiles_n, (long long)pl.ws_bytes);
       break;
+    case PK_TC_PACKED:
+      snprintf(tmp, sizeof(tmp), "tc_packed pack_a=%d pack_b=%d bn=%d split=%d pair=%d sk=%d swap=%d tiles=%lldx%lld ws=%lld",
+               pl.pk_a, pl.pk_b, pl.bn, pl.splits, pl.pair, pl.sk, pl.swap, (long long)pl.tiles_m,
+               (long long)pl.tiles_n, (long long)pl.ws_bytes);
+      break;
     default: snprintf(tmp, sizeof(tmp), "simt"); break;
   }
   const int n = (int)strlen(tmp);
@@ -988,6 +1078,9 @@ int mb_gemm(const mb_gemm_desc *d, void *stream) {
         if constexpr (IsTc<T>::v) return launch_tc<T>(pl.swap ? swapped(o) : o, pl, e, d->workspace, sms, st);
         else return fail(MB_ERR_UNSUPPORTED, "tensor-core path for non-TC dtype");
       case PK_TC_C32: return launch_c32(o, pl, e, d->workspace, sms, st);
+      case PK_TC_PACKED:
+        if constexpr (IsTc<T>::v) return launch_packed<T>(o, pl, e, d->workspace, sms, st);
+        else return fail(MB_ERR_UNSUPPORTED, "tensor-core path for non-TC dtype");
       default: return launch_simt<T>(o, e, st);
     }
   });
@@ -1155,9 +1248,11 @@ int mb_gemm_noalloc(const mb_gemm_desc *d, void *stream) {
   int rc = plan_for(&q, pl, o, sms);
   if (rc) return rc;
   if (pl.kind == PK_EMPTY) return MB_OK;
-  if (pl.kind == PK_TC_C32 && pl.ws_bytes > (int64_t)MB_NOALLOC_SCRATCH_BYTES && q.backend == MB_BACKEND_AUTO) {
-    // complex32 on the tensor cores needs its expanded B' in scratch; when it
-    // does not fit, the CUDA-core kernel (no scratch) computes the product
+  if ((pl.kind == PK_TC_C32 || pl.kind == PK_TC_PACKED) && pl.ws_bytes > (int64_t)MB_NOALLOC_SCRATCH_BYTES &&
+      q.backend == MB_BACKEND_AUTO) {
+    // complex32 on the tensor cores needs its expanded B' in scratch, packed
+    // operands their copies; when they do not fit, the CUDA-core kernel (no
+    // scratch, any layout) computes the product
     q.backend = MB_BACKEND_SIMT;
     rc = plan_for(&q, pl, o, sms);
     if (rc) return rc;
@@ -1185,6 +1280,9 @@ int mb_gemm_noalloc(const mb_gemm_desc *d, void *stream) {
         if constexpr (IsTc<T>::v) return launch_tc<T>(pl.swap ? swapped(o) : o, pl, e, scratch, sms, st);
         else return fail(MB_ERR_UNSUPPORTED, "tensor-core path for non-TC dtype");
       case PK_TC_C32: return launch_c32(o, pl, e, scratch, sms, st);
+      case PK_TC_PACKED:
+        if constexpr (IsTc<T>::v) return launch_packed<T>(o, pl, e, scratch, sms, st);
+        else return fail(MB_ERR_UNSUPPORTED, "tensor-core path for non-TC dtype");
       default: return launch_simt<T>(o, e, st);
     }
   });

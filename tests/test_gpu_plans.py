@@ -171,3 +171,44 @@ def test_gemv_rows_k_split(dtype):
 def test_no_device_timeouts():
     from metalblas_b200 import kernels
     assert kernels.device_status() == 0
+
+
+def _offset(t):
+    """[1:, 1:] of a buffer one row and one column larger (lda = cols + 1, storage
+    offset > 0): the reference's "offset" layout, which TMA cannot address."""
+    big = torch.zeros(*t.shape[:-2], t.shape[-2] + 1, t.shape[-1] + 1, dtype=t.dtype, device=t.device)
+    big[..., 1:, 1:] = t
+    return big[..., 1:, 1:]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.int8, torch.uint8], ids=NAME.get)
+def test_packed_operands_on_tensor_cores(dtype):
+    """Views TMA cannot load in place are packed into the workspace and run on
+    the tensor cores (plan "tc_packed"); results match the oracle for plain,
+    thin-M (swapped), batched/broadcast and epilogue cases."""
+    import metalblas_b200 as mb
+    gen = torch.Generator().manual_seed(14)
+    full = dtype in (torch.int8, torch.uint8)
+    for (M, N, K) in [(512, 640, 768), (16, 1000, 2048), (1000, 96, 1100)]:
+        a = rand((M, K), dtype, gen, full_range=full)
+        b = rand((K, N), dtype, gen, full_range=full)
+        ref = orc.product(to_np(a), to_np(b), NAME[dtype])
+        # row-major offset views, and a column-major one (lda = M + 1)
+        for av, bv in ((_offset(a), b), (a, _offset(b)), (_offset(a), _offset(b)), (_offset(a.t().contiguous()).t(), b)):
+            expect = "tc_packed" if M * N * K >= 1e8 else "simt"  # small products stay on CUDA cores
+            assert mb.kernels.plan(av, bv).startswith(expect), mb.kernels.plan(av, bv)
+            ok, err = orc.check(to_np(mb.matmul(av, bv)), ref, NAME[dtype])
+            assert ok, f"{(M, N, K)} err={err}"
+    # batched with a broadcast B, and addmm
+    A = rand((5, 300, 520), dtype, gen, full_range=full)
+    B = rand((1, 520, 260), dtype, gen, full_range=full)
+    ref = orc.product(to_np(A), np.broadcast_to(to_np(B), (5, 520, 260)), NAME[dtype])
+    ok, err = orc.check(to_np(mb.matmul(_offset(A), _offset(B))), ref, NAME[dtype])
+    assert ok, f"batched err={err}"
+    a = rand((700, 900), dtype, gen, full_range=full)
+    b = rand((900, 500), dtype, gen, full_range=full)
+    bias = rand((500,), dtype, gen, full_range=full)
+    beta, alpha = (3, -2) if full else (0.5, 2.0)
+    got = mb.addmm(bias, _offset(a), b, beta=beta, alpha=alpha)
+    ok, err = orc.check(to_np(got), orc.fused(to_np(bias), to_np(a), to_np(b), beta, alpha, NAME[dtype]), NAME[dtype])
+    assert ok, f"addmm err={err}"
