@@ -227,6 +227,8 @@ def run_ours(args, w, rank, world, device):
         ok_rows, err = orc.check(got.float().numpy() if dt is not torch.int8 else got.numpy(), ref, name)
         ok_rows = {"ok": bool(ok_rows), "rel_frobenius_or_mismatch": err, "rows_checked": int(len(idx))}
 
+    bmm_line = run_bmm_sharded(args, rank, world, device) if not args.no_bmm else None
+
     # gathered variant (N > 1): all-gather the output shards over NVLink each step
     gathered = None
     if world > 1:
@@ -323,7 +325,61 @@ def run_ours(args, w, rank, world, device):
                    "vs_baseline_ref": "Apple M5 Max 42.95 TFLOP/s (perf_benchs/M5_Max.md:17)"},
         "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gathered": gathered,
         "gpu_launches": args.steps, "check": ok_rows, "clocks": sampler.summary() if rank == 0 else None,
+        "bmm": bmm_line,
     }
+
+
+def run_bmm_sharded(args, rank, world, device):
+    """BASELINE's "bmm TFLOP/s at 1-8 GPUs": bf16 bmm [256,1024,1024] @
+    [256,1024,1024] (N(0,1), seed 2) with the batch sharded over the ranks
+    (strong scaling: the 256 batches are split, metalblas_b200.shard.shard_range).
+    `value` keeps each rank's output slab local; `gathered` adds an NCCL
+    all-gather of the slabs into the full [256, 1024, 1024] every step.  Device
+    time, max over ranks, 2 input sets (1.5 GB > L2)."""
+    import metalblas_b200 as mb
+    from metalblas_b200 import shard
+    Bt, M, N, K = 256, 1024, 1024, 1024
+    s, e = shard.shard_range(Bt, world, rank)
+    nb = e - s
+    g = torch.Generator(device=device).manual_seed(2 + rank)
+    As = [torch.randn(nb, M, K, generator=g, device=device, dtype=torch.bfloat16) for _ in range(2)]
+    Bs = [torch.randn(nb, K, N, generator=g, device=device, dtype=torch.bfloat16) for _ in range(2)]
+    Cs = [torch.empty(nb, M, N, device=device, dtype=torch.bfloat16) for _ in range(2)]
+    steps = max(5, min(args.steps, 50))
+    stream = torch.cuda.current_stream(device)
+
+    def timed(fn):
+        for i in range(3):
+            fn(i % 2)
+        _barrier(world, device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(steps):
+            fn(i % 2)
+        e1.record(stream)
+        e1.synchronize()
+        _barrier(world, device)
+        return _max_over_ranks(e0.elapsed_time(e1) / steps, world, device)
+
+    ms = timed(lambda i: mb.bmm(As[i], Bs[i], out=Cs[i]))
+    flops = 2.0 * Bt * M * N * K
+    out = {"workload": "bf16 bmm [256,1024,1024]@[256,1024,1024], batch sharded over ranks (strong scaling)",
+           "value": flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms, "steps": steps,
+           "batches_per_rank": nb, "plan": mb.kernels.plan(As[0], Bs[0])}
+    if world > 1:
+        import torch.distributed as dist
+        per = -(-Bt // world)
+        pad = torch.empty(per, M, N, device=device, dtype=torch.bfloat16)
+        full = torch.empty(world * per, M, N, device=device, dtype=torch.bfloat16)
+
+        def step(i):
+            mb.bmm(As[i], Bs[i], out=Cs[i])
+            pad[:nb].copy_(Cs[i])
+            dist.all_gather_into_tensor(full, pad)
+        gms = timed(step)
+        out["gathered"] = {"value": flops / (gms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": gms,
+                           "collective": "NCCL all_gather_into_tensor of the padded slabs"}
+    return out
 
 
 def run_reference(args, w, rank, world):
@@ -626,7 +682,7 @@ class _Suite:
                                         "tensor_frac": flops / (ms * 1e-3) / 1e12 / self.bf16_peak,
                                         "hbm_frac": byts / (ms * 1e-3) / 1e9 / self.hbm},
                            "check": {"ok": bool(ok), "err": float(err), "batches": bi},
-                           "plan": mb.kernels.plan(As[0][0], Bs[0][0]), "l2": f"{n} rotating input sets",
+                           "plan": mb.kernels.plan(As[0], Bs[0]), "l2": f"{n} rotating input sets",
                            "cpu": {"value": 2.0 * nb * M * N * K / sec / 1e12, "unit": "TFLOP/s",
                                    "cores": self.threads, "kind": "port",
                                    "sample": f"host torch.matmul, {nb} of {Bsz} batches"}})
@@ -772,6 +828,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="bf16_gemm_4096", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-bmm", action="store_true", help="skip the batch-sharded bmm measurement")
     ap.add_argument("--suite", action="store_true",
                     help="measure every BASELINE config on one GPU, one JSON line per case")
     ap.add_argument("--configs", default="C1,C2,C3,C4,C5")

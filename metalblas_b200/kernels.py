@@ -29,18 +29,30 @@ def has_tcgen05() -> bool:
 
 
 def plan(a, b, *, backend=None) -> str:
-    """The plan mb_gemm would run for ``a @ b`` (2-D CUDA tensors)."""
+    """The plan mb_gemm would run for ``a @ b``: 2-D CUDA tensors, or 3-D
+    batches as ``bmm`` takes them (a [B, M, K], b [B or 1, K, N], output
+    row-major [B, M, N])."""
     from .dispatch import _BACKENDS, _matrix_view
-    M, K = a.shape
-    N = b.shape[1]
-    A, B = _matrix_view(a, M, K), _matrix_view(b, K, N)
+    batched = a.dim() == 3
+    M, K = a.shape[-2:]
+    N = b.shape[-1]
     d = _lib.new_desc()
     d.dtype = _lib.DTYPE_CODE[a.dtype]
     d.backend = _BACKENDS[backend]
     d.M, d.N, d.K = M, N, K
+    if batched:
+        A, B = a, b
+        d.batch = a.shape[0]
+        d.a_rs, d.a_cs = A.stride()[1:]
+        d.b_rs, d.b_cs = B.stride()[1:]
+        d.sA = A.stride(0)
+        d.sB = 0 if b.shape[0] == 1 else B.stride(0)
+        d.sC = M * N
+    else:
+        A, B = _matrix_view(a, M, K), _matrix_view(b, K, N)
+        d.a_rs, d.a_cs = A.stride()
+        d.b_rs, d.b_cs = B.stride()
     d.A, d.B, d.C = A.data_ptr(), B.data_ptr(), A.data_ptr()
-    d.a_rs, d.a_cs = A.stride()
-    d.b_rs, d.b_cs = B.stride()
     d.c_rs, d.c_cs = N, 1
     d.workspace_bytes = -1  # plan as a call with a workspace (the public API always provides one)
     return _lib.plan_query(d)
