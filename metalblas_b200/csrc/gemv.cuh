@@ -106,6 +106,71 @@ __device__ __forceinline__ void gemv_store(const GemvParams &p, int64_t b, int64
   ((T *)p.Y)[b * p.sY + r * p.y_s] = Elem<T>::store(v);
 }
 
+// One K row of gemv_cols: acc[i] += x * w[i] for VEC consecutive columns.
+// Generic form: widen and multiply in the accumulator type.
+template <class T, int VEC>
+struct ColRow {
+  using Acc = typename Elem<T>::acc;
+  struct X { Acc v; };
+  __device__ static __forceinline__ X prep(T x, int conj_x, int) { return X{Elem<T>::load(x, conj_x)}; }
+  __device__ static __forceinline__ void run(Acc (&acc)[VEC], const T (&w)[VEC], const X &x, int conj_w) {
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) Elem<T>::mad(acc[i], x.v, Elem<T>::load(w[i], conj_w));
+  }
+};
+// 16-bit floats: the sm_100 mixed-precision FMA takes w's halves directly
+// (fp32 addend and result, one rounding: the same value as fmaf on the widened
+// operands).
+#define MB_COLROW_MIXED(TYPE, PTXT)                                                           \
+  template <>                                                                                 \
+  struct ColRow<TYPE, 8> {                                                                    \
+    struct X { unsigned short h; };                                                           \
+    __device__ static __forceinline__ X prep(TYPE x, int, int) {                              \
+      return X{*reinterpret_cast<const unsigned short *>(&x)};                                \
+    }                                                                                         \
+    __device__ static __forceinline__ void run(float (&acc)[8], const TYPE (&w)[8], const X &x, int) { \
+      const unsigned *wv = reinterpret_cast<const unsigned *>(w);                             \
+      _Pragma("unroll") for (int i = 0; i < 4; ++i)                                           \
+        asm("{.reg .b16 wl, wh;\n\t"                                                          \
+            "mov.b32 {wl, wh}, %2;\n\t"                                                       \
+            "fma.rn.f32." PTXT " %0, wl, %3, %0;\n\t"                                         \
+            "fma.rn.f32." PTXT " %1, wh, %3, %1;}"                                            \
+            : "+f"(acc[2 * i]), "+f"(acc[2 * i + 1]) : "r"(wv[i]), "h"(x.h));                 \
+    }                                                                                         \
+  };
+MB_COLROW_MIXED(__nv_bfloat16, "bf16")
+MB_COLROW_MIXED(__half, "f16")
+#undef MB_COLROW_MIXED
+// complex32: acc += op(w) * x with four mixed-precision FMAs per element on the
+// packed (re, im) halves; x is turned once into the half coefficients
+// (P, Q, R, S) with re += w.re*P + w.im*Q and im += w.re*R + w.im*S, which fold
+// the conjugations of x and of w into signs (negating a half is exact).
+template <>
+struct ColRow<__half2, 4> {
+  struct X { unsigned pq, rs; };
+  __device__ static __forceinline__ X prep(__half2 x, int conj_x, int conj_w) {
+    const __half xr = __low2half(x);
+    const __half xi = conj_x ? __hneg(__high2half(x)) : __high2half(x);
+    const __half2 pq = conj_w ? __halves2half2(xr, xi) : __halves2half2(xr, __hneg(xi));
+    const __half2 rs = conj_w ? __halves2half2(xi, __hneg(xr)) : __halves2half2(xi, xr);
+    return X{*reinterpret_cast<const unsigned *>(&pq), *reinterpret_cast<const unsigned *>(&rs)};
+  }
+  __device__ static __forceinline__ void run(cf32 (&acc)[4], const __half2 (&w)[4], const X &x, int) {
+    const unsigned *wv = reinterpret_cast<const unsigned *>(w);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      asm("{.reg .b16 wr, wi, p, q, r, s;\n\t"
+          "mov.b32 {wr, wi}, %2;\n\t"
+          "mov.b32 {p, q}, %3;\n\t"
+          "mov.b32 {r, s}, %4;\n\t"
+          "fma.rn.f32.f16 %0, wr, p, %0;\n\t"
+          "fma.rn.f32.f16 %0, wi, q, %0;\n\t"
+          "fma.rn.f32.f16 %1, wr, r, %1;\n\t"
+          "fma.rn.f32.f16 %1, wi, s, %1;}"
+          : "+f"(acc[i].re), "+f"(acc[i].im) : "r"(wv[i]), "r"(x.pq), "r"(x.rs));
+  }
+};
+
 // ---------------------------------------------------------------------------
 // gemv_cols: grid (ceil(R / (32*VEC)), ksplit, batch), NW warps per CTA.
 // VEC == 1 is the unaligned fallback (scalar loads).
@@ -136,24 +201,21 @@ __global__ void __launch_bounds__(NW * 32) gemv_cols_kernel(const GemvParams p) 
   if constexpr (VEC > 1) {
     if (full) {
       done = true;
+    using CR = ColRow<T, VEC>;
     for (; k + (U - 1) * NW < kend; k += U * NW) {
       T w[U][VEC];
-      Acc xv[U];
+      typename CR::X xv[U];
 #pragma unroll
       for (int u = 0; u < U; ++u) VecLoad<T, VEC>::load(W + (k + u * NW) * p.w_ld + c0, w[u]);
 #pragma unroll
-      for (int u = 0; u < U; ++u) xv[u] = E::load(X[(k + u * NW) * p.x_s], p.conj_x);
+      for (int u = 0; u < U; ++u) xv[u] = CR::prep(X[(k + u * NW) * p.x_s], p.conj_x, p.conj_w);
 #pragma unroll
-      for (int u = 0; u < U; ++u)
-#pragma unroll
-        for (int i = 0; i < VEC; ++i) E::mad(acc[i], xv[u], E::load(w[u][i], p.conj_w));
+      for (int u = 0; u < U; ++u) CR::run(acc, w[u], xv[u], p.conj_w);
     }
     for (; k < kend; k += NW) {
       T w[VEC];
       VecLoad<T, VEC>::load(W + k * p.w_ld + c0, w);
-      const Acc xv = E::load(X[k * p.x_s], p.conj_x);
-#pragma unroll
-      for (int i = 0; i < VEC; ++i) E::mad(acc[i], xv, E::load(w[i], p.conj_w));
+      CR::run(acc, w, CR::prep(X[k * p.x_s], p.conj_x, p.conj_w), p.conj_w);
     }
     }
   }

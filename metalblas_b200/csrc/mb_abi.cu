@@ -197,6 +197,7 @@ struct Plan {
   // PK_TC_PACKED: operands TMA cannot address are first copied into the
   // workspace as dense row-major matrices (A' M x lda', B' K x ldb')
   int pk_a = 0, pk_b = 0;
+  int pk_a_cm = 0, pk_b_cm = 0;  // packed column-major (source column-contiguous): a plain strided copy
   int64_t pk_lda = 0, pk_ldb = 0, pk_a_off = 0, pk_b_off = 0, pk_a_batches = 1, pk_b_batches = 1;
   // shared
   int64_t ws_bytes = 0;
@@ -491,8 +492,16 @@ bool operand_tma_ok(const void *ptr, int64_t rows, int64_t cols, int64_t rs, int
 // goes to aligned scratch and the product still runs on the tensor cores.
 Op packed_op(const Op &o, const Plan &t, const void *a, const void *b) {
   Op r = o;
-  if (t.pk_a) { r.A = a; r.a_rs = t.pk_lda; r.a_cs = 1; r.sA = o.sA ? o.M * t.pk_lda : 0; }
-  if (t.pk_b) { r.B = b; r.b_rs = t.pk_ldb; r.b_cs = 1; r.sB = o.sB ? o.K * t.pk_ldb : 0; }
+  if (t.pk_a) {
+    r.A = a;
+    if (t.pk_a_cm) { r.a_rs = 1; r.a_cs = t.pk_lda; r.sA = o.sA ? o.K * t.pk_lda : 0; }
+    else { r.a_rs = t.pk_lda; r.a_cs = 1; r.sA = o.sA ? o.M * t.pk_lda : 0; }
+  }
+  if (t.pk_b) {
+    r.B = b;
+    if (t.pk_b_cm) { r.b_rs = 1; r.b_cs = t.pk_ldb; r.sB = o.sB ? o.N * t.pk_ldb : 0; }
+    else { r.b_rs = t.pk_ldb; r.b_cs = 1; r.sB = o.sB ? o.K * t.pk_ldb : 0; }
+  }
   return r;
 }
 
@@ -506,16 +515,19 @@ bool plan_packed(const Op &o, int sms, const mb_gemm_desc *d, bool have_ws, Plan
   t.pk_a = !operand_tma_ok(o.A, o.M, o.K, o.a_rs, o.a_cs, o.sA, o.batch, esz);
   t.pk_b = !operand_tma_ok(o.B, o.K, o.N, o.b_rs, o.b_cs, o.sB, o.batch, esz);
   if (!t.pk_a && !t.pk_b) return false;
-  t.pk_lda = round_up(o.K, 16 / esz);
-  t.pk_ldb = round_up(o.N, 16 / esz);
+  // keep the source's contiguous direction so the copy reads and writes rows
+  t.pk_a_cm = o.a_rs == 1 && o.a_cs != 1;
+  t.pk_b_cm = o.b_rs == 1 && o.b_cs != 1;
+  t.pk_lda = round_up(t.pk_a_cm ? o.M : o.K, 16 / esz);
+  t.pk_ldb = round_up(t.pk_b_cm ? o.K : o.N, 16 / esz);
   t.pk_a_batches = o.sA ? o.batch : 1;
   t.pk_b_batches = o.sB ? o.batch : 1;
   const void *ph = reinterpret_cast<const void *>(uintptr_t(1) << 20);  // aligned placeholder
   const Op r = packed_op(o, t, ph, ph);
   if (!plan_tc_any(r, sms, d, have_ws, t)) return false;
   const int64_t base = std::max<int64_t>(t.ws_bytes, kTicketBytes);
-  const int64_t a_bytes = t.pk_a ? t.pk_a_batches * o.M * t.pk_lda * esz : 0;
-  const int64_t b_bytes = t.pk_b ? t.pk_b_batches * o.K * t.pk_ldb * esz : 0;
+  const int64_t a_bytes = t.pk_a ? t.pk_a_batches * (t.pk_a_cm ? o.K : o.M) * t.pk_lda * esz : 0;
+  const int64_t b_bytes = t.pk_b ? t.pk_b_batches * (t.pk_b_cm ? o.N : o.K) * t.pk_ldb * esz : 0;
   t.pk_a_off = round_up(base, 256);
   t.pk_b_off = round_up(t.pk_a_off + a_bytes, 256);
   t.ws_bytes = t.pk_b_off + b_bytes;
@@ -931,14 +943,27 @@ int launch_packed(const Op &o, const Plan &pl, const EpiScalars &e, void *ws, in
   auto pack = [&](const void *src, void *dst, int64_t rows, int64_t cols, int64_t rs, int64_t cs, int64_t bs,
                   int64_t batches, int64_t ld, const char *what) {
     PackArgs a{src, dst, rows, cols, rs, cs, bs, batches, ld};
-    const int64_t n = batches * rows * cols;
-    pack_matrix_kernel<U><<<(unsigned)std::max<int64_t>(1, std::min<int64_t>(ceil_div(n, 256), grid_cap)), 256, 0,
-                            st>>>(a);
+    if (cs == 1) {
+      const int64_t n = batches * rows * ceil_div(cols, 16 / (int64_t)sizeof(U));
+      pack_rows16_kernel<U><<<(unsigned)std::max<int64_t>(1, std::min<int64_t>(ceil_div(n, 256), grid_cap)), 256, 0,
+                              st>>>(a);
+    } else {
+      const int64_t n = batches * rows * cols;
+      pack_matrix_kernel<U><<<(unsigned)std::max<int64_t>(1, std::min<int64_t>(ceil_div(n, 256), grid_cap)), 256, 0,
+                              st>>>(a);
+    }
     return cuda_check(cudaGetLastError(), what);
   };
   int rc = MB_OK;
-  if (pl.pk_a) rc = pack(o.A, ap, o.M, o.K, o.a_rs, o.a_cs, o.sA, pl.pk_a_batches, pl.pk_lda, "pack A");
-  if (!rc && pl.pk_b) rc = pack(o.B, bp, o.K, o.N, o.b_rs, o.b_cs, o.sB, pl.pk_b_batches, pl.pk_ldb, "pack B");
+  // a column-major source is copied as the rows of its transpose
+  if (pl.pk_a) {
+    rc = pl.pk_a_cm ? pack(o.A, ap, o.K, o.M, o.a_cs, o.a_rs, o.sA, pl.pk_a_batches, pl.pk_lda, "pack A")
+                    : pack(o.A, ap, o.M, o.K, o.a_rs, o.a_cs, o.sA, pl.pk_a_batches, pl.pk_lda, "pack A");
+  }
+  if (!rc && pl.pk_b) {
+    rc = pl.pk_b_cm ? pack(o.B, bp, o.N, o.K, o.b_cs, o.b_rs, o.sB, pl.pk_b_batches, pl.pk_ldb, "pack B")
+                    : pack(o.B, bp, o.K, o.N, o.b_rs, o.b_cs, o.sB, pl.pk_b_batches, pl.pk_ldb, "pack B");
+  }
   if (rc) return rc;
   const Op r = packed_op(o, pl, ap, bp);
   return launch_tc<T>(pl.swap ? swapped(r) : r, pl, e, ws, sms, st);
