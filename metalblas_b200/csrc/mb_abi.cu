@@ -172,7 +172,7 @@ constexpr int kGemvWarps = 8;         // warps per GEMV CTA
 constexpr int kGemvRowsPerWarp = 2;   // staged-x rows kernel
 constexpr int64_t kGemvRowsPerCta = kGemvWarps * kGemvRowsPerWarp;
 
-enum PlanKind { PK_EMPTY = 0, PK_GEMV_COLS, PK_GEMV_ROWS, PK_TC, PK_SIMT, PK_TC_C32, PK_TC_PACKED };
+enum PlanKind { PK_EMPTY = 0, PK_GEMV_COLS, PK_GEMV_ROWS, PK_TC, PK_SIMT, PK_TC_C32, PK_TC_PACKED, PK_TC_3XTF32 };
 
 struct Plan {
   int kind = PK_EMPTY;
@@ -199,6 +199,10 @@ struct Plan {
   int pk_a = 0, pk_b = 0;
   int pk_a_cm = 0, pk_b_cm = 0;  // packed column-major (source column-contiguous): a plain strided copy
   int64_t pk_lda = 0, pk_ldb = 0, pk_a_off = 0, pk_b_off = 0, pk_a_batches = 1, pk_b_batches = 1;
+  // PK_TC_3XTF32: fp32 split into tf32 high / low parts, both operands K-major
+  // in the workspace (A' M x ldk, B'ᵀ N x ldk)
+  int64_t x3_ldk = 0, x3_a_batches = 1, x3_b_batches = 1;
+  int64_t x3_ahi = 0, x3_alo = 0, x3_bhi = 0, x3_blo = 0, x3_flag = 0;
   // shared
   int64_t ws_bytes = 0;
   std::string why;
@@ -209,6 +213,7 @@ struct Op {
   int dt;
   int64_t M, N, K, batch;
   const void *A, *B;
+  const void *A2 = nullptr, *B2 = nullptr;  // 3xTF32: low parts, laid out like A / B
   void *C;
   int64_t a_rs, a_cs, sA, b_rs, b_cs, sB, c_rs, c_cs, sC;
   int conj_a, conj_b;
@@ -235,6 +240,7 @@ Op swapped(const Op &o) {
   Op s = o;
   s.M = o.N; s.N = o.M;
   s.A = o.B; s.B = o.A;
+  s.A2 = o.B2; s.B2 = o.A2;
   s.a_rs = o.b_cs; s.a_cs = o.b_rs; s.sA = o.sB;
   s.b_rs = o.a_cs; s.b_cs = o.a_rs; s.sB = o.sA;
   s.c_rs = o.c_cs; s.c_cs = o.c_rs;
@@ -298,6 +304,13 @@ void choose_tc_tile(const Op &o, int sms, int force_bn, int force_split, int for
                     Plan &pl) {
   const int esz = elem_size(o.dt);
   const int64_t BK = 128 / esz;
+  // fp32 runs as 3xTF32: three tf32 MMAs (half the bf16 rate) per K-block and
+  // twice the operand bytes (high and low parts)
+  const bool s3 = o.dt == MB_F32;
+  auto kbc = [&](int bn) { return s3 ? std::max(6.0 * bn, 2.0 * (128.0 + bn) * 128.0 / 45.0) : kblock_cycles(bn); };
+  auto kbcp = [&](int bn) {
+    return s3 ? std::max(6.0 * bn, 2.0 * (128.0 + bn / 2.0) * 128.0 / 35.0) : kblock_cycles_pair(bn);
+  };
   const int64_t kb_total = ceil_div(o.K, BK);
   static const int bns[] = {16, 32, 64, 128, 256};
   double best = 1e300;
@@ -325,11 +338,12 @@ void choose_tc_tile(const Op &o, int sms, int force_bn, int force_split, int for
   };
   for (int bn : bns) {
     if (force_bn && bn != force_bn) continue;
+    if (s3 && bn > 128) continue;  // 3xTF32: see launch_tc<float>
     int am, bm;
     if (!tc_layout_ok(o, bn, am, bm, nullptr)) continue;
     if (!force_bn && bn > 16 && round_up(o.N, 16) <= bn / 2) continue;  // a smaller tile already covers N
     const int64_t tiles = o.batch * ceil_div(o.M, 128) * ceil_div(o.N, bn);
-    const double unit_full = kb_total * kblock_cycles(bn) + 4.0 * bn;
+    const double unit_full = kb_total * kbc(bn) + 4.0 * bn;
     if ((!force_split || force_split == 1) && force_pair != 2 && force_sk != 2) {
       // whole tiles
       const int64_t w = ceil_div(tiles, sms);
@@ -339,7 +353,7 @@ void choose_tc_tile(const Op &o, int sms, int force_bn, int force_split, int for
       if (half_ok && tiles > sms && tiles % sms) {
         const int64_t dp = (tiles / sms) * sms;
         const int64_t tail_units = 2 * (tiles - dp);
-        const double unit_half = kb_total * kblock_cycles(bn / 2) + 2.0 * bn;
+        const double unit_half = kb_total * kbc(bn / 2) + 2.0 * bn;
         const double waves = (double)(dp / sms + ceil_div(tail_units, sms));
         consider((dp / sms) * unit_full + ceil_div(tail_units, sms) * unit_half, (double)(dp + tail_units), waves,
                  0.0, bn, am, bm, 1, kb_total, dp, 1);
@@ -350,18 +364,18 @@ void choose_tc_tile(const Op &o, int sms, int force_bn, int force_split, int for
     const bool pair_fits = !bm || (bn / 2) * esz >= 128;
     // Pairs pay a cross-CTA handshake per tile (both epilogues must drain an
     // accumulator before the next MMA): only worth it with enough K per tile.
-    const bool want_pair = force_pair == 2 || (force_pair == 0 && g_pair_enabled && o.M > 128 && kb_total >= 8);
+    const bool want_pair = !s3 && (force_pair == 2 || (force_pair == 0 && g_pair_enabled && o.M > 128 && kb_total >= 8));
     if ((bn == 128 || bn == 256) && pair_fits && want_pair && (!force_split || force_split == 1) && force_sk != 2) {
       const int pairs = sms / 2;
       const int64_t ptiles = o.batch * ceil_div(o.M, 256) * ceil_div(o.N, bn);
-      const double punit = kb_total * kblock_cycles_pair(bn) + 4.0 * bn;
+      const double punit = kb_total * kbcp(bn) + 4.0 * bn;
       const int64_t w = ceil_div(ptiles, pairs);
       consider(w * punit, (double)ptiles * 2, (double)w, 0.0, bn, am, bm, 1, kb_total, ptiles, 0, 2);
       const bool half_ok = bn == 256 && bm && (bn / 4) * esz >= 128;
       if (half_ok && ptiles > pairs && ptiles % pairs) {
         const int64_t dp = (ptiles / pairs) * pairs;
         const int64_t tail_units = 2 * (ptiles - dp);
-        const double phalf = kb_total * kblock_cycles_pair(bn / 2) + 2.0 * bn;
+        const double phalf = kb_total * kbcp(bn / 2) + 2.0 * bn;
         const double waves = (double)(dp / pairs + ceil_div(tail_units, pairs));
         consider((dp / pairs) * punit + ceil_div(tail_units, pairs) * phalf, (double)(dp + tail_units) * 2, waves,
                  0.0, bn, am, bm, 1, kb_total, dp, 1, 2);
@@ -376,7 +390,7 @@ void choose_tc_tile(const Op &o, int sms, int force_bn, int force_split, int for
       if (iters >= 4 * (int64_t)sms || (force_sk == 2 && iters >= sms)) {
         const int maxp = sk_max_parts(tail, kb_total, sms);
         if (tail * tc::NUM_EPI_WARPS <= kMaxTickets) {
-          const double share = (double)ceil_div(iters, sms) * kblock_cycles(bn);
+          const double share = (double)ceil_div(iters, sms) * kbc(bn);
           // the fixup: the last piece of a tile re-reads every partial of it
           const double fix = maxp > 1 ? 8.0 * 4.0 * bn + 8.0 * maxp * bn : 4.0 * bn;
           const double extra = maxp > 1 ? (double)tail * maxp * 128.0 * bn * 8.0 : 0.0;
@@ -397,7 +411,7 @@ void choose_tc_tile(const Op &o, int sms, int force_bn, int force_split, int for
       // a split unit writes 128 x BN fp32 partials and the last warp to arrive
       // re-reads all of them before the epilogue: measured far costlier than a
       // whole-tile epilogue, so it is charged per split and per column
-      const double unit_split = kbp * kblock_cycles(bn) + 4.0 * bn + 16.0 * seff * bn;
+      const double unit_split = kbp * kbc(bn) + 4.0 * bn + 16.0 * seff * bn;
       const int64_t units = tiles * seff;
       const int64_t w = ceil_div(units, sms);
       consider(w * unit_split, (double)units, (double)w, (double)tiles * seff * 128.0 * bn * 8.0, bn, am, bm,
@@ -536,6 +550,48 @@ bool plan_packed(const Op &o, int sms, const mb_gemm_desc *d, bool have_ws, Plan
   return true;
 }
 
+// fp32 on the tensor cores as 3xTF32 (METALBLAS_FP32_TF32X3=0 keeps every fp32
+// product on the CUDA-core FFMA kernel).  The split operands live in the
+// workspace, K-major: A' = [batch][M][ldk], B'ᵀ = [batch][N][ldk].
+const bool g_fp32_tf32x3 = [] {
+  const char *s = getenv("METALBLAS_FP32_TF32X3");
+  return !(s && s[0] == '0');
+}();
+
+Op x3_op(const Op &o, const Plan &t, const void *ahi, const void *alo, const void *bhi, const void *blo) {
+  Op r = o;
+  r.A = ahi; r.A2 = alo; r.a_rs = t.x3_ldk; r.a_cs = 1; r.sA = o.sA ? o.M * t.x3_ldk : 0;
+  r.B = bhi; r.B2 = blo; r.b_rs = 1; r.b_cs = t.x3_ldk; r.sB = o.sB ? o.N * t.x3_ldk : 0;
+  return r;
+}
+
+bool plan_3xtf32(const Op &o, int sms, const mb_gemm_desc *d, bool have_ws, Plan &pl) {
+  if (o.dt != MB_F32 || !have_ws || o.M < 1 || o.N < 1 || o.K < 1) return false;
+  if (o.M >= (1ll << 31) || o.N >= (1ll << 31) || o.K >= (1ll << 31)) return false;
+  // A product with non-finite inputs is recomputed on the CUDA cores after the
+  // tensor-core pass, which must then still see the original bias: an epilogue
+  // whose bias is the output itself runs on the CUDA cores from the start.
+  if (d->epilogue && d->beta_nz && d->bias == d->C) return false;
+  Plan t;
+  t.x3_ldk = round_up(o.K, 4);
+  t.x3_a_batches = o.sA ? o.batch : 1;
+  t.x3_b_batches = o.sB ? o.batch : 1;
+  const void *ph = reinterpret_cast<const void *>(uintptr_t(1) << 20);  // aligned placeholder
+  if (!plan_tc_any(x3_op(o, t, ph, ph, ph, ph), sms, d, have_ws, t)) return false;
+  if (t.a_mn || t.b_mn) return false;
+  const int64_t base = std::max<int64_t>(t.ws_bytes, kTicketBytes);
+  const int64_t a_bytes = t.x3_a_batches * o.M * t.x3_ldk * 4, b_bytes = t.x3_b_batches * o.N * t.x3_ldk * 4;
+  t.x3_ahi = round_up(base, 256);
+  t.x3_alo = round_up(t.x3_ahi + a_bytes, 256);
+  t.x3_bhi = round_up(t.x3_alo + a_bytes, 256);
+  t.x3_blo = round_up(t.x3_bhi + b_bytes, 256);
+  t.x3_flag = round_up(t.x3_blo + b_bytes, 256);
+  t.ws_bytes = t.x3_flag + 256;
+  t.kind = PK_TC_3XTF32;
+  pl = t;
+  return true;
+}
+
 bool plan_gemv(const Op &o, int sms, const mb_gemm_desc *d, bool have_ws, Plan &pl) {
   GemvParams g{};
   int kind = 0;
@@ -628,7 +684,11 @@ int make_plan(const mb_gemm_desc *d, const Op &o, int sms, bool have_ws, Plan &p
     return fail(MB_ERR_UNSUPPORTED, "tensor-core complex32 needs a row-major output and a workspace");
   }
   if (be == MB_BACKEND_TC) {
-    if (!is_tc_dtype(o.dt)) return fail(MB_ERR_UNSUPPORTED, "tensor-core backend supports bf16/fp16/int8/uint8 only");
+    if (o.dt == MB_F32) {  // fp32 on the tensor cores is 3xTF32
+      if (plan_3xtf32(o, sms, d, have_ws, pl)) return MB_OK;
+      return fail(MB_ERR_UNSUPPORTED, "tensor-core fp32 (3xTF32) needs a workspace for the split operands");
+    }
+    if (!is_tc_dtype(o.dt)) return fail(MB_ERR_UNSUPPORTED, "tensor-core backend supports bf16/fp16/fp32/int8/uint8 only");
     if (plan_tc_any(o, sms, d, have_ws, pl)) return MB_OK;
     if (plan_packed(o, sms, d, have_ws, pl)) return MB_OK;
     return fail(MB_ERR_UNSUPPORTED, "tensor-core backend: operands not TMA-addressable (need a unit stride, "
@@ -637,6 +697,20 @@ int make_plan(const mb_gemm_desc *d, const Op &o, int sms, bool have_ws, Plan &p
   // AUTO
   if ((o.M == 1 || o.N == 1) && plan_gemv(o, sms, d, have_ws, pl)) return MB_OK;
   if (o.dt == MB_C32 && plan_c32(o, sms, d, have_ws, pl)) return MB_OK;
+  // fp32: 3xTF32 on the tensor cores when its estimated time beats the CUDA-core
+  // kernel's.  3xTF32: the split pass moves 12 bytes per operand element and the
+  // GEMM reads 8, at ~6 TB/s, plus the FLOPs at ~190 TFLOP/s and ~6 us of extra
+  // launches.  FFMA: ~40 TFLOP/s when its 128 x 128 tiles fill two CTAs per SM,
+  // proportionally less when they do not (it has no split-K).
+  if (o.dt == MB_F32 && g_fp32_tf32x3 && o.M >= 16 && o.N >= 16) {
+    const double bt = (double)std::max<int64_t>(o.batch, 1);
+    const double flops = 2.0 * o.M * o.N * o.K * bt;
+    const double opnd = (double)o.M * o.K * (o.sA ? bt : 1.0) + (double)o.K * o.N * (o.sB ? bt : 1.0);
+    const double ctas = (double)ceil_div(o.M, 128) * ceil_div(o.N, 128) * bt;
+    const double t_simt = flops / (40.0e12 * std::min(1.0, ctas / (2.0 * sms)));
+    const double t_x3 = 20.0 * 4.0 * opnd / 6.0e12 + flops / 190.0e12 + 6.0e-6;
+    if (t_x3 < t_simt && plan_3xtf32(o, sms, d, have_ws, pl)) return MB_OK;
+  }
   if (is_tc_dtype(o.dt)) {
     if (plan_tc_any(o, sms, d, have_ws, pl)) return MB_OK;
     // worth a copy when the product is large enough for the tensor cores to
@@ -690,8 +764,9 @@ EpiScalars make_epi(const mb_gemm_desc *d) {
 
 // --------------------------------------------------------------------------- launches
 template <class T>
-int launch_simt(const Op &o, const EpiScalars &e, cudaStream_t st) {
+int launch_simt(const Op &o, const EpiScalars &e, cudaStream_t st, const int *gate = nullptr) {
   SimtParams p{};
+  p.gate = gate;
   p.A = o.A; p.B = o.B; p.C = o.C; p.bias = o.bias;
   p.M = o.M; p.N = o.N; p.K = o.K; p.batch = o.batch;
   p.a_rs = o.a_rs; p.a_cs = o.a_cs; p.sA = o.sA;
@@ -778,6 +853,7 @@ CUtensorMapDataType tma_dtype(int dt) {
   switch (dt) {
     case MB_BF16: return CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
     case MB_F16: return CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    case MB_F32: return CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
     default: return CU_TENSOR_MAP_DATA_TYPE_UINT8;
   }
 }
@@ -818,6 +894,13 @@ int launch_tc_bn(const Op &o, const Plan &pl, const EpiScalars &e, void *ws, int
   if (!pl.b_mn) rc = encode_map(&p.tmB, o.dt, o.B, o.K, o.N, bB, o.b_cs, o.sB, BK, BN / PAIR);
   else rc = encode_map(&p.tmB, o.dt, o.B, o.N, o.K, bB, o.b_rs, o.sB, 128 / ESZ, BK);
   if (rc) return rc;
+  if constexpr (C_::NPART == 2) {
+    // 3xTF32 low parts: K-major like the high parts
+    if (pl.a_mn || pl.b_mn || !o.A2 || !o.B2) return fail(MB_ERR_INVALID, "3xTF32 operands must be K-major");
+    rc = encode_map(&p.tmA2, o.dt, o.A2, o.K, o.M, bA, o.a_rs, o.sA, BK, tc::BM);
+    if (!rc) rc = encode_map(&p.tmB2, o.dt, o.B2, o.K, o.N, bB, o.b_cs, o.sB, BK, BN / PAIR);
+    if (rc) return rc;
+  }
   p.M = (int)o.M; p.N = (int)o.N; p.K = (int)o.K; p.batch = (int)o.batch;
   p.a_mn = pl.a_mn; p.b_mn = pl.b_mn;
   p.a_bcast = o.sA == 0; p.b_bcast = o.sB == 0;
@@ -888,6 +971,16 @@ int launch_tc_bn(const Op &o, const Plan &pl, const EpiScalars &e, void *ws, int
 
 template <class T>
 int launch_tc(const Op &o, const Plan &pl, const EpiScalars &e, void *ws, int sms, cudaStream_t st) {
+  if constexpr (std::is_same_v<T, float>) {
+    // 3xTF32 keeps BN/2 fp32 running sums per epilogue thread: single-CTA tiles, BN <= 128
+    switch (pl.pair == 1 ? pl.bn : 0) {
+      case 16: return launch_tc_bn<T, 16, 1>(o, pl, e, ws, sms, st);
+      case 32: return launch_tc_bn<T, 32, 1>(o, pl, e, ws, sms, st);
+      case 64: return launch_tc_bn<T, 64, 1>(o, pl, e, ws, sms, st);
+      case 128: return launch_tc_bn<T, 128, 1>(o, pl, e, ws, sms, st);
+    }
+    return fail(MB_ERR_INVALID, "3xTF32 plan with tile_n %d pair %d", pl.bn, pl.pair);
+  } else {
   if (pl.pair == 2) {
     switch (pl.bn) {
       case 128: return launch_tc_bn<T, 128, 2>(o, pl, e, ws, sms, st);
@@ -903,6 +996,7 @@ int launch_tc(const Op &o, const Plan &pl, const EpiScalars &e, void *ws, int sm
     case 256: return launch_tc_bn<T, 256, 1>(o, pl, e, ws, sms, st);
   }
   return fail(MB_ERR_INVALID, "bad tile_n %d", pl.bn);
+  }
 }
 
 // complex32 on the tensor cores: build B' (and A' when A is not row-major),
@@ -967,6 +1061,32 @@ int launch_packed(const Op &o, const Plan &pl, const EpiScalars &e, void *ws, in
   if (rc) return rc;
   const Op r = packed_op(o, pl, ap, bp);
   return launch_tc<T>(pl.swap ? swapped(r) : r, pl, e, ws, sms, st);
+}
+
+int launch_3xtf32(const Op &o, const Plan &pl, const EpiScalars &e, void *ws, int sms, cudaStream_t st) {
+  char *w = reinterpret_cast<char *>(ws);
+  float *ahi = reinterpret_cast<float *>(w + pl.x3_ahi), *alo = reinterpret_cast<float *>(w + pl.x3_alo);
+  float *bhi = reinterpret_cast<float *>(w + pl.x3_bhi), *blo = reinterpret_cast<float *>(w + pl.x3_blo);
+  int *flag = reinterpret_cast<int *>(w + pl.x3_flag);
+  int rc = cuda_check(cudaMemsetAsync(flag, 0, sizeof(int), st), "3xTF32 clear flag");
+  if (rc) return rc;
+  auto split = [&](const void *src, float *hi, float *lo, int64_t rows, int64_t cols, int64_t rs, int64_t cs,
+                   int64_t bs, int64_t batches, const char *what) {
+    SplitArgs a{static_cast<const float *>(src), hi, lo, flag, rows, cols, rs, cs, bs, batches, pl.x3_ldk};
+    const int64_t tiles = batches * ceil_div(rows, 32) * ceil_div(cols, 32);
+    split_tf32_kernel<<<(unsigned)std::max<int64_t>(1, std::min<int64_t>(tiles, (int64_t)sms * 16)), dim3(32, 8), 0,
+                        st>>>(a);
+    return cuda_check(cudaGetLastError(), what);
+  };
+  // A (M x K) and Bᵀ (N x K, element (n, k) = B(k, n))
+  rc = split(o.A, ahi, alo, o.M, o.K, o.a_rs, o.a_cs, o.sA, pl.x3_a_batches, "3xTF32 split A");
+  if (!rc) rc = split(o.B, bhi, blo, o.N, o.K, o.b_cs, o.b_rs, o.sB, pl.x3_b_batches, "3xTF32 split B");
+  if (rc) return rc;
+  const Op r = x3_op(o, pl, ahi, alo, bhi, blo);
+  rc = launch_tc<float>(pl.swap ? swapped(r) : r, pl, e, ws, sms, st);
+  if (rc) return rc;
+  // inf / NaN in an input: FFMA recomputes the product (its CTAs exit at once otherwise)
+  return launch_simt<float>(o, e, st, flag);
 }
 
 template <class F>
@@ -1070,6 +1190,11 @@ int mb_plan_query(const mb_gemm_desc *d, char *buf, int buflen) {
       snprintf(tmp, sizeof(tmp), "tc_c32 pack_a=%d bn=%d split=%d pair=%d tiles=%lldx%lld ws=%lld", pl.c32_pack_a,
                pl.bn, pl.splits, pl.pair, (long long)pl.tiles_m, (long long)pl.tiles_n, (long long)pl.ws_bytes);
       break;
+    case PK_TC_3XTF32:
+      snprintf(tmp, sizeof(tmp), "tc_3xtf32 bn=%d split=%d dp=%lld half=%d pair=%d sk=%d swap=%d tiles=%lldx%lld ws=%lld",
+               pl.bn, pl.splits, (long long)pl.dp_tiles, pl.tail_half, pl.pair, pl.sk, pl.swap, (long long)pl.tiles_m,
+               (long long)pl.tiles_n, (long long)pl.ws_bytes);
+      break;
     case PK_TC_PACKED:
       snprintf(tmp, sizeof(tmp), "tc_packed pack_a=%d pack_b=%d bn=%d split=%d pair=%d sk=%d swap=%d tiles=%lldx%lld ws=%lld",
                pl.pk_a, pl.pk_b, pl.bn, pl.splits, pl.pair, pl.sk, pl.swap, (long long)pl.tiles_m,
@@ -1106,6 +1231,9 @@ int mb_gemm(const mb_gemm_desc *d, void *stream) {
       case PK_TC_PACKED:
         if constexpr (IsTc<T>::v) return launch_packed<T>(o, pl, e, d->workspace, sms, st);
         else return fail(MB_ERR_UNSUPPORTED, "tensor-core path for non-TC dtype");
+      case PK_TC_3XTF32:
+        if constexpr (std::is_same_v<T, float>) return launch_3xtf32(o, pl, e, d->workspace, sms, st);
+        else return fail(MB_ERR_UNSUPPORTED, "3xTF32 path for a non-fp32 dtype");
       default: return launch_simt<T>(o, e, st);
     }
   });
@@ -1273,7 +1401,8 @@ int mb_gemm_noalloc(const mb_gemm_desc *d, void *stream) {
   int rc = plan_for(&q, pl, o, sms);
   if (rc) return rc;
   if (pl.kind == PK_EMPTY) return MB_OK;
-  if ((pl.kind == PK_TC_C32 || pl.kind == PK_TC_PACKED) && pl.ws_bytes > (int64_t)MB_NOALLOC_SCRATCH_BYTES &&
+  if ((pl.kind == PK_TC_C32 || pl.kind == PK_TC_PACKED || pl.kind == PK_TC_3XTF32) &&
+      pl.ws_bytes > (int64_t)MB_NOALLOC_SCRATCH_BYTES &&
       q.backend == MB_BACKEND_AUTO) {
     // complex32 on the tensor cores needs its expanded B' in scratch, packed
     // operands their copies; when they do not fit, the CUDA-core kernel (no
@@ -1308,6 +1437,9 @@ int mb_gemm_noalloc(const mb_gemm_desc *d, void *stream) {
       case PK_TC_PACKED:
         if constexpr (IsTc<T>::v) return launch_packed<T>(o, pl, e, scratch, sms, st);
         else return fail(MB_ERR_UNSUPPORTED, "tensor-core path for non-TC dtype");
+      case PK_TC_3XTF32:
+        if constexpr (std::is_same_v<T, float>) return launch_3xtf32(o, pl, e, scratch, sms, st);
+        else return fail(MB_ERR_UNSUPPORTED, "3xTF32 path for a non-fp32 dtype");
       default: return launch_simt<T>(o, e, st);
     }
   });

@@ -61,3 +61,74 @@ __global__ void __launch_bounds__(256) pack_rows16_kernel(const PackArgs a) {
 }
 
 }  // namespace mb
+
+namespace mb {
+
+// fp32 -> 3xTF32 operand split for the tensor cores: x = hi + lo + r with
+// hi = x rounded to tf32 (nearest, ties away; cvt.rna), lo = (x - hi) rounded to
+// tf32, |r| <= 2^-22 |x|.  Products hi*hi + hi*lo + lo*hi then reproduce x*y to
+// about 2^-21 relative, inside the fp32 tolerance of the reference's tests.
+// Non-finite x keep hi = x and lo = 0, and the split reports them: the cross
+// terms inf * lo can turn into NaN where FFMA gives inf, so the caller then
+// recomputes that product on the CUDA cores.  A finite x that rounds up to inf
+// is truncated instead.
+__device__ __forceinline__ float tf32_rna(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+__device__ __forceinline__ void tf32_split(float x, float &hi, float &lo) {
+  if (!isfinite(x)) { hi = x; lo = 0.f; return; }
+  hi = tf32_rna(x);
+  if (isinf(hi)) hi = __uint_as_float(__float_as_uint(x) & 0xffffe000u);
+  lo = tf32_rna(x - hi);
+}
+
+struct SplitArgs {
+  const float *src;
+  float *hi, *lo;
+  int *nonfinite;       // set to 1 when any input value is inf or NaN
+  int64_t rows, cols;   // output rows x cols (cols is the K dimension)
+  int64_t rs, cs, bs;   // source strides of element (row, col) and batch
+  int64_t batch, ld;    // batches; destination row pitch (elements, 16-byte multiple)
+};
+
+// dst[b][r][c] = split(src(b, r, c)) through a 32 x 32 shared-memory tile, so
+// both the source read (along whichever of r / c is contiguous) and the
+// destination rows are coalesced.  Block 32 x 8, grid-stride over tiles.
+__global__ void __launch_bounds__(256) split_tf32_kernel(const SplitArgs a) {
+  __shared__ float tile[32][33];
+  const int tx = threadIdx.x, ty = threadIdx.y;
+  const int64_t rt = (a.rows + 31) / 32, ct = (a.cols + 31) / 32;
+  const int64_t tiles = a.batch * rt * ct;
+  const bool c_fast = a.cs == 1 || (a.rs != 1 && (a.cs < 0 ? -a.cs : a.cs) <= (a.rs < 0 ? -a.rs : a.rs));
+  for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
+    const int64_t b = t / (rt * ct);
+    const int64_t rem = t - b * rt * ct;
+    const int64_t r0 = (rem / ct) * 32, c0 = (rem % ct) * 32;
+    const float *src = a.src + b * a.bs;
+#pragma unroll
+    for (int i = ty; i < 32; i += 8) {
+      const int64_t r = r0 + (c_fast ? i : tx), c = c0 + (c_fast ? tx : i);
+      const float v = (r < a.rows && c < a.cols) ? src[r * a.rs + c * a.cs] : 0.f;
+      if (c_fast) tile[i][tx] = v; else tile[tx][i] = v;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = ty; i < 32; i += 8) {
+      const int64_t r = r0 + i, c = c0 + tx;
+      if (r < a.rows && c < a.cols) {
+        float hi, lo;
+        const float x = tile[i][tx];
+        if (!isfinite(x)) *a.nonfinite = 1;
+        tf32_split(x, hi, lo);
+        const int64_t o = (b * a.rows + r) * a.ld + c;
+        a.hi[o] = hi;
+        a.lo[o] = lo;
+      }
+    }
+    __syncthreads();
+  }
+}
+
+}  // namespace mb

@@ -36,6 +36,7 @@ struct SimtParams {
   int conj_a, conj_b;
   int a_vec, b_vec;  // 4-element runs along the contiguous dimension are aligned vectors
   EpiScalars epi;
+  const int *gate;   // non-null: the kernel runs only if *gate != 0 (set on the device)
 };
 
 // Four consecutive elements from an address aligned to 4 * sizeof(T).
@@ -94,6 +95,7 @@ __global__ void __launch_bounds__(256, 2) simt_gemm_kernel(const SimtParams p) {
   __shared__ __align__(16) Acc As[2][BK][BM + PAD];
   __shared__ __align__(16) Acc Bs[2][BK][BN + PAD];
 
+  if (p.gate != nullptr && *reinterpret_cast<const volatile int *>(p.gate) == 0) return;  // uniform per CTA
   const int tid = threadIdx.x;
   const int tx = tid % TX, ty = tid / TX;
   const int64_t m0 = (int64_t)blockIdx.y * BM, n0 = (int64_t)blockIdx.x * BN;

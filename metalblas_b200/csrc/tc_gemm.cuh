@@ -68,6 +68,8 @@ constexpr int STAGING_PER_WARP = 2 * STAGING_BUF;  // double-buffered
 struct TcParams {
   CUtensorMap tmA;   // UMMA-A operand (rows of C), 3-D {inner, outer, batch}
   CUtensorMap tmB;   // UMMA-B operand (cols of C)
+  CUtensorMap tmA2;  // fp32 (3xTF32): the low tf32 parts of A and B, same geometry
+  CUtensorMap tmB2;
   CUtensorMap tmC;   // output, 3-D {N, M, batch}, box {64 B, 32 rows}, SWIZZLE_64B; valid when c_tma
   int M, N, K, batch;
   int a_mn, b_mn;        // operand is MN-major in global memory
@@ -98,11 +100,20 @@ struct Cfg {
   static constexpr int KSTEPS = BK / UMMA_K;    // 4
   static constexpr int A_BYTES = BM * 128;
   static constexpr int B_BYTES = (BN / PAIR) * 128;  // this CTA's share of B's columns
-  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  // fp32 runs as 3xTF32: each stage holds the high and the low tf32 parts of
+  // both operands (A_hi, A_lo, B_hi, B_lo)
+  static constexpr int NPART = ESZ == 4 ? 2 : 1;
+  // K-blocks accumulated in TMEM before the epilogue takes the sum: the tensor
+  // core's fp32 accumulation drifts over long chains, so fp32 (3xTF32) sums
+  // chunks of 16 K-blocks (512 elements of K) in registers with IEEE adds.
+  static constexpr int KCHUNK = ESZ == 4 ? 16 : (1 << 30);
+  // fp32 running sums per epilogue thread (whole-width unit: BN/2 columns)
+  static constexpr int RUN = ESZ == 4 ? BN / 2 : 1;
+  static constexpr int STAGE_BYTES = NPART * (A_BYTES + B_BYTES);
   static constexpr int HALF = BN / 2;           // columns per epilogue warp (whole-tile unit)
   static constexpr int QUART = BN / 4;          // columns per epilogue warp (half-width unit)
   static constexpr int CC = STAGING_ROW / ESZ;  // columns per staged row
-  static constexpr bool TMA_STORE = (QUART % CC) == 0;
+  static constexpr bool TMA_STORE = ESZ <= 2 && (QUART % CC) == 0;  // fp32 outputs: direct stores
   static constexpr int STAGING_BYTES = TMA_STORE ? NUM_EPI_WARPS * STAGING_PER_WARP : 0;
   static constexpr int BAR_BYTES = 256;
   static constexpr int STAGES_RAW = (SMEM_LIMIT - 1024 - STAGING_BYTES - BAR_BYTES) / STAGE_BYTES;
@@ -110,9 +121,9 @@ struct Cfg {
   static constexpr int ACC_COLS = BN;           // fp32/s32: one column per N
   static constexpr int TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
   static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + STAGING_BYTES + BAR_BYTES;
-  // columns per tcgen05.ld on the direct-store and split-K paths (16 for 16-bit
-  // outputs keeps the epilogue within the register budget of 320 threads)
-  static constexpr int RCH = QUART < (ESZ == 2 ? 16 : 32) ? (QUART < 8 ? 8 : QUART) : (ESZ == 2 ? 16 : 32);
+  // columns per tcgen05.ld on the direct-store and split-K paths (16 for 16- and
+  // 32-bit outputs keeps the epilogue within the register budget of 320 threads)
+  static constexpr int RCH = QUART < (ESZ >= 2 ? 16 : 32) ? (QUART < 8 ? 8 : QUART) : (ESZ >= 2 ? 16 : 32);
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N for M=128");
   static_assert(STAGES >= 2, "need a pipeline");
   static_assert(SMEM_BYTES <= SMEM_LIMIT, "shared memory");
@@ -204,7 +215,13 @@ __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::
 
 template <int ESZ>
 __device__ __forceinline__ void umma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accum) {
-  if constexpr (ESZ == 2) {
+  if constexpr (ESZ == 4) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accum)
+        : "memory");
+  } else if constexpr (ESZ == 2) {
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
@@ -316,6 +333,12 @@ __device__ __forceinline__ void umma_g(uint32_t d_tmem, uint64_t adesc, uint64_t
                                        uint32_t accum) {
   if constexpr (PAIR == 1) {
     umma<ESZ>(d_tmem, adesc, bdesc, idesc, accum);
+  } else if constexpr (ESZ == 4) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accum)
+        : "memory");
   } else if constexpr (ESZ == 2) {
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
@@ -406,6 +429,7 @@ template <> struct UFmt<__half> { static constexpr uint32_t d = 1, ab = 0; };
 template <> struct UFmt<__nv_bfloat16> { static constexpr uint32_t d = 1, ab = 1; };
 template <> struct UFmt<uint8_t> { static constexpr uint32_t d = 2, ab = 0; };
 template <> struct UFmt<int8_t> { static constexpr uint32_t d = 2, ab = 1; };
+template <> struct UFmt<float> { static constexpr uint32_t d = 1, ab = 2; };  // tf32 operands, f32 accumulator
 
 template <class T, int BN, int UM = BM>
 __device__ __forceinline__ uint32_t make_idesc(int a_mn, int b_mn) {
@@ -674,6 +698,69 @@ __device__ __forceinline__ void pack32(const TcParams &p, int b, int m, int n0, 
   for (int j = 0; j < 32 * (int)sizeof(T) / 4; ++j) pk[j] = reinterpret_cast<const uint32_t *>(out)[j];
 }
 
+// Split-K / stream-K epilogue after a warp published its partial: take a ticket
+// for (tail tile, warp); the warp that draws the last one sums every partial of
+// its 32 rows x wcols columns in K order and stores the result.
+template <class T, int BN, int RCH>
+__device__ __forceinline__ void split_finish(const TcParams &p, const Unit &w, int ew, int lane, int m, int nbase,
+                                             int wcols) {
+  const int64_t slot_words = (int64_t)BM * BN;
+  const int64_t warp_off = (int64_t)ew * 32 * wcols;
+  // Each warp owns 32 rows x wcols columns of the tile and reduces them on
+  // its own: per-(tail tile, warp) tickets, so no cross-warp barrier exists
+  // that an aborting warp could leave the others waiting at.
+  __threadfence();
+  __syncwarp();
+  unsigned tk = 0;
+  unsigned *ticket = p.tickets + (int64_t)w.tail * NUM_EPI_WARPS + ew;
+  if (lane == 0) tk = atomicAdd(ticket, 1u);
+  tk = __shfl_sync(0xffffffffu, tk, 0);
+  if (tk == (unsigned)(w.nparts - 1)) {
+    __threadfence();
+    const uint4 *base = reinterpret_cast<const uint4 *>(reinterpret_cast<const uint32_t *>(p.ws) +
+                                                        (int64_t)w.tail * p.splits * slot_words + warp_off) + lane;
+    const int64_t slot_vec = slot_words / 4;
+    constexpr int NV = RCH / 4;                  // uint4 per lane per partial and chunk
+    constexpr int PB = NV >= 8 ? 2 : (NV >= 4 ? 4 : 8);  // partials in flight: 16 loads per lane
+#pragma unroll 1
+    for (int c = 0; c < wcols; c += RCH) {
+      uint32_t r[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) r[j] = 0;
+      const uint4 *src = base + (c >> 2) * 32;
+#pragma unroll 1
+      for (int s0 = 0; s0 < w.nparts; s0 += PB) {
+        uint4 v[PB][NV];
+#pragma unroll
+        for (int b = 0; b < PB; ++b)
+#pragma unroll
+          for (int q = 0; q < NV; ++q)
+            v[b][q] = (s0 + b < w.nparts) ? __ldcg(src + (int64_t)(s0 + b) * slot_vec + q * 32) : make_uint4(0, 0, 0, 0);
+        // summed in K order: partial s0, s0+1, ...
+#pragma unroll
+        for (int b = 0; b < PB; ++b) {
+          if (s0 + b >= w.nparts) break;
+#pragma unroll
+          for (int q = 0; q < NV; ++q) {
+            const uint4 x = v[b][q];
+            if constexpr (Elem<T>::is_int) {
+              r[4 * q] += x.x; r[4 * q + 1] += x.y; r[4 * q + 2] += x.z; r[4 * q + 3] += x.w;
+            } else {
+              r[4 * q] = __float_as_uint(__uint_as_float(r[4 * q]) + __uint_as_float(x.x));
+              r[4 * q + 1] = __float_as_uint(__uint_as_float(r[4 * q + 1]) + __uint_as_float(x.y));
+              r[4 * q + 2] = __float_as_uint(__uint_as_float(r[4 * q + 2]) + __uint_as_float(x.z));
+              r[4 * q + 3] = __float_as_uint(__uint_as_float(r[4 * q + 3]) + __uint_as_float(x.w));
+            }
+          }
+        }
+      }
+      const int n0 = nbase + c;
+      if (m < p.M && n0 < p.N) store_row_chunk<T, RCH>(p, w.b, m, n0, r);
+    }
+    if (lane == 0) *ticket = 0u;
+  }
+}
+
 // ---------------------------------------------------------------------------
 template <class T, int BN, int PAIR = 1>
 __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_constant__ TcParams p) {
@@ -762,9 +849,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!wait_x(empty_bar(stage), phase ^ 1u)) goto producer_done;
           // Both CTAs' bytes of this stage are counted on the leader's full barrier.
-          if (rank == 0) mbar_arrive_expect_tx(full_bar(stage), (A_BYTES + b_bytes) * PAIR);
+          if (rank == 0) mbar_arrive_expect_tx(full_bar(stage), C_::NPART * (A_BYTES + b_bytes) * PAIR);
           const uint32_t sa = ring_u32 + stage * STAGE_BYTES;
-          const uint32_t sb = sa + A_BYTES;
+          const uint32_t sb = sa + C_::NPART * A_BYTES;
           auto load = [&](uint32_t dst, const CUtensorMap *map, int c0, int c1, int c2) {
             if constexpr (PAIR == 2) tma_load_3d_pair(dst, map, leader_full(stage), c0, c1, c2);
             else tma_load_3d(dst, map, full_bar(stage), c0, c1, c2);
@@ -779,6 +866,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
             load(sb, &p.tmB, kb * BK, w.tn * BN + (int)rank * (BN / PAIR), bb);
           } else {
             for (int j = 0; j < b_boxes; ++j) load(sb + j * (BK * 128), &p.tmB, b_col0 + j * (128 / ESZ), kb * BK, bb);
+          }
+          if constexpr (C_::NPART == 2) {  // low parts (both operands K-major)
+            load(sa + A_BYTES, &p.tmA2, kb * BK, a_row0, ba);
+            load(sb + b_bytes, &p.tmB2, kb * BK, w.tn * BN + (int)rank * (BN / PAIR), bb);
           }
           issued_stage = stage;
           issued_phase = phase;
@@ -815,28 +906,43 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
         const uint32_t idesc = w.half >= 0 ? idesc_half : idesc_full;
         // K-major B holds the whole tile: a half-width unit starts BN/2 rows in.
         const uint32_t b_off = (w.half > 0 && !p.b_mn) ? (uint32_t)(BN / 2) * 128u : 0u;
-        if (!wait_x(tempty_bar(abuf), aphase ^ 1u)) break;
-        tc_fence_after();
-        const uint32_t d_tmem = tmem_base + (uint32_t)(abuf * C_::ACC_COLS);
         bool aborted = false;
-        for (int kb = w.kb0; kb < w.kb1; ++kb) {
-          if (!wait_x(full_bar(stage), phase)) { aborted = true; break; }
+        // One TMEM accumulation per K chunk (the whole unit, except for fp32:
+        // see C_::KCHUNK); each chunk is handed to the epilogue.
+        for (int c0 = w.kb0; c0 < w.kb1 && !aborted; c0 += C_::KCHUNK) {
+          const int c1 = min(w.kb1, c0 + C_::KCHUNK);
+          if (!wait_x(tempty_bar(abuf), aphase ^ 1u)) { aborted = true; break; }
           tc_fence_after();
-          const uint32_t sa = ring_u32 + stage * STAGE_BYTES;
-          const uint32_t sb = sa + A_BYTES + b_off;
+          const uint32_t d_tmem = tmem_base + (uint32_t)(abuf * C_::ACC_COLS);
+          for (int kb = c0; kb < c1; ++kb) {
+            if (!wait_x(full_bar(stage), phase)) { aborted = true; break; }
+            tc_fence_after();
+            const uint32_t sa = ring_u32 + stage * STAGE_BYTES;
+            const uint32_t sb = sa + C_::NPART * A_BYTES + b_off;
 #pragma unroll
-          for (int ks = 0; ks < C_::KSTEPS; ++ks) {
-            const uint64_t ad = sdesc(sa + ks * a_kstep, a_lbo, 1024);
-            const uint64_t bd = sdesc(sb + ks * b_kstep, b_lbo, 1024);
-            umma_g<ESZ, PAIR>(d_tmem, ad, bd, idesc, (kb > w.kb0 || ks > 0) ? 1u : 0u);
+            for (int ks = 0; ks < C_::KSTEPS; ++ks) {
+              const uint64_t ad = sdesc(sa + ks * a_kstep, a_lbo, 1024);
+              const uint64_t bd = sdesc(sb + ks * b_kstep, b_lbo, 1024);
+              umma_g<ESZ, PAIR>(d_tmem, ad, bd, idesc, (kb > c0 || ks > 0) ? 1u : 0u);
+              if constexpr (C_::NPART == 2) {
+                // 3xTF32: + A_hi B_lo + A_lo B_hi (A_lo B_lo is below fp32 resolution).
+                // Both operands are K-major here, so B_lo is one whole B share
+                // after B_hi (a half-width unit keeps its b_off into it).
+                const uint64_t bd_lo = sdesc(sb + C_::B_BYTES + ks * b_kstep, b_lbo, 1024);
+                const uint64_t ad_lo = sdesc(sa + A_BYTES + ks * a_kstep, a_lbo, 1024);
+                umma_g<ESZ, PAIR>(d_tmem, ad, bd_lo, idesc, 1u);
+                umma_g<ESZ, PAIR>(d_tmem, ad_lo, bd, idesc, 1u);
+              }
+            }
+            issued_any = true;
+            umma_commit_g<PAIR>(empty_bar(stage));  // frees this smem stage (in both CTAs) when the MMAs finish
+            if (++stage == STAGES) { stage = 0; phase ^= 1u; }
           }
-          issued_any = true;
-          umma_commit_g<PAIR>(empty_bar(stage));  // frees this smem stage (in both CTAs) when the MMAs finish
-          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+          if (aborted) break;
+          umma_commit_g<PAIR>(tfull_bar(abuf));  // accumulators ready for the epilogue(s)
+          if (++abuf == 2) { abuf = 0; aphase ^= 1u; }
         }
         if (aborted) break;
-        umma_commit_g<PAIR>(tfull_bar(abuf));  // accumulators ready for the epilogue(s)
-        if (++abuf == 2) { abuf = 0; aphase ^= 1u; }
       }
       if (*abort_flag && issued_any) {
         // Drain every MMA this thread issued before TMEM is freed.
@@ -862,6 +968,62 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
     UnitIter it = unit_iter(p, pair_id, npairs);
     Unit w;
     while (unit_next(p, it, npairs, w)) {
+      if constexpr (C_::NPART == 2) {
+        // fp32 (3xTF32): each K chunk's TMEM sum is added to fp32 running sums
+        // in registers (IEEE adds), then stored or published as a partial.
+        const int m = w.tm * TM_ROWS + (int)rank * BM + row;
+        const int ucols = w.half >= 0 ? BN / 2 : BN;
+        const int wcols = ucols / 2;
+        const int col0 = (ew >> 2) * wcols;
+        const int nbase = w.tn * BN + (w.half > 0 ? BN / 2 : 0) + col0;
+        float run[C_::RUN];
+#pragma unroll
+        for (int j = 0; j < C_::RUN; ++j) run[j] = 0.f;
+        bool ok = true;
+        for (int c0 = w.kb0; c0 < w.kb1; c0 += C_::KCHUNK) {
+          if (!wait_x(tfull_bar(abuf), aphase)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t tb = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(abuf * C_::ACC_COLS + col0);
+#pragma unroll
+          for (int c = 0; c < C_::RUN; c += RCH) {
+            if (c < wcols) {
+              uint32_t r[32];
+              tmem_ld<RCH>(tb + c, r);
+              tmem_wait_ld();
+#pragma unroll
+              for (int j = 0; j < RCH; ++j) run[c + j] += __uint_as_float(r[j]);
+            }
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) release_tmem(abuf);
+          if (++abuf == 2) { abuf = 0; aphase ^= 1u; }
+        }
+        if (!ok) break;
+        if (!w.split) {
+#pragma unroll
+          for (int c = 0; c < C_::RUN; c += RCH) {
+            if (c < wcols) {
+              uint32_t r[32];
+#pragma unroll
+              for (int j = 0; j < RCH; ++j) r[j] = __float_as_uint(run[c + j]);
+              const int n0 = nbase + c;
+              if (m < p.M && n0 < p.N) store_row_chunk<T, RCH>(p, w.b, m, n0, r);
+            }
+          }
+        } else {
+          uint4 *part = reinterpret_cast<uint4 *>(reinterpret_cast<uint32_t *>(p.ws) +
+                                                  ((int64_t)w.tail * p.splits + w.s) * ((int64_t)BM * BN) +
+                                                  (int64_t)ew * 32 * wcols) + lane;
+#pragma unroll
+          for (int c = 0; c < C_::RUN; c += 4)
+            if (c < wcols)
+              __stcg(part + (c >> 2) * 32, make_uint4(__float_as_uint(run[c]), __float_as_uint(run[c + 1]),
+                                                      __float_as_uint(run[c + 2]), __float_as_uint(run[c + 3])));
+          split_finish<T, BN, RCH>(p, w, ew, lane, m, nbase, wcols);
+        }
+        continue;
+      }
       if (!wait_x(tfull_bar(abuf), aphase)) break;
       tc_fence_after();
       const int m0 = w.tm * TM_ROWS + (int)rank * BM;  // this CTA's first output row of the tile
@@ -960,59 +1122,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
         tc_fence_before();
         __syncwarp();
         if (lane == 0) release_tmem(abuf);
-        // Each warp owns 32 rows x wcols columns of the tile and reduces them on
-        // its own: per-(tail tile, warp) tickets, so no cross-warp barrier exists
-        // that an aborting warp could leave the others waiting at.
-        __threadfence();
-        __syncwarp();
-        unsigned tk = 0;
-        unsigned *ticket = p.tickets + (int64_t)w.tail * NUM_EPI_WARPS + ew;
-        if (lane == 0) tk = atomicAdd(ticket, 1u);
-        tk = __shfl_sync(0xffffffffu, tk, 0);
-        if (tk == (unsigned)(w.nparts - 1)) {
-          __threadfence();
-          const uint4 *base = reinterpret_cast<const uint4 *>(reinterpret_cast<const uint32_t *>(p.ws) +
-                                                              (int64_t)w.tail * p.splits * slot_words + warp_off) + lane;
-          const int64_t slot_vec = slot_words / 4;
-          constexpr int NV = RCH / 4;                  // uint4 per lane per partial and chunk
-          constexpr int PB = NV >= 8 ? 2 : (NV >= 4 ? 4 : 8);  // partials in flight: 16 loads per lane
-#pragma unroll 1
-          for (int c = 0; c < wcols; c += RCH) {
-            uint32_t r[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) r[j] = 0;
-            const uint4 *src = base + (c >> 2) * 32;
-#pragma unroll 1
-            for (int s0 = 0; s0 < w.nparts; s0 += PB) {
-              uint4 v[PB][NV];
-#pragma unroll
-              for (int b = 0; b < PB; ++b)
-#pragma unroll
-                for (int q = 0; q < NV; ++q)
-                  v[b][q] = (s0 + b < w.nparts) ? __ldcg(src + (int64_t)(s0 + b) * slot_vec + q * 32) : make_uint4(0, 0, 0, 0);
-              // summed in K order: partial s0, s0+1, ...
-#pragma unroll
-              for (int b = 0; b < PB; ++b) {
-                if (s0 + b >= w.nparts) break;
-#pragma unroll
-                for (int q = 0; q < NV; ++q) {
-                  const uint4 x = v[b][q];
-                  if constexpr (Elem<T>::is_int) {
-                    r[4 * q] += x.x; r[4 * q + 1] += x.y; r[4 * q + 2] += x.z; r[4 * q + 3] += x.w;
-                  } else {
-                    r[4 * q] = __float_as_uint(__uint_as_float(r[4 * q]) + __uint_as_float(x.x));
-                    r[4 * q + 1] = __float_as_uint(__uint_as_float(r[4 * q + 1]) + __uint_as_float(x.y));
-                    r[4 * q + 2] = __float_as_uint(__uint_as_float(r[4 * q + 2]) + __uint_as_float(x.z));
-                    r[4 * q + 3] = __float_as_uint(__uint_as_float(r[4 * q + 3]) + __uint_as_float(x.w));
-                  }
-                }
-              }
-            }
-            const int n0 = nbase + c;
-            if (m < p.M && n0 < p.N) store_row_chunk<T, RCH>(p, w.b, m, n0, r);
-          }
-          if (lane == 0) *ticket = 0u;
-        }
+        split_finish<T, BN, RCH>(p, w, ew, lane, m, nbase, wcols);
       }
       if (++abuf == 2) { abuf = 0; aphase ^= 1u; }
     }

@@ -28,7 +28,7 @@ from . import plan as _plan
 INTS = (torch.int8, torch.uint8, torch.int16, torch.int32, torch.int64)
 FLOATS = (torch.float32, torch.float16, torch.bfloat16)
 COMPLEX = (torch.complex64, torch.complex32)
-TC_DTYPES = (torch.bfloat16, torch.float16, torch.int8, torch.uint8, torch.complex32)
+TC_DTYPES = (torch.bfloat16, torch.float16, torch.int8, torch.uint8, torch.complex32, torch.float32)  # fp32: 3xTF32
 _INT64_MASK = (1 << 64) - 1
 
 

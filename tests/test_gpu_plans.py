@@ -212,3 +212,41 @@ def test_packed_operands_on_tensor_cores(dtype):
     got = mb.addmm(bias, _offset(a), b, beta=beta, alpha=alpha)
     ok, err = orc.check(to_np(got), orc.fused(to_np(bias), to_np(a), to_np(b), beta, alpha, NAME[dtype]), NAME[dtype])
     assert ok, f"addmm err={err}"
+
+
+def test_fp32_3xtf32_matches_oracle():
+    """fp32 on the tensor cores (3xTF32: tf32 high/low split, three MMAs per
+    K-step) stays inside the north star's 1e-5 relative-Frobenius bound across
+    layouts, thin M (swap), split / stream-K tails, batches with a broadcast
+    operand and the alpha/beta/bias epilogue."""
+    import metalblas_b200 as mb
+    gen = torch.Generator().manual_seed(15)
+    # backend="mpp_tensor" puts any fp32 product on the tensor cores; the planner
+    # chooses them by itself for compute-heavy shapes (2048^3 here)
+    for (M, N, K) in [(512, 640, 768), (1000, 1000, 1000), (64, 4096, 2048), (256, 512, 16384), (2048, 2048, 2048)]:
+        a = rand((M, K), torch.float32, gen)
+        b = rand((K, N), torch.float32, gen)
+        ref = orc.product(to_np(a), to_np(b), "float32")
+        for av, bv in ((a, b), (a.t().contiguous().t(), b), (a, b.t().contiguous().t()), (_offset(a), _offset(b))):
+            plan = mb.kernels.plan(av, bv, backend="mpp_tensor")
+            assert plan.startswith("tc_3xtf32"), plan
+            ok, err = orc.check(to_np(mb.matmul(av, bv, backend="mpp_tensor")), ref, "float32")
+            assert ok, f"{(M, N, K)} err={err}"
+        if M * N * K >= 512 * (M * K + K * N):
+            assert mb.kernels.plan(a, b).startswith("tc_3xtf32")
+    A = rand((8, 1024, 1024), torch.float32, gen)
+    B = rand((1, 1024, 1024), torch.float32, gen)
+    bias = rand((8, 1024, 1024), torch.float32, gen)
+    assert mb.kernels.plan(A, B).startswith("tc_3xtf32")  # compute-heavy: the planner's own choice
+    got = mb.baddbmm(bias, A, B.expand(8, 1024, 1024), beta=0.5, alpha=-2.0)
+    ref = orc.fused(to_np(bias), to_np(A), np.broadcast_to(to_np(B), (8, 1024, 1024)), 0.5, -2.0, "float32")
+    ok, err = orc.check(to_np(got), ref, "float32")
+    assert ok, f"baddbmm err={err}"
+    # non-finite inputs propagate like the CUDA-core kernel's
+    a = rand((256, 512), torch.float32, gen)
+    b = rand((512, 384), torch.float32, gen)
+    a[3, 7] = float("inf")
+    a[5, 1] = float("nan")
+    got = mb.matmul(a, b, backend="mpp_tensor")
+    simd = mb.matmul(a, b, backend="simd")
+    assert torch.equal(torch.isnan(got), torch.isnan(simd)) and torch.equal(torch.isinf(got), torch.isinf(simd))
