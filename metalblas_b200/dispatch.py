@@ -283,6 +283,34 @@ def _mm2d(a, b, out, epilogue=None, backend=None, tile=None):
                    epilogue=epilogue, backend=be, tile_n=tile_n, split_k=split_k)
 
 
+def _flat3(t, size, rows, cols):
+    """[*batch, rows, cols] as a [size, rows, cols] view when its batch dims
+    collapse into one stride (contiguous batches, or all broadcast), else None."""
+    try:
+        return t.view(size, rows, cols)
+    except RuntimeError:
+        return None
+
+
+def _batched_into(a, b, out):
+    """out[...] = a[...] @ b[...] for equal batch shapes, without copying the
+    operands: the batch dims are flattened when their strides allow, otherwise
+    the leading batch dim is walked and the rest flattened (the reference
+    reshapes, which copies a broadcast-expanded operand, metalblas/dispatch.py:163-166)."""
+    batch = a.shape[:-2]
+    M, K = a.shape[-2:]
+    N = b.shape[-1]
+    size = prod(batch)
+    if size == 0:
+        return
+    a3, b3 = _flat3(a, size, M, K), _flat3(b, size, K, N)
+    if a3 is not None and b3 is not None:
+        bmm(a3, b3, out=out.view(size, M, N))
+        return
+    for i in range(batch[0]):
+        _batched_into(a[i], b[i], out[i])
+
+
 def _matmul_nd(a, b, out=None):
     """Vector promotion and broadcast batches around the 2-D/3-D kernels
     (metalblas/dispatch.py:148-171)."""
@@ -297,14 +325,12 @@ def _matmul_nd(a, b, out=None):
     assert K == K2, f"shape mismatch: A is {a.shape}, B is {b.shape}"
     batch = torch.broadcast_shapes(a.shape[:-2], b.shape[:-2])
     if batch:
-        size = prod(batch)
-        a3 = a.expand(*batch, M, K).reshape(size, M, K)
-        b3 = b.expand(*batch, K, N).reshape(size, K, N)
         if (out is not None and not (a_vec or b_vec) and out.shape == (*batch, M, N) and out.dtype == a.dtype
                 and out.is_contiguous()):
-            bmm(a3, b3, out=out.view(size, M, N))  # written in place, no temporary
+            _batched_into(a.expand(*batch, M, K), b.expand(*batch, K, N), out)  # written in place
             return out
-        result = bmm(a3, b3).reshape(*batch, M, N)
+        result = torch.empty((*batch, M, N), dtype=a.dtype, device=a.device)
+        _batched_into(a.expand(*batch, M, K), b.expand(*batch, K, N), result)
     else:
         result = matmul(a, b)
     if a_vec:

@@ -250,3 +250,34 @@ def test_fp32_3xtf32_matches_oracle():
     got = mb.matmul(a, b, backend="mpp_tensor")
     simd = mb.matmul(a, b, backend="simd")
     assert torch.equal(torch.isnan(got), torch.isnan(simd)) and torch.equal(torch.isinf(got), torch.isinf(simd))
+
+
+def test_nd_broadcast_batches_read_operands_in_place(monkeypatch):
+    """matmul over multi-dim broadcast batches: when the
+    expanded batch dims cannot be flattened into one stride, the leading dim is
+    walked instead of copying the operand; every launch reads the caller's own
+    storage."""
+    import metalblas_b200 as mb
+    from metalblas_b200 import dispatch
+    gen = torch.Generator().manual_seed(16)
+    cases = [((2, 3, 64, 96), (3, 96, 80)), ((2, 1, 64, 96), (1, 3, 96, 80)), ((4, 64, 96), (96, 80)),
+             ((2, 3, 64, 96), (2, 3, 96, 80)), ((5, 1, 33, 40), (1, 7, 40, 20))]
+    real_bmm = dispatch.bmm
+    for dtype in (torch.bfloat16, torch.float32, torch.int32):
+        for sa, sb in cases:
+            a = rand(sa, dtype, gen)
+            b = rand(sb, dtype, gen)
+            storages = {a.untyped_storage().data_ptr(), b.untyped_storage().data_ptr()}
+            seen = []
+
+            def spy(x, y, *, out=None):
+                seen.append((x.untyped_storage().data_ptr(), y.untyped_storage().data_ptr()))
+                return real_bmm(x, y, out=out)
+            monkeypatch.setattr(dispatch, "bmm", spy)
+            got = mb.matmul(a, b)
+            monkeypatch.setattr(dispatch, "bmm", real_bmm)
+            assert seen and all(p in storages and q in storages for p, q in seen), (sa, sb)
+            ref = orc.product(np.broadcast_to(to_np(a), got.shape[:-2] + a.shape[-2:]),
+                              np.broadcast_to(to_np(b), got.shape[:-2] + b.shape[-2:]), NAME[dtype])
+            ok, err = orc.check(to_np(got), ref, NAME[dtype])
+            assert ok, f"{dtype} {sa} @ {sb} err={err}"
