@@ -364,7 +364,10 @@ void choose_tc_tile(const Op &o, int sms, int force_bn, int force_split, int for
     const bool pair_fits = !bm || (bn / 2) * esz >= 128;
     // Pairs pay a cross-CTA handshake per tile (both epilogues must drain an
     // accumulator before the next MMA): only worth it with enough K per tile.
-    const bool want_pair = !s3 && (force_pair == 2 || (force_pair == 0 && g_pair_enabled && o.M > 128 && kb_total >= 8));
+    // (3xTF32 is bound by its three tf32 MMAs, not by operand traffic: pairs
+    // measured no faster at 4096^3 and slower at 8192^3, so only on request)
+    const bool want_pair = s3 ? (bn == 128 && force_pair == 2)
+                              : (force_pair == 2 || (force_pair == 0 && g_pair_enabled && o.M > 128 && kb_total >= 8));
     if ((bn == 128 || bn == 256) && pair_fits && want_pair && (!force_split || force_split == 1) && force_sk != 2) {
       const int pairs = sms / 2;
       const int64_t ptiles = o.batch * ceil_div(o.M, 256) * ceil_div(o.N, bn);
@@ -972,7 +975,8 @@ int launch_tc_bn(const Op &o, const Plan &pl, const EpiScalars &e, void *ws, int
 template <class T>
 int launch_tc(const Op &o, const Plan &pl, const EpiScalars &e, void *ws, int sms, cudaStream_t st) {
   if constexpr (std::is_same_v<T, float>) {
-    // 3xTF32 keeps BN/2 fp32 running sums per epilogue thread: single-CTA tiles, BN <= 128
+    // 3xTF32 keeps BN/2 fp32 running sums per epilogue thread: BN <= 128
+    if (pl.pair == 2 && pl.bn == 128) return launch_tc_bn<T, 128, 2>(o, pl, e, ws, sms, st);
     switch (pl.pair == 1 ? pl.bn : 0) {
       case 16: return launch_tc_bn<T, 16, 1>(o, pl, e, ws, sms, st);
       case 32: return launch_tc_bn<T, 32, 1>(o, pl, e, ws, sms, st);
