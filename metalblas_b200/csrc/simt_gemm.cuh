@@ -97,7 +97,12 @@ __global__ void __launch_bounds__(256, 2) simt_gemm_kernel(const SimtParams p) {
 
   if (p.gate != nullptr && *reinterpret_cast<const volatile int *>(p.gate) == 0) return;  // uniform per CTA
   const int tid = threadIdx.x;
-  const int tx = tid % TX, ty = tid / TX;
+  // Each warp covers an 8 (x) by 4 (y) block of micro-tiles, so one K row's
+  // fragment reads touch 4 distinct 16-byte A vectors and 8 B vectors: one
+  // shared-memory wavefront per read instead of two for a 16 x 2 layout.
+  static_assert(TX % 8 == 0 && TY % 4 == 0 && (TX / 8) * (TY / 4) == NT / 32, "8 x 4 warp blocks");
+  const int lane = tid & 31, wid = tid >> 5;
+  const int tx = (wid % (TX / 8)) * 8 + (lane & 7), ty = (wid / (TX / 8)) * 4 + (lane >> 3);
   const int64_t m0 = (int64_t)blockIdx.y * BM, n0 = (int64_t)blockIdx.x * BN;
   // A: k contiguous (row-major) -> runs along k; otherwise runs along m.
   const bool a_kfast = p.a_cs == 1 || (p.a_rs != 1 && (p.a_cs < 0 ? -p.a_cs : p.a_cs) <= (p.a_rs < 0 ? -p.a_rs : p.a_rs));
