@@ -233,7 +233,7 @@ def run_ours(args, w, rank, world, device):
     gathered = None
     if world > 1:
         import torch.distributed as dist
-        G = torch.empty(world, M, N, dtype=dt, device=device)
+        G = torch.empty(world * M, N, dtype=dt, device=device)
         for i in range(3):
             mb.matmul(As[i % SETS], Bs[i % SETS], out=Cs[i % SETS])
             dist.all_gather_into_tensor(G, Cs[i % SETS])
@@ -248,7 +248,8 @@ def run_ours(args, w, rank, world, device):
         _barrier(world, device)
         gms = _max_over_ranks(g0.elapsed_time(g1) / args.steps, world, device)
         gathered = {"value": flops * world / (gms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": gms,
-                    "layout": "[N_ranks, M, N/N_ranks] via NCCL all_gather_into_tensor"}
+                    "layout": "C as its N_ranks column blocks, [N_ranks, M, N/N_ranks], on every rank",
+                    "collective": "NCCL all_gather_into_tensor after each product"}
 
     # e2e: host buffers -> public API -> host result, every step.  Three streams
     # (copy-in, compute, copy-out) and two device buffer sets, so step i's
@@ -333,18 +334,17 @@ def run_bmm_sharded(args, rank, world, device):
     """BASELINE's "bmm TFLOP/s at 1-8 GPUs": bf16 bmm [256,1024,1024] @
     [256,1024,1024] (N(0,1), seed 2) with the batch sharded over the ranks
     (strong scaling: the 256 batches are split, metalblas_b200.shard.shard_range).
-    `value` keeps each rank's output slab local; `gathered` adds an NCCL
-    all-gather of the slabs into the full [256, 1024, 1024] every step.  Device
-    time, max over ranks, 2 input sets (1.5 GB > L2)."""
+    `value` keeps each rank's output slab local; `gathered` returns the full
+    [256, 1024, 1024] on every rank every step (pipelined NCCL all-gathers).
+    Device time, max over ranks, 2 input sets (1.5 GB > L2)."""
     import metalblas_b200 as mb
     from metalblas_b200 import shard
     Bt, M, N, K = 256, 1024, 1024, 1024
     s, e = shard.shard_range(Bt, world, rank)
     nb = e - s
-    g = torch.Generator(device=device).manual_seed(2 + rank)
-    As = [torch.randn(nb, M, K, generator=g, device=device, dtype=torch.bfloat16) for _ in range(2)]
-    Bs = [torch.randn(nb, K, N, generator=g, device=device, dtype=torch.bfloat16) for _ in range(2)]
-    Cs = [torch.empty(nb, M, N, device=device, dtype=torch.bfloat16) for _ in range(2)]
+    g = torch.Generator(device=device).manual_seed(2)  # the same full operands on every rank
+    As = [torch.randn(Bt, M, K, generator=g, device=device, dtype=torch.bfloat16) for _ in range(2)]
+    Bs = [torch.randn(Bt, K, N, generator=g, device=device, dtype=torch.bfloat16) for _ in range(2)]
     steps = max(5, min(args.steps, 50))
     stream = torch.cuda.current_stream(device)
 
@@ -361,24 +361,17 @@ def run_bmm_sharded(args, rank, world, device):
         _barrier(world, device)
         return _max_over_ranks(e0.elapsed_time(e1) / steps, world, device)
 
-    ms = timed(lambda i: mb.bmm(As[i], Bs[i], out=Cs[i]))
+    ms = timed(lambda i: shard.sharded_bmm(As[i], Bs[i], gather=False))
     flops = 2.0 * Bt * M * N * K
     out = {"workload": "bf16 bmm [256,1024,1024]@[256,1024,1024], batch sharded over ranks (strong scaling)",
            "value": flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms, "steps": steps,
-           "batches_per_rank": nb, "plan": mb.kernels.plan(As[0], Bs[0])}
+           "batches_per_rank": nb, "plan": mb.kernels.plan(As[0][s:e], Bs[0][s:e]),
+           "api": "metalblas_b200.shard.sharded_bmm"}
     if world > 1:
-        import torch.distributed as dist
-        per = -(-Bt // world)
-        pad = torch.empty(per, M, N, device=device, dtype=torch.bfloat16)
-        full = torch.empty(world * per, M, N, device=device, dtype=torch.bfloat16)
-
-        def step(i):
-            mb.bmm(As[i], Bs[i], out=Cs[i])
-            pad[:nb].copy_(Cs[i])
-            dist.all_gather_into_tensor(full, pad)
-        gms = timed(step)
+        gms = timed(lambda i: shard.sharded_bmm(As[i], Bs[i], gather=True, chunks=4))
         out["gathered"] = {"value": flops / (gms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": gms,
-                           "collective": "NCCL all_gather_into_tensor of the padded slabs"}
+                           "collective": "NCCL all_gather_into_tensor in 4 rounds straight into the output, "
+                                         "each overlapping the next round's products"}
     return out
 
 

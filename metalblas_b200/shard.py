@@ -5,7 +5,8 @@ helpers spread its products over N GPUs the way the north star asks:
 
 * ``sharded_bmm``     — the batch is independent: rank r computes its contiguous
   slice of batches with no communication; ``gather=True`` all-gathers the slabs
-  over NCCL (NVLink) into the full [B, M, N] output.
+  over NCCL (NVLink) into the full [B, M, N] output, optionally in pipelined
+  rounds that overlap the exchange with the next round's products.
 * ``sharded_matmul_n`` — large GEMMs split along N: rank r holds all of A and its
   column block of B and computes C[:, block r]; ``gather=True`` all-gathers the
   blocks and lays them out as one row-major C.
@@ -37,6 +38,9 @@ def shard_range(n: int, world: int, rank: int) -> tuple[int, int]:
 
 
 def _world(group):
+    """(world size, rank); a single process without a process group is world 1."""
+    if group is None and not (dist.is_available() and dist.is_initialized()):
+        return 1, 0
     return dist.get_world_size(group), dist.get_rank(group)
 
 
@@ -63,15 +67,36 @@ def _all_gather_rows(local: torch.Tensor, n_total: int, group, world: int) -> to
 
 
 def sharded_bmm(a: torch.Tensor, b: torch.Tensor, *, group=None, gather: bool = False,
-                local_bmm: Optional[Callable] = None) -> torch.Tensor:
+                local_bmm: Optional[Callable] = None, chunks: int = 1) -> torch.Tensor:
     """Batch-sharded bmm.  ``a``: [B, M, K] and ``b``: [B, K, N] (or [1, K, N],
-    broadcast) on every rank; returns this rank's [B_r, M, N] slab, or the whole
-    [B, M, N] when ``gather``."""
+    broadcast) on every rank; returns this rank's [B_r, M, N] slab (its
+    shard_range of the batches), or the whole [B, M, N] when ``gather``.
+
+    ``chunks > 1`` with ``gather`` pipelines the exchange: the batches are
+    dealt out in ``chunks`` rounds (round c holds ranks' blocks side by side),
+    each round's all-gather is issued asynchronously on NCCL's stream as soon
+    as its products are done and runs while the next round computes, and each
+    gathers straight into its contiguous slice of the output (no assembly
+    copy).  This needs B divisible by world * chunks; otherwise one exchange
+    after all products is used."""
     world, rank = _world(group)
     bsz = a.shape[0]
-    s, e = shard_range(bsz, world, rank)
     bb = b.expand(bsz, *b.shape[1:]) if b.shape[0] == 1 and bsz > 1 else b
-    local = (local_bmm or _default_bmm)(a[s:e], bb[s:e])
+    mm = local_bmm or _default_bmm
+    if gather and chunks > 1 and world > 1 and bsz % (world * chunks) == 0:
+        cb = bsz // (world * chunks)                 # batches per rank and round
+        out = torch.empty((bsz,) + tuple(a.shape[1:2]) + tuple(bb.shape[2:]), dtype=a.dtype, device=a.device)
+        works = []
+        for c in range(chunks):
+            lo = (c * world + rank) * cb             # this rank's block of round c
+            slab = mm(a[lo:lo + cb], bb[lo:lo + cb]).contiguous()
+            dst = out[c * world * cb:(c + 1) * world * cb]
+            works.append((dist.all_gather_into_tensor(dst, slab, group=group, async_op=True), slab))
+        for w, _ in works:
+            w.wait()
+        return out
+    s, e = shard_range(bsz, world, rank)
+    local = mm(a[s:e], bb[s:e])
     if not gather:
         return local
     return _all_gather_rows(local.contiguous(), bsz, group, world)

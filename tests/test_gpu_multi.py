@@ -49,7 +49,13 @@ def _worker(rank, world, port, results):
         s, e = shard.shard_range(1024, world, rank)
         Ck = shard.sharded_matmul_k(A[:, s:e].contiguous().to(dev), B[s:e].contiguous().to(dev))
         ok3, _ = orc.check(Ck.float().cpu().numpy(), ref, "bfloat16")
-        results[rank] = (bool(ok1), bool(ok2), bool(ok3))
+        # pipelined exchange: bmm in 4 rounds (8 batches over 2 ranks)
+        a8 = torch.randn(8, 384, 256, generator=g).to(torch.bfloat16)
+        b8 = torch.randn(8, 256, 320, generator=g).to(torch.bfloat16)
+        c8 = shard.sharded_bmm(a8.to(dev), b8.to(dev), gather=True, chunks=4)
+        ok4, _ = orc.check(c8.float().cpu().numpy(), orc.product(a8.float().numpy(), b8.float().numpy(), "bfloat16"),
+                           "bfloat16")
+        results[rank] = (bool(ok1), bool(ok2), bool(ok3 and ok4))
     finally:
         dist.destroy_process_group()
 

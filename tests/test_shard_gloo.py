@@ -45,7 +45,13 @@ def _worker(rank, world, port, results):
         s, e = shard.shard_range(8, world, rank)
         Ck = shard.sharded_matmul_k(A[:, s:e].contiguous(), B[s:e].contiguous(), local_mm=torch.matmul)
         ok_k = torch.allclose(Ck, A @ B, atol=1e-5)
-        results[rank] = (ok_bmm, ok_part, ok_n, ok_k)
+        # pipelined exchange: bmm in rounds gathered straight into the output
+        # (8 batches = 2 ranks x 4 rounds)
+        a8 = torch.randn(8, 6, 7, generator=g)
+        b8 = torch.randn(8, 7, 5, generator=g)
+        ok_pipe = torch.allclose(shard.sharded_bmm(a8, b8, gather=True, local_bmm=torch.bmm, chunks=4),
+                                 torch.bmm(a8, b8), atol=1e-5)
+        results[rank] = (ok_bmm, ok_part, ok_n, ok_k and ok_pipe)
     finally:
         dist.destroy_process_group()
 
