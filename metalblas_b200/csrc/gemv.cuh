@@ -195,7 +195,7 @@ __global__ void __launch_bounds__(NW * 32) gemv_cols_kernel(const GemvParams p) 
   for (int i = 0; i < VEC; ++i) acc[i] = E::zero();
 
   const bool full = (c0 + VEC <= p.R);
-  constexpr int U = 4;  // independent 16-byte loads in flight per thread
+  constexpr int U = 8;  // independent 16-byte loads in flight per thread
   int64_t k = kbeg + warp;
   bool done = false;
   if constexpr (VEC > 1) {

@@ -631,7 +631,8 @@ bool plan_gemv(const Op &o, int sms, const mb_gemm_desc *d, bool have_ws, Plan &
     if (ks > 1 && !have_ws) ks = 1;
     if (o.batch * ctas_x > kMaxTickets) ks = 1;  // not enough ticket counters
     if (ks > 1) {
-      g.kchunk = ceil_div(g.K, ks);
+      // whole unrolled steps per chunk: 8 warps x 8 rows in flight per lane
+      g.kchunk = round_up(ceil_div(g.K, ks), 64);
       ks = ceil_div(g.K, g.kchunk);
     }
     g.ksplit = (int)ks;
