@@ -182,6 +182,7 @@ struct Plan {
   int64_t gemv_ctas_x = 0;
   // TC (operands already swapped when swap == 1)
   int swap = 0, bn = 0, splits = 1;
+  double est = 0.0;  // the tile chooser's time estimate (cycles)
   int64_t tiles_m = 0, tiles_n = 0, kb_total = 0, kb_per_split = 0;
   int64_t dp_tiles = 0;  // whole tiles; tiles after them are split `splits` ways along K,
   int tail_half = 0;     // or (tail_half) into two half-width units each
@@ -287,8 +288,9 @@ const bool g_pair_enabled = [] {
 
 // HBM bytes per clock per SM when every SM streams (6537 GB/s / 148 / 1.965 GHz).
 constexpr double kHbmBytesPerClkPerSm = 22.4;
-// Operand bytes one SM's TMA pipeline sustains per clock (B200, 4-8 stage ring).
-constexpr double kSmFillBytesPerClk = 45.0;
+// DRAM bytes one SM pulls per clock when its operands stream from HBM rather
+// than L2 (B200, thin and split-K shapes on 96-128 busy SMs: 57-61 GB/s each).
+constexpr double kSmStreamBytesPerClk = 31.0;
 
 // Stream-K partition of `tail` tiles of kb K-blocks over G CTAs: the most
 // pieces any tile is cut into (CTA g owns iterations [g*I/G, (g+1)*I/G)).
@@ -319,16 +321,22 @@ void choose_tc_tile(const Op &o, int sms, int force_bn, int force_split, int for
       (double)(o.M * o.N * o.batch) * esz;
   auto consider = [&](double compute, double units, double waves, double extra_bytes, int bn, int am, int bm,
                       int seff, int64_t kbp, int64_t dp, int half, int pair = 1, int sk = 0) {
-    // HBM floor: the whole chip's bandwidth, or what the SMs busy on average
-    // across the waves can pull (about 45 B/clk each through TMA), if lower.
-    // Stream-K CTAs stream B rows at unrelated K offsets at the same time,
-    // which measured ~15% below the same bytes read by K-aligned splits.
-    const double avg_active = units / std::max(1.0, waves);
-    const double rate = std::min(kHbmBytesPerClkPerSm * sms, kSmFillBytesPerClk * avg_active);
-    const double mem = (opnd_bytes + extra_bytes) / rate * (sk ? 1.15 : 1.0);
+    // HBM floor, wave by wave: a wave with n busy SMs streams at the whole
+    // chip's bandwidth or at what n SMs can pull from DRAM, whichever is lower
+    // (a short last wave streams slowly).  Stream-K CTAs stream B rows at
+    // unrelated K offsets at the same time, measured below the same bytes read
+    // by K-aligned units: ~15% with wide tiles (skinny 128 x 8192 x 65536),
+    // ~8% with narrow ones (thin-M swapped tiles).
+    const double full = std::max(0.0, waves - 1.0);
+    const double first = std::min<double>(units, sms);
+    const double last = std::min<double>(sms, std::max(1.0, units - full * sms));
+    const double per_unit = (opnd_bytes + extra_bytes) / std::max(1.0, units);
+    auto rate = [&](double n) { return std::min(kHbmBytesPerClkPerSm * sms, kSmStreamBytesPerClk * n); };
+    const double mem = (full * first * per_unit / rate(first) + last * per_unit / rate(last)) * (sk ? (bn >= 128 ? 1.15 : 1.08) : 1.0);
     const double t = std::max(compute, mem) * (1.0 + 0.002 * seff);
     if (t < best) {
       best = t;
+      pl.est = t;
       pl.bn = bn; pl.splits = seff; pl.a_mn = am; pl.b_mn = bm;
       pl.tiles_m = ceil_div(o.M, 128 * pair); pl.tiles_n = ceil_div(o.N, bn);
       pl.kb_total = kb_total; pl.kb_per_split = kbp;
@@ -416,6 +424,10 @@ void choose_tc_tile(const Op &o, int sms, int force_bn, int force_split, int for
       // whole-tile epilogue, so it is charged per split and per column
       const double unit_split = kbp * kbc(bn) + 4.0 * bn + 16.0 * seff * bn;
       const int64_t units = tiles * seff;
+      // splits fill one wave; past that a stream-K tail balances the same work
+      // with fewer fix-ups (measured on B200: thin 224-tile shapes, split 3-4
+      // at 0.87-0.91x the stream-K time)
+      if (!force_split && units > sms) continue;
       const int64_t w = ceil_div(units, sms);
       consider(w * unit_split, (double)units, (double)w, (double)tiles * seff * 128.0 * bn * 8.0, bn, am, bm,
                (int)seff, kbp, 0, 0);
@@ -595,6 +607,8 @@ bool plan_3xtf32(const Op &o, int sms, const mb_gemm_desc *d, bool have_ws, Plan
   return true;
 }
 
+int gemv_cols_per_sm(int dt);
+
 bool plan_gemv(const Op &o, int sms, const mb_gemm_desc *d, bool have_ws, Plan &pl) {
   GemvParams g{};
   int kind = 0;
@@ -624,8 +638,11 @@ bool plan_gemv(const Op &o, int sms, const mb_gemm_desc *d, bool have_ws, Plan &
     const int64_t cols_per_cta = 32 * pl.vec;
     const int64_t ctas_x = ceil_div(g.R, cols_per_cta);
     pl.gemv_ctas_x = ctas_x;
-    const int64_t want = 4 * (int64_t)sms;  // CTAs wanted in flight
-    int64_t ks = d->split_k > 0 ? d->split_k : ceil_div(want, ctas_x * o.batch);
+    // one full wave of resident CTAs: a partial second wave leaves most SMs
+    // idle while it streams (672 CTAs on 592 slots measured 0.78 of HBM at
+    // N = 28672)
+    const int64_t want = (int64_t)gemv_cols_per_sm(o.dt) * sms;
+    int64_t ks = d->split_k > 0 ? d->split_k : std::max<int64_t>(1, want / (ctas_x * o.batch));
     ks = std::max<int64_t>(1, std::min<int64_t>(ks, ceil_div(g.K, 64)));  // >= 64 rows per CTA
     if (ks > 65535) ks = 65535;
     if (ks > 1 && !have_ws) ks = 1;
@@ -731,7 +748,20 @@ bool plan_tc_any(const Op &o, int sms, const mb_gemm_desc *d, bool have_ws, Plan
   const bool want_swap = d->swap_ab == 1 || (d->swap_ab == 0 && o.M < 128 && o.N > o.M);
   if (want_swap && d->swap_ab != -1) {
     Op s = swapped(o);
-    if (plan_tc(s, sms, d, have_ws, pl)) { pl.swap = 1; return true; }
+    if (plan_tc(s, sms, d, have_ws, pl)) {
+      pl.swap = 1;
+      // thin M, free choice: wide unswapped tiles stream B in longer rows and
+      // win where they fill the machine (M = 16..100, N = 28672: 112 tiles of
+      // 128 x 256 measured 1.05-1.40x the swapped plans on B200; below M = 16
+      // they lost at K <= 8192, and split unswapped tiles measured no gain)
+      Plan u;
+      if (d->swap_ab == 0 && o.M >= 16 && plan_tc(o, sms, d, have_ws, u) && u.splits == 1 && !u.sk &&
+          u.est < 0.97 * pl.est) {
+        pl = u;
+        pl.swap = 0;
+      }
+      return true;
+    }
   }
   if (d->swap_ab != 1 && plan_tc(o, sms, d, have_ws, pl)) { pl.swap = 0; return true; }
   return false;
@@ -1109,6 +1139,28 @@ int by_dtype(int dt, F &&f) {
     case MB_I64: return f((int64_t *)nullptr);
   }
   return fail(MB_ERR_UNSUPPORTED, "dtype");
+}
+
+// Resident CTAs per SM of the vectorised column GEMV for dtype dt, from the
+// occupancy calculator; 4 when no device answers (plan queries on a host).
+int gemv_cols_per_sm(int dt) {
+  static std::atomic<int> cache[MB_I64 + 1];
+  if (dt < 0 || dt > MB_I64) return 4;
+  int v = cache[dt].load(std::memory_order_relaxed);
+  if (v > 0) return v;
+  v = by_dtype(dt, [](auto *p) -> int {
+    using T = std::remove_pointer_t<decltype(p)>;
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_cols_kernel<T, 16 / sizeof(T), kGemvWarps>,
+                                                      kGemvWarps * 32, 0) != cudaSuccess) {
+      cudaGetLastError();
+      return 0;
+    }
+    return n;
+  });
+  if (v <= 0) return 4;
+  cache[dt].store(v, std::memory_order_relaxed);
+  return v;
 }
 
 template <class T> struct IsTc { static constexpr bool v = false; };
