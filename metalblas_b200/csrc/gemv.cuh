@@ -33,8 +33,13 @@ struct GemvParams {
   EpiScalars epi;
   int ksplit;            // cols and staged-x rows kernels: CTAs along K
   int64_t kchunk;        // K elements per CTA (a multiple of 16 bytes of W for the rows kernel)
-  void *ws;              // ksplit*batch*R accumulators
-  unsigned *tickets;     // batch * (CTAs along R) counters, zero on entry and exit
+  void *ws;              // ksplit*batch*mrows*R accumulators
+  unsigned *tickets;     // batch * gridDim.x counters, zero on entry and exit
+  // cols kernel with several x rows (thin M): x row m at X + m*x_rs, y row m at
+  // Y + m*y_rs, bias row m at bias + m*bias_rs; rows in mrb blocks of the
+  // kernel's MR (grid x = column blocks * mrb, the row block varying fastest)
+  int mrows, mrb;
+  int64_t x_rs, y_rs, bias_rs;
 };
 
 template <class T, int VEC>
@@ -106,6 +111,17 @@ __device__ __forceinline__ void gemv_store(const GemvParams &p, int64_t b, int64
   ((T *)p.Y)[b * p.sY + r * p.y_s] = Elem<T>::store(v);
 }
 
+// gemv_store for row m of a thin-M product (cols kernel).
+template <class T>
+__device__ __forceinline__ void gemv_store_m(const GemvParams &p, int64_t b, int64_t m, int64_t r,
+                                             typename Elem<T>::acc v) {
+  if (p.epi.enabled) {
+    const T *bias = (const T *)p.bias + b * p.sBias + m * p.bias_rs + r * p.bias_s;
+    v = EpiOps<T>::apply(v, bias, p.epi);
+  }
+  ((T *)p.Y)[b * p.sY + m * p.y_rs + r * p.y_s] = Elem<T>::store(v);
+}
+
 // One K row of gemv_cols: acc[i] += x * w[i] for VEC consecutive columns.
 // Generic form: widen and multiply in the accumulator type.
 template <class T, int VEC>
@@ -173,8 +189,12 @@ struct ColRow<__half2, 4> {
 
 // ---------------------------------------------------------------------------
 // gemv_cols: grid (ceil(R / (32*VEC)), ksplit, batch), NW warps per CTA.
-// VEC == 1 is the unaligned fallback (scalar loads).
-template <class T, int VEC, int NW>
+// VEC == 1 is the unaligned fallback (scalar loads).  MR > 1: thin M, a block
+// of up to MR rows of x shares every 16-byte load of W (each W element feeds
+// MR FMAs; rows past the block's last re-read it and their sums are dropped).
+// Grid x = column blocks * p.mrb with the row block varying fastest, so the
+// row blocks of one column stripe run together and share it through L2.
+template <class T, int VEC, int NW, int MR = 1>
 __global__ void __launch_bounds__(NW * 32) gemv_cols_kernel(const GemvParams p) {
   using E = Elem<T>;
   using Acc = typename E::acc;
@@ -183,78 +203,125 @@ __global__ void __launch_bounds__(NW * 32) gemv_cols_kernel(const GemvParams p) 
   __shared__ unsigned s_ticket;
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int mrb = MR == 1 ? 1 : p.mrb;
   const int64_t b = blockIdx.z;
-  const int64_t c0 = (int64_t)blockIdx.x * COLS + lane * VEC;
+  const int row0 = (int)(blockIdx.x % mrb) * MR;
+  const int64_t cblk = blockIdx.x / mrb;
+  const int64_t c0 = cblk * COLS + lane * VEC;
   const int64_t kbeg = (int64_t)blockIdx.y * p.kchunk;
   const int64_t kend = min(p.K, kbeg + p.kchunk);
   const T *W = (const T *)p.W + b * p.sW;
   const T *X = (const T *)p.X + b * p.sX;
-
-  Acc acc[VEC];
+  const int mrows = MR == 1 ? 1 : p.mrows;          // rows of x in all
+  const int rows = MR == 1 ? 1 : min(MR, mrows - row0);  // rows in this CTA's block
+  int64_t xoff[MR];
 #pragma unroll
-  for (int i = 0; i < VEC; ++i) acc[i] = E::zero();
+  for (int r = 0; r < MR; ++r) xoff[r] = (int64_t)(row0 + min(r, rows - 1)) * p.x_rs;
+
+  Acc acc[MR][VEC];
+#pragma unroll
+  for (int r = 0; r < MR; ++r)
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) acc[r][i] = E::zero();
 
   const bool full = (c0 + VEC <= p.R);
-  constexpr int U = 8;  // independent 16-byte loads in flight per thread
+  constexpr int U = MR == 1 ? 8 : 4;  // independent 16-byte loads of W in flight per thread
   int64_t k = kbeg + warp;
   bool done = false;
-  if constexpr (VEC > 1) {
+  if constexpr (VEC > 1 && MR > 1) {
+    if (full) {
+      // Several x rows: each warp walks a contiguous K range so that its x
+      // reads run along K through L1 lines (interleaved warps would take every
+      // x element from L2 once per CTA).
+      done = true;
+      using CR = ColRow<T, VEC>;
+      const int64_t span = ((kend - kbeg + NW - 1) / NW + U - 1) / U * U;
+      k = kbeg + warp * span;
+      const int64_t kw = min(kend, k + span);
+      for (; k + U <= kw; k += U) {
+        T w[U][VEC];
+        typename CR::X xv[U][MR];
+#pragma unroll
+        for (int u = 0; u < U; ++u) VecLoad<T, VEC>::load(W + (k + u) * p.w_ld + c0, w[u]);
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+#pragma unroll
+          for (int r = 0; r < MR; ++r) xv[u][r] = CR::prep(X[xoff[r] + (k + u) * p.x_s], p.conj_x, p.conj_w);
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+#pragma unroll
+          for (int r = 0; r < MR; ++r) CR::run(acc[r], w[u], xv[u][r], p.conj_w);
+      }
+      for (; k < kw; ++k) {
+        T w[VEC];
+        VecLoad<T, VEC>::load(W + k * p.w_ld + c0, w);
+#pragma unroll
+        for (int r = 0; r < MR; ++r) CR::run(acc[r], w, CR::prep(X[xoff[r] + k * p.x_s], p.conj_x, p.conj_w), p.conj_w);
+      }
+    }
+  } else if constexpr (VEC > 1) {
     if (full) {
       done = true;
-    using CR = ColRow<T, VEC>;
-    for (; k + (U - 1) * NW < kend; k += U * NW) {
-      T w[U][VEC];
-      typename CR::X xv[U];
+      using CR = ColRow<T, VEC>;
+      for (; k + (U - 1) * NW < kend; k += U * NW) {
+        T w[U][VEC];
+        typename CR::X xv[U][MR];
 #pragma unroll
-      for (int u = 0; u < U; ++u) VecLoad<T, VEC>::load(W + (k + u * NW) * p.w_ld + c0, w[u]);
+        for (int u = 0; u < U; ++u) VecLoad<T, VEC>::load(W + (k + u * NW) * p.w_ld + c0, w[u]);
 #pragma unroll
-      for (int u = 0; u < U; ++u) xv[u] = CR::prep(X[(k + u * NW) * p.x_s], p.conj_x, p.conj_w);
+        for (int u = 0; u < U; ++u)
 #pragma unroll
-      for (int u = 0; u < U; ++u) CR::run(acc, w[u], xv[u], p.conj_w);
-    }
-    for (; k < kend; k += NW) {
-      T w[VEC];
-      VecLoad<T, VEC>::load(W + k * p.w_ld + c0, w);
-      CR::run(acc, w, CR::prep(X[k * p.x_s], p.conj_x, p.conj_w), p.conj_w);
-    }
+          for (int r = 0; r < MR; ++r) xv[u][r] = CR::prep(X[xoff[r] + (k + u * NW) * p.x_s], p.conj_x, p.conj_w);
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+#pragma unroll
+          for (int r = 0; r < MR; ++r) CR::run(acc[r], w[u], xv[u][r], p.conj_w);
+      }
+      for (; k < kend; k += NW) {
+        T w[VEC];
+        VecLoad<T, VEC>::load(W + k * p.w_ld + c0, w);
+#pragma unroll
+        for (int r = 0; r < MR; ++r) CR::run(acc[r], w, CR::prep(X[xoff[r] + k * p.x_s], p.conj_x, p.conj_w), p.conj_w);
+      }
     }
   }
   if (!done) {
     for (; k < kend; k += NW) {
-      const Acc xv = E::load(X[k * p.x_s], p.conj_x);
 #pragma unroll
-      for (int i = 0; i < VEC; ++i)
-        if (c0 + i < p.R) E::mad(acc[i], xv, E::load(W[k * p.w_ld + c0 + i], p.conj_w));
+      for (int r = 0; r < MR; ++r) {
+        const Acc xv = E::load(X[xoff[r] + k * p.x_s], p.conj_x);
+#pragma unroll
+        for (int i = 0; i < VEC; ++i)
+          if (c0 + i < p.R) E::mad(acc[r][i], xv, E::load(W[k * p.w_ld + c0 + i], p.conj_w));
+      }
     }
   }
 
+  // Sum the warps' partials row by row through one shared buffer.  ksplit == 1
+  // stores the result; otherwise the partial is published for the last CTA.
+  const int64_t cbase = cblk * COLS;
+  Acc *ws = p.ksplit > 1 ? (Acc *)p.ws + ((b * p.ksplit + blockIdx.y) * mrows + row0) * p.R : nullptr;
 #pragma unroll
-  for (int i = 0; i < VEC; ++i) red[warp][lane * VEC + i] = acc[i];
-  __syncthreads();
-
-  const int64_t cbase = (int64_t)blockIdx.x * COLS;
-  if (p.ksplit == 1) {
+  for (int r = 0; r < MR; ++r) {
+    if (r >= rows) break;
+    if (r) __syncthreads();  // the previous row's sums have been read
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) red[warp][lane * VEC + i] = acc[r][i];
+    __syncthreads();
     for (int c = threadIdx.x; c < COLS; c += NW * 32) {
       if (cbase + c >= p.R) continue;
       Acc s = red[0][c];
 #pragma unroll
       for (int w = 1; w < NW; ++w) acc_add(s, red[w][c]);
-      gemv_store<T>(p, b, cbase + c, s);
+      if (p.ksplit == 1) gemv_store_m<T>(p, b, row0 + r, cbase + c, s);
+      else ws[r * p.R + cbase + c] = s;
     }
-    return;
   }
+  if (p.ksplit == 1) return;
 
   // Split K across CTAs: publish this CTA's partial, take a ticket; the CTA
   // that draws the last ticket sums all partials in split order (deterministic)
   // and resets the ticket for the next launch.
-  Acc *ws = (Acc *)p.ws + (b * p.ksplit + blockIdx.y) * p.R;
-  for (int c = threadIdx.x; c < COLS; c += NW * 32) {
-    if (cbase + c >= p.R) continue;
-    Acc s = red[0][c];
-#pragma unroll
-    for (int w = 1; w < NW; ++w) acc_add(s, red[w][c]);
-    ws[cbase + c] = s;
-  }
   __threadfence();
   __syncthreads();
   unsigned *ticket = p.tickets + b * gridDim.x + blockIdx.x;
@@ -262,22 +329,25 @@ __global__ void __launch_bounds__(NW * 32) gemv_cols_kernel(const GemvParams p) 
   __syncthreads();
   if (s_ticket != (unsigned)(p.ksplit - 1)) return;
   __threadfence();
-  const Acc *ws0 = (const Acc *)p.ws + b * p.ksplit * p.R;
-  for (int c = threadIdx.x; c < COLS; c += NW * 32) {
-    const int64_t r = cbase + c;
-    if (r >= p.R) continue;
-    Acc s = E::zero();
-    for (int sp = 0; sp < p.ksplit; ++sp) {
-      Acc v;
-      if constexpr (sizeof(Acc) == 8 && !E::is_int) {
-        float2 f = __ldcg((const float2 *)(ws0 + sp * p.R + r));
-        v = *reinterpret_cast<Acc *>(&f);
-      } else {
-        v = __ldcg(ws0 + sp * p.R + r);
+  const Acc *ws0 = (const Acc *)p.ws + b * p.ksplit * mrows * p.R;
+  for (int m = row0; m < row0 + rows; ++m) {
+    for (int c = threadIdx.x; c < COLS; c += NW * 32) {
+      const int64_t r = cbase + c;
+      if (r >= p.R) continue;
+      Acc s = E::zero();
+      for (int sp = 0; sp < p.ksplit; ++sp) {
+        const Acc *src = ws0 + ((int64_t)sp * mrows + m) * p.R + r;
+        Acc v;
+        if constexpr (sizeof(Acc) == 8 && !E::is_int) {
+          float2 f = __ldcg((const float2 *)src);
+          v = *reinterpret_cast<Acc *>(&f);
+        } else {
+          v = __ldcg(src);
+        }
+        acc_add(s, v);
       }
-      acc_add(s, v);
+      gemv_store_m<T>(p, b, m, r, s);
     }
-    gemv_store<T>(p, b, r, s);
   }
   if (threadIdx.x == 0) *ticket = 0u;
 }

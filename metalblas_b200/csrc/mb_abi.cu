@@ -607,10 +607,25 @@ bool plan_3xtf32(const Op &o, int sms, const mb_gemm_desc *d, bool have_ws, Plan
   return true;
 }
 
-int gemv_cols_per_sm(int dt);
+int gemv_cols_per_sm(int dt, int mr);
+
+// Thin products the column GEMV runs with several x rows sharing each load of
+// W (the gemv_bt role, metalblas/shaders/gemv_bt.h:47-269): 16/32-bit floats,
+// up to kGemvMaxRows rows (fp32: kGemvMaxRowsF32, in blocks of 8).
+constexpr int kGemvMaxRows = 4;
+constexpr int kGemvMaxRowsF32 = 32;
+bool gemv_thin_dtype(int dt) { return dt == MB_BF16 || dt == MB_F16 || dt == MB_F32; }
+int64_t gemv_max_rows(int dt) { return dt == MB_F32 ? kGemvMaxRowsF32 : kGemvMaxRows; }
+// rows per CTA block (the kernel's MR)
+int gemv_mr(int dt, int64_t mrows) {
+  if (mrows <= 1) return 1;
+  if (mrows == 2) return 2;
+  return (dt == MB_F32 && mrows > 4) ? 8 : 4;
+}
 
 bool plan_gemv(const Op &o, int sms, const mb_gemm_desc *d, bool have_ws, Plan &pl) {
   GemvParams g{};
+  g.mrows = 1;
   int kind = 0;
   if (o.M == 1) {
     // y[n] = sum_k A(0,k) B(k,n): W = B
@@ -625,12 +640,29 @@ bool plan_gemv(const Op &o, int sms, const mb_gemm_desc *d, bool have_ws, Plan &
     if (o.a_cs == 1) { kind = PK_GEMV_ROWS; g.w_ld = o.a_rs; }
     else if (o.a_rs == 1) { kind = PK_GEMV_COLS; g.w_ld = o.a_cs; }
   }
+  if (!kind && gemv_thin_dtype(o.dt) && o.M <= gemv_max_rows(o.dt) && o.b_cs == 1) {
+    // thin M: y[m][n] = sum_k A(m,k) B(k,n), W = B (row-major) read once
+    g.R = o.N; g.K = o.K; g.W = o.B; g.X = o.A; g.x_s = o.a_cs; g.y_s = o.c_cs; g.bias_s = o.bias_cs;
+    g.sW = o.sB; g.sX = o.sA; g.conj_w = o.conj_b; g.conj_x = o.conj_a;
+    g.mrows = (int)o.M; g.x_rs = o.a_rs; g.y_rs = o.c_rs; g.bias_rs = o.bias_rs;
+    kind = PK_GEMV_COLS; g.w_ld = o.b_rs;
+  } else if (!kind && gemv_thin_dtype(o.dt) && o.N <= gemv_max_rows(o.dt) && o.a_rs == 1) {
+    // thin N: the transposed product, W = A (column-major), x rows = B's columns
+    g.R = o.M; g.K = o.K; g.W = o.A; g.X = o.B; g.x_s = o.b_rs; g.y_s = o.c_rs; g.bias_s = o.bias_rs;
+    g.sW = o.sA; g.sX = o.sB; g.conj_w = o.conj_a; g.conj_x = o.conj_b;
+    g.mrows = (int)o.N; g.x_rs = o.b_cs; g.y_rs = o.c_cs; g.bias_rs = o.bias_cs;
+    kind = PK_GEMV_COLS; g.w_ld = o.a_cs;
+  }
   if (!kind) return false;
   g.Y = o.C; g.bias = o.bias; g.batch = o.batch; g.sY = o.sC; g.sBias = o.bias_bs;
   const int esz = elem_size(o.dt);
   const int vmax = 16 / esz;
   const bool wvec = aligned16(g.W) && (g.w_ld % vmax == 0) && (o.batch <= 1 || (g.sW % vmax == 0));
   pl.vec = wvec ? vmax : 1;
+  if (g.mrows > 1 && pl.vec == 1) return false;  // thin kernels are vectorised only
+  const int mr = gemv_mr(o.dt, g.mrows);
+  g.mrb = (int)ceil_div(g.mrows, mr);
+
   g.x_vec = (g.x_s == 1 && aligned16(g.X) && (o.batch <= 1 || g.sX % vmax == 0)) ? 1 : 0;
   g.ksplit = 1;
   g.kchunk = std::max<int64_t>(g.K, 1);
@@ -641,12 +673,13 @@ bool plan_gemv(const Op &o, int sms, const mb_gemm_desc *d, bool have_ws, Plan &
     // one full wave of resident CTAs: a partial second wave leaves most SMs
     // idle while it streams (672 CTAs on 592 slots measured 0.78 of HBM at
     // N = 28672)
-    const int64_t want = (int64_t)gemv_cols_per_sm(o.dt) * sms;
-    int64_t ks = d->split_k > 0 ? d->split_k : std::max<int64_t>(1, want / (ctas_x * o.batch));
+    const int64_t want = (int64_t)gemv_cols_per_sm(o.dt, mr) * sms;
+    const int64_t zb = o.batch * g.mrb;  // CTAs per K chunk: column blocks x row blocks x batches
+    int64_t ks = d->split_k > 0 ? d->split_k : std::max<int64_t>(1, want / (ctas_x * zb));
     ks = std::max<int64_t>(1, std::min<int64_t>(ks, ceil_div(g.K, 64)));  // >= 64 rows per CTA
     if (ks > 65535) ks = 65535;
     if (ks > 1 && !have_ws) ks = 1;
-    if (o.batch * ctas_x > kMaxTickets) ks = 1;  // not enough ticket counters
+    if (zb * ctas_x > kMaxTickets) ks = 1;  // not enough ticket counters
     if (ks > 1) {
       // whole unrolled steps per chunk: 8 warps x 8 rows in flight per lane
       g.kchunk = round_up(ceil_div(g.K, ks), 64);
@@ -655,7 +688,7 @@ bool plan_gemv(const Op &o, int sms, const mb_gemm_desc *d, bool have_ws, Plan &
     g.ksplit = (int)ks;
     if (ks > 1) {
       const int64_t accb = acc_is_8byte(o.dt) ? 8 : 4;
-      pl.ws_bytes = kTicketBytes + ks * o.batch * g.R * accb;
+      pl.ws_bytes = kTicketBytes + ks * o.batch * g.mrows * g.R * accb;
     }
   } else if (pl.vec > 1 && g.x_vec) {
     // Staged-x rows kernel: CTAs of kGemvRowsPerCta rows.  A short CTA pays a
@@ -693,7 +726,10 @@ int make_plan(const mb_gemm_desc *d, const Op &o, int sms, bool have_ws, Plan &p
   if (o.M == 0 || o.N == 0 || o.batch == 0) { pl.kind = PK_EMPTY; return MB_OK; }
   const int be = d->backend;
   if (be == MB_BACKEND_GEMV) {
-    if (!(o.M == 1 || o.N == 1)) return fail(MB_ERR_INVALID, "gemv backend requires M==1 or N==1");
+    const bool thin = gemv_thin_dtype(o.dt) && std::min(o.M, o.N) <= gemv_max_rows(o.dt);
+    if (!(o.M == 1 || o.N == 1 || thin))
+      return fail(MB_ERR_INVALID, "gemv backend requires M==1 or N==1 (or min(M, N) <= 4 for 16-bit floats, "
+                                  "<= 32 for fp32)");
     if (o.K == 0) { pl.kind = PK_SIMT; return MB_OK; }
     if (plan_gemv(o, sms, d, have_ws, pl)) return MB_OK;
     pl.kind = PK_SIMT;  // no unit stride: CUDA-core kernel reads it in place
@@ -717,6 +753,11 @@ int make_plan(const mb_gemm_desc *d, const Op &o, int sms, bool have_ws, Plan &p
   }
   // AUTO
   if ((o.M == 1 || o.N == 1) && plan_gemv(o, sms, d, have_ws, pl)) return MB_OK;
+  // fp32 thin products: the column GEMV with the rows sharing W's loads streams
+  // W at 0.5-1.0 of HBM where the FFMA tile kernel measured 0.02-0.06 (B200,
+  // M = 2..4, K and N 4096..16384); 3xTF32 would move ~5x the bytes.  16-bit
+  // floats stay on the tensor cores, measured faster there.
+  if (o.dt == MB_F32 && std::min(o.M, o.N) <= kGemvMaxRowsF32 && plan_gemv(o, sms, d, have_ws, pl)) return MB_OK;
   if (o.dt == MB_C32 && plan_c32(o, sms, d, have_ws, pl)) return MB_OK;
   // fp32: 3xTF32 on the tensor cores when its estimated time beats the CUDA-core
   // kernel's.  3xTF32: the split pass moves 12 bytes per operand element and the
@@ -853,9 +894,21 @@ int launch_gemv(const Plan &pl, const EpiScalars &e, void *ws, cudaStream_t st) 
   const unsigned gz = (unsigned)std::min<int64_t>(g.batch, 65535);
   if (g.batch > 65535) return fail(MB_ERR_INVALID, "batch too large for GEMV");
   if (pl.kind == PK_GEMV_COLS) {
-    dim3 grid((unsigned)pl.gemv_ctas_x, (unsigned)g.ksplit, gz);
-    if (pl.vec > 1) gemv_cols_kernel<T, V, NW><<<grid, NW * 32, 0, st>>>(g);
-    else gemv_cols_kernel<T, 1, NW><<<dim3((unsigned)ceil_div(g.R, 32), (unsigned)g.ksplit, gz), NW * 32, 0, st>>>(g);
+    dim3 grid((unsigned)(pl.gemv_ctas_x * std::max(g.mrb, 1)), (unsigned)g.ksplit, gz);
+    constexpr bool thin = std::is_same<T, __nv_bfloat16>::value || std::is_same<T, __half>::value ||
+                          std::is_same<T, float>::value;
+    if (pl.vec > 1) {
+      if constexpr (thin) {
+        const int mr = gemv_mr(std::is_same<T, float>::value ? MB_F32 : MB_BF16, g.mrows);
+        if (mr == 8) {
+          if constexpr (std::is_same<T, float>::value) gemv_cols_kernel<T, V, NW, 8><<<grid, NW * 32, 0, st>>>(g);
+        } else if (mr == 4) gemv_cols_kernel<T, V, NW, 4><<<grid, NW * 32, 0, st>>>(g);
+        else if (mr == 2) gemv_cols_kernel<T, V, NW, 2><<<grid, NW * 32, 0, st>>>(g);
+        else gemv_cols_kernel<T, V, NW><<<grid, NW * 32, 0, st>>>(g);
+      } else {
+        gemv_cols_kernel<T, V, NW><<<grid, NW * 32, 0, st>>>(g);
+      }
+    } else gemv_cols_kernel<T, 1, NW><<<dim3((unsigned)ceil_div(g.R, 32), (unsigned)g.ksplit, gz), NW * 32, 0, st>>>(g);
   } else {
     if (pl.vec > 1 && g.x_vec) {
       constexpr int RPW = kGemvRowsPerWarp;  // x staged in shared memory
@@ -1143,23 +1196,34 @@ int by_dtype(int dt, F &&f) {
 
 // Resident CTAs per SM of the vectorised column GEMV for dtype dt, from the
 // occupancy calculator; 4 when no device answers (plan queries on a host).
-int gemv_cols_per_sm(int dt) {
-  static std::atomic<int> cache[MB_I64 + 1];
+int gemv_cols_per_sm(int dt, int mr) {
+  static std::atomic<int> cache[MB_I64 + 1][4];
   if (dt < 0 || dt > MB_I64) return 4;
-  int v = cache[dt].load(std::memory_order_relaxed);
+  const int mi = mr == 8 ? 3 : mr == 4 ? 2 : mr == 2 ? 1 : 0;
+  int v = cache[dt][mi].load(std::memory_order_relaxed);
   if (v > 0) return v;
-  v = by_dtype(dt, [](auto *p) -> int {
-    using T = std::remove_pointer_t<decltype(p)>;
+  auto occ = [](auto kernel) -> int {
     int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_cols_kernel<T, 16 / sizeof(T), kGemvWarps>,
-                                                      kGemvWarps * 32, 0) != cudaSuccess) {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, kGemvWarps * 32, 0) != cudaSuccess) {
       cudaGetLastError();
       return 0;
     }
     return n;
+  };
+  v = by_dtype(dt, [&](auto *p) -> int {
+    using T = std::remove_pointer_t<decltype(p)>;
+    constexpr int V = 16 / sizeof(T);
+    if constexpr (std::is_same<T, __nv_bfloat16>::value || std::is_same<T, __half>::value ||
+                  std::is_same<T, float>::value) {
+      if constexpr (std::is_same<T, float>::value)
+        if (mi == 3) return occ(gemv_cols_kernel<T, V, kGemvWarps, 8>);
+      if (mi == 2) return occ(gemv_cols_kernel<T, V, kGemvWarps, 4>);
+      if (mi == 1) return occ(gemv_cols_kernel<T, V, kGemvWarps, 2>);
+    }
+    return occ(gemv_cols_kernel<T, V, kGemvWarps>);
   });
   if (v <= 0) return 4;
-  cache[dt].store(v, std::memory_order_relaxed);
+  cache[dt][mi].store(v, std::memory_order_relaxed);
   return v;
 }
 
@@ -1232,7 +1296,12 @@ int mb_plan_query(const mb_gemm_desc *d, char *buf, int buflen) {
   char tmp[256];
   switch (pl.kind) {
     case PK_EMPTY: snprintf(tmp, sizeof(tmp), "empty"); break;
-    case PK_GEMV_COLS: snprintf(tmp, sizeof(tmp), "gemv_cols vec=%d ksplit=%d", pl.vec, pl.g.ksplit); break;
+    case PK_GEMV_COLS:
+      if (pl.g.mrows > 1)
+        snprintf(tmp, sizeof(tmp), "gemv_cols vec=%d ksplit=%d rows=%d", pl.vec, pl.g.ksplit, pl.g.mrows);
+      else
+        snprintf(tmp, sizeof(tmp), "gemv_cols vec=%d ksplit=%d", pl.vec, pl.g.ksplit);
+      break;
     case PK_GEMV_ROWS:
       snprintf(tmp, sizeof(tmp), "gemv_rows vec=%d x_smem=%d ksplit=%d", pl.vec, (pl.vec > 1 && pl.g.x_vec) ? 1 : 0,
                pl.g.ksplit);

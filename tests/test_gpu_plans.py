@@ -168,6 +168,54 @@ def test_gemv_rows_k_split(dtype):
             assert ok, f"{(B, N, K)} split={split} addmv err={err}"
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32], ids=NAME.get)
+def test_gemv_thin_rows(dtype):
+    """Thin products on the column GEMV with several x rows sharing each load
+    of W (M = 2..4 with W row-major, and the mirrored N = 2..4 with A
+    column-major): batches, K splits (ragged chunks), full and broadcast bias
+    epilogues, and an N that is not a multiple of the vector width (no thin
+    plan: the library falls back to another kernel); fp32 also with row
+    blocks."""
+    gen = torch.Generator().manual_seed(12)
+    # fp32 takes up to 32 rows, in blocks of 8 (9 and 20: ragged last block)
+    for M in (2, 3, 4) + ((7, 9, 20) if dtype == torch.float32 else ()):
+        for (B, K, N) in [(1, 5000, 1000), (3, 1000, 2056), (2, 4096, 333)]:
+            x = rand((B, M, K), dtype, gen)
+            w = rand((B, K, N), dtype, gen)
+            bias = rand((B, M, N), dtype, gen)
+            bvec = rand((N,), dtype, gen)
+            ref = orc.product(to_np(x), to_np(w), NAME[dtype])
+            fref = orc.fused(to_np(bias), to_np(x), to_np(w), 2, 3, NAME[dtype])
+            vref = orc.fused(to_np(bvec), to_np(x), to_np(w), 0.5, 1, NAME[dtype])
+            a3, b3, c3 = (K, 1, M * K), (N, 1, K * N), (N, 1, M * N)
+            for split in (0, 1, 2, 5):
+                for be in (_lib.MB_BACKEND_GEMV, _lib.MB_BACKEND_AUTO):
+                    c = torch.empty(B, M, N, dtype=dtype, device=x.device)
+                    dispatch._launch(x, w, c, M, N, K, B, a3, b3, c3, backend=be, split_k=split if be else 0,
+                                     autotune=False)
+                    ok, err = orc.check(to_np(c), ref, NAME[dtype])
+                    assert ok, f"M={M} {(B, K, N)} split={split} backend={be} err={err}"
+                c = torch.empty(B, M, N, dtype=dtype, device=x.device)
+                dispatch._launch(x, w, c, M, N, K, B, a3, b3, c3, epilogue=(bias, (N, 1, M * N), 2, 3, True, True),
+                                 backend=_lib.MB_BACKEND_GEMV, split_k=split, autotune=False)
+                ok, err = orc.check(to_np(c), fref, NAME[dtype])
+                assert ok, f"M={M} {(B, K, N)} split={split} addmm err={err}"
+                dispatch._launch(x, w, c, M, N, K, B, a3, b3, c3, epilogue=(bvec, (0, 1, 0), 0.5, 1, True, True),
+                                 backend=_lib.MB_BACKEND_GEMV, split_k=split, autotune=False)
+                ok, err = orc.check(to_np(c), vref, NAME[dtype])
+                assert ok, f"M={M} {(B, K, N)} split={split} bias-vector err={err}"
+            # mirrored: C[N, M] = A[N, K] @ x^T with A column-major (stored [K, N])
+            at = rand((B, K, N), dtype, gen)
+            xt = rand((B, K, M), dtype, gen)
+            ref_t = orc.product(to_np(at).transpose(0, 2, 1), to_np(xt), NAME[dtype])
+            for split in (0, 3):
+                c = torch.empty(B, N, M, dtype=dtype, device=x.device)
+                dispatch._launch(at, xt, c, N, M, K, B, (1, N, K * N), (M, 1, K * M), (M, 1, N * M),
+                                 backend=_lib.MB_BACKEND_GEMV, split_k=split, autotune=False)
+                ok, err = orc.check(to_np(c), ref_t, NAME[dtype])
+                assert ok, f"thin N={M} {(B, K, N)} split={split} err={err}"
+
+
 def test_no_device_timeouts():
     from metalblas_b200 import kernels
     assert kernels.device_status() == 0
