@@ -761,16 +761,19 @@ int make_plan(const mb_gemm_desc *d, const Op &o, int sms, bool have_ws, Plan &p
   if (o.dt == MB_C32 && plan_c32(o, sms, d, have_ws, pl)) return MB_OK;
   // fp32: 3xTF32 on the tensor cores when its estimated time beats the CUDA-core
   // kernel's.  3xTF32: the split pass moves 12 bytes per operand element and the
-  // GEMM reads 8, at ~6 TB/s, plus the FLOPs at ~190 TFLOP/s and ~6 us of extra
-  // launches.  FFMA: ~40 TFLOP/s when its 128 x 128 tiles fill two CTAs per SM,
+  // GEMM reads 8 (measured ~36 B of time per element at ~6 TB/s on thin and
+  // small shapes, B200), plus the FLOPs at ~190 TFLOP/s and ~6 us of extra
+  // launches.  FFMA: ~40 TFLOP/s on the work of its 128 x 128 tiles (padding
+  // included: a thin product wastes most of each tile) when they fill every SM,
   // proportionally less when they do not (it has no split-K).
-  if (o.dt == MB_F32 && g_fp32_tf32x3 && o.M >= 16 && o.N >= 16) {
+  if (o.dt == MB_F32 && g_fp32_tf32x3) {
     const double bt = (double)std::max<int64_t>(o.batch, 1);
     const double flops = 2.0 * o.M * o.N * o.K * bt;
     const double opnd = (double)o.M * o.K * (o.sA ? bt : 1.0) + (double)o.K * o.N * (o.sB ? bt : 1.0);
     const double ctas = (double)ceil_div(o.M, 128) * ceil_div(o.N, 128) * bt;
-    const double t_simt = flops / (40.0e12 * std::min(1.0, ctas / (2.0 * sms)));
-    const double t_x3 = 20.0 * 4.0 * opnd / 6.0e12 + flops / 190.0e12 + 6.0e-6;
+    const double tile_flops = 2.0 * 128.0 * 128.0 * (double)o.K * ctas;
+    const double t_simt = tile_flops / (40.0e12 * std::min(1.0, ctas / (double)sms));
+    const double t_x3 = 36.0 * opnd / 6.0e12 + flops / 190.0e12 + 6.0e-6;
     if (t_x3 < t_simt && plan_3xtf32(o, sms, d, have_ws, pl)) return MB_OK;
   }
   if (is_tc_dtype(o.dt)) {
