@@ -670,19 +670,35 @@ bool plan_gemv(const Op &o, int sms, const mb_gemm_desc *d, bool have_ws, Plan &
     const int64_t cols_per_cta = 32 * pl.vec;
     const int64_t ctas_x = ceil_div(g.R, cols_per_cta);
     pl.gemv_ctas_x = ctas_x;
-    // one full wave of resident CTAs: a partial second wave leaves most SMs
-    // idle while it streams (672 CTAs on 592 slots measured 0.78 of HBM at
-    // N = 28672)
-    const int64_t want = (int64_t)gemv_cols_per_sm(o.dt, mr) * sms;
+    // K split by wave efficiency: the CTAs (column blocks x row blocks x
+    // batches x splits) should fill whole waves of the resident slots; a
+    // nearly empty last wave leaves most SMs idle while it streams (672 CTAs
+    // on 592 slots measured 0.78 of HBM at N = 28672, 560 CTAs 0.96).  Each
+    // extra split costs ~1% (partials, a shorter stream per CTA).
+    const int64_t slots = (int64_t)gemv_cols_per_sm(o.dt, mr) * sms;
     const int64_t zb = o.batch * g.mrb;  // CTAs per K chunk: column blocks x row blocks x batches
-    int64_t ks = d->split_k > 0 ? d->split_k : std::max<int64_t>(1, want / (ctas_x * zb));
-    ks = std::max<int64_t>(1, std::min<int64_t>(ks, ceil_div(g.K, 64)));  // >= 64 rows per CTA
-    if (ks > 65535) ks = 65535;
+    // whole unrolled steps per chunk: 8 warps x 8 rows in flight per lane
+    auto chunk_of = [&](int64_t k) { return round_up(ceil_div(g.K, k), 64); };
+    const int64_t ks_cap = std::min<int64_t>({ceil_div(g.K, 64), 65535, 3 * std::max<int64_t>(1, slots / (ctas_x * zb)) + 2});
+    int64_t ks = 1;
+    if (d->split_k > 0) {
+      ks = std::min<int64_t>(d->split_k, std::min<int64_t>(ceil_div(g.K, 64), 65535));
+    } else {
+      double best = -1.0;
+      for (int64_t k = 1; k <= ks_cap; ++k) {
+        const int64_t eff_k = ceil_div(g.K, chunk_of(k));
+        if (eff_k != k) continue;
+        const double units = (double)(ctas_x * zb * k);
+        const double waves = std::ceil(units / (double)slots);
+        const double score = units / (waves * slots) * (1.0 - 0.01 * (k - 1));
+        if (score > best + 1e-9) { best = score; ks = k; }
+      }
+    }
+    ks = std::max<int64_t>(1, ks);
     if (ks > 1 && !have_ws) ks = 1;
     if (zb * ctas_x > kMaxTickets) ks = 1;  // not enough ticket counters
     if (ks > 1) {
-      // whole unrolled steps per chunk: 8 warps x 8 rows in flight per lane
-      g.kchunk = round_up(ceil_div(g.K, ks), 64);
+      g.kchunk = chunk_of(ks);
       ks = ceil_div(g.K, g.kchunk);
     }
     g.ksplit = (int)ks;
