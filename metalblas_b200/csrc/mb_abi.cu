@@ -172,7 +172,9 @@ constexpr int kGemvWarps = 8;         // warps per GEMV CTA
 constexpr int kGemvRowsPerWarp = 2;   // staged-x rows kernel
 constexpr int64_t kGemvRowsPerCta = kGemvWarps * kGemvRowsPerWarp;
 
-enum PlanKind { PK_EMPTY = 0, PK_GEMV_COLS, PK_GEMV_ROWS, PK_TC, PK_SIMT, PK_TC_C32, PK_TC_PACKED, PK_TC_3XTF32 };
+enum PlanKind {
+  PK_EMPTY = 0, PK_GEMV_COLS, PK_GEMV_ROWS, PK_TC, PK_SIMT, PK_TC_C32, PK_TC_PACKED, PK_TC_3XTF32, PK_TC_C64X3
+};
 
 struct Plan {
   int kind = PK_EMPTY;
@@ -607,6 +609,38 @@ bool plan_3xtf32(const Op &o, int sms, const mb_gemm_desc *d, bool have_ws, Plan
   return true;
 }
 
+EpiScalars make_epi(const mb_gemm_desc *d);
+
+// complex64 as one real fp32 GEMM on the tensor cores through 3xTF32, in the
+// block form of c32.cuh: C' [M x 2N] (C's storage) = A' [M x 2K] B' [2K x 2N].
+// The split pass reads the complex operands directly (SplitArgs modes 1 and 2),
+// so A and B keep their complex strides here.  The reference computes complex64
+// as real products on its fp32 path (metalblas/complex_dispatch.py:69-115).
+Op c64_real(const Op &o) {
+  Op r = o;
+  r.dt = MB_F32;
+  r.N = 2 * o.N;
+  r.K = 2 * o.K;
+  r.c_rs = 2 * o.c_rs; r.c_cs = 1; r.sC = 2 * o.sC;
+  r.bias_rs = 2 * o.bias_rs; r.bias_cs = 1; r.bias_bs = 2 * o.bias_bs;
+  r.conj_a = r.conj_b = 0;
+  return r;
+}
+
+bool plan_c64x3(const Op &o, int sms, const mb_gemm_desc *d, bool have_ws, Plan &pl) {
+  if (o.dt != MB_C64 || !have_ws || o.M < 1 || o.N < 1 || o.K < 1) return false;
+  if (o.c_cs != 1 || o.c_rs < o.N) return false;  // C' must be a row-major real view
+  if (o.N >= (1ll << 30) || o.K >= (1ll << 30)) return false;
+  // the real epilogue applies alpha / beta per component: real scalars only,
+  // and a bias whose components sit next to each other along N
+  const EpiScalars e = make_epi(d);
+  if (e.enabled && (e.alpha_im != 0.f || e.beta_im != 0.f)) return false;
+  if (e.enabled && e.beta_nz && o.bias_cs != 1) return false;
+  if (!plan_3xtf32(c64_real(o), sms, d, have_ws, pl)) return false;
+  pl.kind = PK_TC_C64X3;
+  return true;
+}
+
 int gemv_cols_per_sm(int dt, int mr);
 
 // Thin products the column GEMV runs with several x rows sharing each load of
@@ -761,7 +795,13 @@ int make_plan(const mb_gemm_desc *d, const Op &o, int sms, bool have_ws, Plan &p
       if (plan_3xtf32(o, sms, d, have_ws, pl)) return MB_OK;
       return fail(MB_ERR_UNSUPPORTED, "tensor-core fp32 (3xTF32) needs a workspace for the split operands");
     }
-    if (!is_tc_dtype(o.dt)) return fail(MB_ERR_UNSUPPORTED, "tensor-core backend supports bf16/fp16/fp32/int8/uint8 only");
+    if (o.dt == MB_C64) {  // complex64 on the tensor cores is one real 3xTF32 GEMM
+      if (plan_c64x3(o, sms, d, have_ws, pl)) return MB_OK;
+      return fail(MB_ERR_UNSUPPORTED, "tensor-core complex64 (3xTF32) needs a row-major output, real alpha/beta, "
+                                      "a bias contiguous along N and a workspace");
+    }
+    if (!is_tc_dtype(o.dt))
+      return fail(MB_ERR_UNSUPPORTED, "tensor-core backend supports bf16/fp16/fp32/complex32/complex64/int8/uint8 only");
     if (plan_tc_any(o, sms, d, have_ws, pl)) return MB_OK;
     if (plan_packed(o, sms, d, have_ws, pl)) return MB_OK;
     return fail(MB_ERR_UNSUPPORTED, "tensor-core backend: operands not TMA-addressable (need a unit stride, "
@@ -791,6 +831,18 @@ int make_plan(const mb_gemm_desc *d, const Op &o, int sms, bool have_ws, Plan &p
     const double t_simt = tile_flops / (40.0e12 * std::min(1.0, ctas / (double)sms));
     const double t_x3 = 36.0 * opnd / 6.0e12 + flops / 190.0e12 + 6.0e-6;
     if (t_x3 < t_simt && plan_3xtf32(o, sms, d, have_ws, pl)) return MB_OK;
+  }
+  // complex64: the same estimate on the real form (8MNK real FLOPs; A' is
+  // M x 2K, B' 2K x 2N; the FFMA kernel's complex tiles are 64 x 64).
+  if (o.dt == MB_C64 && g_fp32_tf32x3) {
+    const double bt = (double)std::max<int64_t>(o.batch, 1);
+    const double flops = 8.0 * o.M * o.N * o.K * bt;
+    const double opnd = 2.0 * o.M * o.K * (o.sA ? bt : 1.0) + 4.0 * o.K * o.N * (o.sB ? bt : 1.0);
+    const double ctas = (double)ceil_div(o.M, 64) * ceil_div(o.N, 64) * bt;
+    const double tile_flops = 8.0 * 64.0 * 64.0 * (double)o.K * ctas;
+    const double t_simt = tile_flops / (40.0e12 * std::min(1.0, ctas / (double)sms));
+    const double t_x3 = 36.0 * opnd / 6.0e12 + flops / 190.0e12 + 6.0e-6;
+    if (t_x3 < t_simt && plan_c64x3(o, sms, d, have_ws, pl)) return MB_OK;
   }
   if (is_tc_dtype(o.dt)) {
     if (plan_tc_any(o, sms, d, have_ws, pl)) return MB_OK;
@@ -1196,6 +1248,38 @@ int launch_3xtf32(const Op &o, const Plan &pl, const EpiScalars &e, void *ws, in
   return launch_simt<float>(o, e, st, flag);
 }
 
+// complex64 through 3xTF32: split A' and B'ᵀ straight from the complex
+// operands, the real GEMM with the real epilogue, then the gated FFMA
+// recompute of the complex product when an input held inf or NaN.
+int launch_c64x3(const Op &o, const Plan &pl, const EpiScalars &e, void *ws, int sms, cudaStream_t st) {
+  char *w = reinterpret_cast<char *>(ws);
+  float *ahi = reinterpret_cast<float *>(w + pl.x3_ahi), *alo = reinterpret_cast<float *>(w + pl.x3_alo);
+  float *bhi = reinterpret_cast<float *>(w + pl.x3_bhi), *blo = reinterpret_cast<float *>(w + pl.x3_blo);
+  int *flag = reinterpret_cast<int *>(w + pl.x3_flag);
+  int rc = cuda_check(cudaMemsetAsync(flag, 0, sizeof(int), st), "complex64 3xTF32 clear flag");
+  if (rc) return rc;
+  const Op r = c64_real(o);
+  auto split = [&](const void *src, float *hi, float *lo, int64_t rows, int64_t cols, int64_t rs, int64_t cs,
+                   int64_t bs, int64_t batches, int mode, const char *what) {
+    SplitArgs a{static_cast<const float *>(src), hi, lo, flag, rows, cols, rs, cs, bs, batches, pl.x3_ldk,
+                mode, o.conj_a, o.conj_b};
+    const int64_t tiles = batches * ceil_div(rows, 32) * ceil_div(cols, 32);
+    split_tf32_kernel<<<(unsigned)std::max<int64_t>(1, std::min<int64_t>(tiles, (int64_t)sms * 16)), dim3(32, 8), 0,
+                        st>>>(a);
+    return cuda_check(cudaGetLastError(), what);
+  };
+  // A' (M x 2K) and B'ᵀ (2N x 2K); complex strides
+  rc = split(o.A, ahi, alo, o.M, r.K, o.a_rs, o.a_cs, o.sA, pl.x3_a_batches, 1, "complex64 3xTF32 split A");
+  if (!rc) rc = split(o.B, bhi, blo, r.N, r.K, o.b_cs, o.b_rs, o.sB, pl.x3_b_batches, 2, "complex64 3xTF32 split B");
+  if (rc) return rc;
+  EpiScalars er = e;
+  er.cplx = 0;
+  const Op x = x3_op(r, pl, ahi, alo, bhi, blo);
+  rc = launch_tc<float>(pl.swap ? swapped(x) : x, pl, er, ws, sms, st);
+  if (rc) return rc;
+  return launch_simt<float2>(o, e, st, flag);
+}
+
 template <class F>
 int by_dtype(int dt, F &&f) {
   switch (dt) {
@@ -1336,8 +1420,9 @@ int mb_plan_query(const mb_gemm_desc *d, char *buf, int buflen) {
                pl.bn, pl.splits, pl.pair, (long long)pl.tiles_m, (long long)pl.tiles_n, (long long)pl.ws_bytes);
       break;
     case PK_TC_3XTF32:
-      snprintf(tmp, sizeof(tmp), "tc_3xtf32 bn=%d split=%d dp=%lld half=%d pair=%d sk=%d swap=%d tiles=%lldx%lld ws=%lld",
-               pl.bn, pl.splits, (long long)pl.dp_tiles, pl.tail_half, pl.pair, pl.sk, pl.swap, (long long)pl.tiles_m,
+    case PK_TC_C64X3:
+      snprintf(tmp, sizeof(tmp), "%s bn=%d split=%d dp=%lld half=%d pair=%d sk=%d swap=%d tiles=%lldx%lld ws=%lld",
+               pl.kind == PK_TC_C64X3 ? "tc_c64x3" : "tc_3xtf32", pl.bn, pl.splits, (long long)pl.dp_tiles, pl.tail_half, pl.pair, pl.sk, pl.swap, (long long)pl.tiles_m,
                (long long)pl.tiles_n, (long long)pl.ws_bytes);
       break;
     case PK_TC_PACKED:
@@ -1379,6 +1464,9 @@ int mb_gemm(const mb_gemm_desc *d, void *stream) {
       case PK_TC_3XTF32:
         if constexpr (std::is_same_v<T, float>) return launch_3xtf32(o, pl, e, d->workspace, sms, st);
         else return fail(MB_ERR_UNSUPPORTED, "3xTF32 path for a non-fp32 dtype");
+      case PK_TC_C64X3:
+        if constexpr (std::is_same_v<T, float2>) return launch_c64x3(o, pl, e, d->workspace, sms, st);
+        else return fail(MB_ERR_UNSUPPORTED, "complex64 3xTF32 path for a non-complex64 dtype");
       default: return launch_simt<T>(o, e, st);
     }
   });
@@ -1546,7 +1634,7 @@ int mb_gemm_noalloc(const mb_gemm_desc *d, void *stream) {
   int rc = plan_for(&q, pl, o, sms);
   if (rc) return rc;
   if (pl.kind == PK_EMPTY) return MB_OK;
-  if ((pl.kind == PK_TC_C32 || pl.kind == PK_TC_PACKED || pl.kind == PK_TC_3XTF32) &&
+  if ((pl.kind == PK_TC_C32 || pl.kind == PK_TC_PACKED || pl.kind == PK_TC_3XTF32 || pl.kind == PK_TC_C64X3) &&
       pl.ws_bytes > (int64_t)MB_NOALLOC_SCRATCH_BYTES &&
       q.backend == MB_BACKEND_AUTO) {
     // complex32 on the tensor cores needs its expanded B' in scratch, packed
@@ -1585,6 +1673,9 @@ int mb_gemm_noalloc(const mb_gemm_desc *d, void *stream) {
       case PK_TC_3XTF32:
         if constexpr (std::is_same_v<T, float>) return launch_3xtf32(o, pl, e, scratch, sms, st);
         else return fail(MB_ERR_UNSUPPORTED, "3xTF32 path for a non-fp32 dtype");
+      case PK_TC_C64X3:
+        if constexpr (std::is_same_v<T, float2>) return launch_c64x3(o, pl, e, scratch, sms, st);
+        else return fail(MB_ERR_UNSUPPORTED, "complex64 3xTF32 path for a non-complex64 dtype");
       default: return launch_simt<T>(o, e, st);
     }
   });

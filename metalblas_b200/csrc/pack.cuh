@@ -89,9 +89,27 @@ struct SplitArgs {
   float *hi, *lo;
   int *nonfinite;       // set to 1 when any input value is inf or NaN
   int64_t rows, cols;   // output rows x cols (cols is the K dimension)
-  int64_t rs, cs, bs;   // source strides of element (row, col) and batch
+  int64_t rs, cs, bs;   // source strides of element (row, col) and batch (complex units in modes 1, 2)
   int64_t batch, ld;    // batches; destination row pitch (elements, 16-byte multiple)
+  // complex64 as one real GEMM (the c32.cuh block form):
+  //   mode 0: real source, element (r, c) at src[r*rs + c*cs]
+  //   mode 1: A' = component c&1 of complex A(r, c/2) at complex index r*rs + (c/2)*cs
+  //   mode 2: B'ᵀ (2N x 2K) from complex B(k = c/2, n = r/2) at complex index
+  //           (r/2)*rs + (c/2)*cs: the 2 x 2 block [[re, -s*im'], [im', s*re]]
+  //           (rows r&1, columns c&1) with im' = -im for conj(B), s = -1 for conj(A)
+  int mode, conj_a, conj_b;
 };
+
+__device__ __forceinline__ float split_load(const SplitArgs &a, const float *src, int64_t r, int64_t c) {
+  if (a.mode == 0) return src[r * a.rs + c * a.cs];
+  const int64_t q = (a.mode == 1 ? r : (r >> 1)) * a.rs + (c >> 1) * a.cs;
+  const float2 v = reinterpret_cast<const float2 *>(src)[q];
+  if (a.mode == 1) return (c & 1) ? v.y : v.x;
+  const float im = a.conj_b ? -v.y : v.y;
+  const float s = a.conj_a ? -1.f : 1.f;
+  if ((r & 1) == 0) return (c & 1) ? -s * im : v.x;
+  return (c & 1) ? s * v.x : im;
+}
 
 // dst[b][r][c] = split(src(b, r, c)) through a 32 x 32 shared-memory tile, so
 // both the source read (along whichever of r / c is contiguous) and the
@@ -106,11 +124,11 @@ __global__ void __launch_bounds__(256) split_tf32_kernel(const SplitArgs a) {
     const int64_t b = t / (rt * ct);
     const int64_t rem = t - b * rt * ct;
     const int64_t r0 = (rem / ct) * 32, c0 = (rem % ct) * 32;
-    const float *src = a.src + b * a.bs;
+    const float *src = a.src + b * a.bs * (a.mode ? 2 : 1);
 #pragma unroll
     for (int i = ty; i < 32; i += 8) {
       const int64_t r = r0 + (c_fast ? i : tx), c = c0 + (c_fast ? tx : i);
-      const float v = (r < a.rows && c < a.cols) ? src[r * a.rs + c * a.cs] : 0.f;
+      const float v = (r < a.rows && c < a.cols) ? split_load(a, src, r, c) : 0.f;
       if (c_fast) tile[i][tx] = v; else tile[tx][i] = v;
     }
     __syncthreads();

@@ -300,6 +300,53 @@ def test_fp32_3xtf32_matches_oracle():
     assert torch.equal(torch.isnan(got), torch.isnan(simd)) and torch.equal(torch.isinf(got), torch.isinf(simd))
 
 
+def test_complex64_3xtf32_matches_oracle():
+    """complex64 on the tensor cores: one real 3xTF32 GEMM in the block form
+    C' = A' B' (A' the interleaved storage of A, B' the 2x2 real blocks of B),
+    with the split pass reading the complex operands in place.  Checked within
+    the 1e-5 bound across layouts, conj(A) / conj(B), thin M, batches with a
+    broadcast operand, real alpha/beta with a bias (on the tensor cores) and a
+    complex alpha (the FFMA kernel), and non-finite inputs."""
+    import metalblas_b200 as mb
+    gen = torch.Generator().manual_seed(16)
+    for (M, N, K) in [(512, 640, 768), (1000, 1000, 1000), (3, 2048, 512), (256, 96, 4096)]:
+        a = rand((M, K), torch.complex64, gen)
+        b = rand((K, N), torch.complex64, gen)
+        for av, bv in ((a, b), (a.t().contiguous().t(), b), (a, b.t().contiguous().t()), (a.conj(), b),
+                       (a, b.conj()), (a.conj(), b.conj()), (_offset(a), _offset(b))):
+            ref = orc.product(to_np(av.resolve_conj()), to_np(bv.resolve_conj()), "complex64")
+            plan = mb.kernels.plan(av, bv, backend="mpp_tensor")
+            assert plan.startswith("tc_c64x3"), plan
+            ok, err = orc.check(to_np(mb.matmul(av, bv, backend="mpp_tensor")), ref, "complex64")
+            assert ok, f"{(M, N, K)} conj=({av.is_conj()}, {bv.is_conj()}) err={err}"
+            ok, err = orc.check(to_np(mb.matmul(av, bv)), ref, "complex64")
+            assert ok, f"{(M, N, K)} auto err={err}"
+    a = rand((2048, 1024), torch.complex64, gen)
+    b = rand((1024, 1024), torch.complex64, gen)
+    assert mb.kernels.plan(a, b).startswith("tc_c64x3")  # compute-heavy: the planner's own choice
+    bias = rand((1024,), torch.complex64, gen)
+    for beta, alpha in ((0.5, -2.0), (0.0, 1.0), (1.5, 0.0), (0.5, complex(2.0, 1.0)), (complex(0, 1), 1.0)):
+        got = mb.addmm(bias, a, b, beta=beta, alpha=alpha)
+        ref = orc.fused(to_np(bias), to_np(a), to_np(b), beta, alpha, "complex64")
+        ok, err = orc.check(to_np(got), ref, "complex64")
+        assert ok, f"addmm beta={beta} alpha={alpha} err={err}"
+    A = rand((6, 256, 384), torch.complex64, gen)
+    B = rand((1, 384, 320), torch.complex64, gen)
+    bias3 = rand((6, 256, 320), torch.complex64, gen)
+    got = mb.baddbmm(bias3, A, B.expand(6, 384, 320), beta=0.5, alpha=2.0)
+    ref = orc.fused(to_np(bias3), to_np(A), np.broadcast_to(to_np(B), (6, 384, 320)), 0.5, 2.0, "complex64")
+    ok, err = orc.check(to_np(got), ref, "complex64")
+    assert ok, f"baddbmm err={err}"
+    # non-finite inputs propagate like the CUDA-core kernel's
+    a = rand((256, 512), torch.complex64, gen)
+    b = rand((512, 384), torch.complex64, gen)
+    a[3, 7] = complex(float("inf"), 0.0)
+    a[5, 1] = complex(0.0, float("nan"))
+    got = mb.matmul(a, b, backend="mpp_tensor")
+    simd = mb.matmul(a, b, backend="simd")
+    assert torch.equal(torch.isnan(got), torch.isnan(simd)) and torch.equal(torch.isinf(got), torch.isinf(simd))
+
+
 def test_nd_broadcast_batches_read_operands_in_place(monkeypatch):
     """matmul over multi-dim broadcast batches: when the
     expanded batch dims cannot be flattened into one stride, the leading dim is
