@@ -741,7 +741,9 @@ class _Suite:
                 self.emit(line)
 
     def c4(self):
-        """Integers, bit-exact: 8-bit on the int8 tensor cores, 16/32/64-bit on IMAD."""
+        """Integers, bit-exact: 8-bit on the int8 tensor cores; 16/32/64-bit as
+        byte planes on them too (L(L+1)/2 u8 GEMM-equivalents for L-byte
+        integers, so the ceiling is the measured int8 rate / 3, / 10, / 36)."""
         mb = self.mb
         layouts = {
             "rm_rm": (None, None),
@@ -761,9 +763,9 @@ class _Suite:
                     self.gemm_case("C4", f"{name} {n}^3 {lay} full range", a, b, name, self.int8_peak,
                                    "tensor int8 dense (cuBLASLt measured)", a_view=av, b_view=bv,
                                    cpu=(lay == "rm_rm" and n == 4096), check_name=name)
-        for dt, name, peak, pname in ((torch.int16, "int16", self.imad, "IMAD probe"),
-                                      (torch.int32, "int32", self.imad, "IMAD probe"),
-                                      (torch.int64, "int64", self.imad64, "int64 mul-add probe")):
+        for dt, name, peak, pname in ((torch.int16, "int16", self.int8_peak / 3.0, "int8 tensor / 3 (byte planes)"),
+                                      (torch.int32, "int32", self.int8_peak / 10.0, "int8 tensor / 10 (byte planes)"),
+                                      (torch.int64, "int64", self.int8_peak / 36.0, "int8 tensor / 36 (byte planes)")):
             g = torch.Generator().manual_seed(4)
             a = torch.randint(-1000, 1000, (2048, 2048), dtype=dt, generator=g)
             b = torch.randint(-1000, 1000, (2048, 2048), dtype=dt, generator=g)

@@ -173,7 +173,8 @@ constexpr int kGemvRowsPerWarp = 2;   // staged-x rows kernel
 constexpr int64_t kGemvRowsPerCta = kGemvWarps * kGemvRowsPerWarp;
 
 enum PlanKind {
-  PK_EMPTY = 0, PK_GEMV_COLS, PK_GEMV_ROWS, PK_TC, PK_SIMT, PK_TC_C32, PK_TC_PACKED, PK_TC_3XTF32, PK_TC_C64X3
+  PK_EMPTY = 0, PK_GEMV_COLS, PK_GEMV_ROWS, PK_TC, PK_SIMT, PK_TC_C32, PK_TC_PACKED, PK_TC_3XTF32, PK_TC_C64X3,
+  PK_TC_LIMB
 };
 
 struct Plan {
@@ -206,6 +207,10 @@ struct Plan {
   // in the workspace (A' M x ldk, B'ᵀ N x ldk)
   int64_t x3_ldk = 0, x3_a_batches = 1, x3_b_batches = 1;
   int64_t x3_ahi = 0, x3_alo = 0, x3_bhi = 0, x3_blo = 0, x3_flag = 0;
+  // PK_TC_LIMB: 16/32/64-bit integers as byte planes on the 8-bit tensor cores
+  int limb_L = 0;
+  int64_t limb_kc = 0, limb_kp = 0, limb_ld = 0, limb_a_off = 0, limb_b_off = 0;
+  int64_t limb_a_batches = 1, limb_b_batches = 1;
   // shared
   int64_t ws_bytes = 0;
   std::string why;
@@ -641,6 +646,82 @@ bool plan_c64x3(const Op &o, int sms, const mb_gemm_desc *d, bool have_ws, Plan 
   return true;
 }
 
+// ---------------------------------------------------------------------------
+// 16/32/64-bit integer products on the 8-bit tensor cores.  An L-byte integer
+// is the sum of its unsigned bytes a_l * 2^(8l) modulo 2^(8L) (two's
+// complement), so modulo 2^(8L)
+//   C = A B = sum over s < L of 2^(8s) * P_s,   P_s = sum over i + j = s of A_i B_j,
+// and each P_s is ONE u8 x u8 GEMM over K' = (s+1) kp: A_cat = [A_0 | ... | A_{L-1}]
+// (M x L*kp, byte planes side by side along K) and B_rev = [B_{L-1}; ...; B_0]
+// (stored transposed, N x L*kp), so P_s = A_cat[:, :(s+1)kp] @ B_rev[(L-1-s)kp:, :].
+// P_s lands in C through the epilogue, C = alpha * 2^(8s) * P_s + C with
+// wrapping integer arithmetic, the first GEMM with the caller's beta * bias.
+// The s32 accumulators stay exact while L * kp * 255^2 < 2^31; a longer K runs
+// in chunks.  Bit-exact like the CUDA-core IMAD kernel (metalblas/shaders/
+// int_gemm.h:41-154 is the reference's register-tiled integer GEMM).
+const bool g_int_limbs = [] {
+  const char *s = getenv("METALBLAS_INT_LIMBS");
+  return !(s && s[0] == '0');
+}();
+int limb_planes(int dt) { return dt == MB_I16 ? 2 : dt == MB_I32 ? 4 : dt == MB_I64 ? 8 : 0; }
+
+Op limb_gemm_op(const Op &o, const Plan &t, int s, const void *acat, const void *brev) {
+  Op r = o;
+  r.dt = MB_U8;
+  r.K = (int64_t)(s + 1) * t.limb_kp;
+  r.A = acat; r.a_rs = t.limb_ld; r.a_cs = 1; r.sA = o.sA ? o.M * t.limb_ld : 0;
+  r.B = static_cast<const uint8_t *>(brev) + (int64_t)(t.limb_L - 1 - s) * t.limb_kp;
+  r.b_rs = 1; r.b_cs = t.limb_ld; r.sB = o.sB ? o.N * t.limb_ld : 0;
+  r.conj_a = r.conj_b = 0;
+  return r;  // C and bias stay the caller's; the epilogue chain sets them per GEMM
+}
+
+// Whole-tile plan (no split-K workspace) of GEMM s of the chain, over the tile
+// widths that have integer-output kernels.
+bool limb_gemm_plan(const Op &o, const Plan &t, int s, int sms, Plan &g) {
+  const void *ph = reinterpret_cast<const void *>(uintptr_t(1) << 20);  // aligned placeholder
+  const Op r = limb_gemm_op(o, t, s, ph, ph);
+  mb_gemm_desc q;
+  mb_gemm_desc_init(&q);
+  q.split_k = 1;
+  q.stream_k = 1;
+  bool ok = false;
+  double best = 1e300;
+  for (int bn : {64, 128, 256}) {
+    q.tile_n = bn;
+    Plan c;
+    if (!plan_tc_any(r, sms, &q, false, c)) continue;
+    if (c.pair == 2 && c.bn != 128 && c.bn != 256) continue;
+    if (c.est < best) { best = c.est; g = c; ok = true; }
+  }
+  return ok;
+}
+
+bool plan_limb(const Op &o, int sms, const mb_gemm_desc *d, bool have_ws, Plan &pl) {
+  (void)d;
+  const int L = limb_planes(o.dt);
+  if (!L || !have_ws || o.M < 1 || o.N < 1 || o.K < 1) return false;
+  if (o.M >= (1ll << 31) || o.N >= (1ll << 31)) return false;
+  const int64_t kp_max = (33024 / L) / 16 * 16;  // L * kp * 255^2 < 2^31
+  Plan t;
+  t.limb_L = L;
+  t.limb_kc = std::min<int64_t>(o.K, kp_max);
+  t.limb_kp = round_up(t.limb_kc, 16);
+  t.limb_ld = L * t.limb_kp;
+  t.limb_a_batches = o.sA ? o.batch : 1;
+  t.limb_b_batches = o.sB ? o.batch : 1;
+  const int64_t a_bytes = t.limb_a_batches * o.M * t.limb_ld, b_bytes = t.limb_b_batches * o.N * t.limb_ld;
+  t.limb_a_off = round_up(kTicketBytes, 256);
+  t.limb_b_off = round_up(t.limb_a_off + a_bytes, 256);
+  t.ws_bytes = t.limb_b_off + b_bytes;
+  Plan g;  // the widest GEMM of the chain, for the plan's description
+  if (!limb_gemm_plan(o, t, L - 1, sms, g)) return false;
+  t.bn = g.bn; t.pair = g.pair; t.swap = g.swap; t.tiles_m = g.tiles_m; t.tiles_n = g.tiles_n; t.est = g.est;
+  t.kind = PK_TC_LIMB;
+  pl = t;
+  return true;
+}
+
 int gemv_cols_per_sm(int dt, int mr);
 
 // Thin products the column GEMV runs with several x rows sharing each load of
@@ -800,8 +881,13 @@ int make_plan(const mb_gemm_desc *d, const Op &o, int sms, bool have_ws, Plan &p
       return fail(MB_ERR_UNSUPPORTED, "tensor-core complex64 (3xTF32) needs a row-major output, real alpha/beta, "
                                       "a bias contiguous along N and a workspace");
     }
+    if (limb_planes(o.dt)) {  // 16/32/64-bit integers as byte planes on the 8-bit tensor cores
+      if (plan_limb(o, sms, d, have_ws, pl)) return MB_OK;
+      return fail(MB_ERR_UNSUPPORTED, "tensor-core integer product (byte planes) needs a workspace");
+    }
     if (!is_tc_dtype(o.dt))
-      return fail(MB_ERR_UNSUPPORTED, "tensor-core backend supports bf16/fp16/fp32/complex32/complex64/int8/uint8 only");
+      return fail(MB_ERR_UNSUPPORTED, "tensor-core backend supports bf16/fp16/fp32/complex32/complex64/8-64-bit "
+                                      "integers only");
     if (plan_tc_any(o, sms, d, have_ws, pl)) return MB_OK;
     if (plan_packed(o, sms, d, have_ws, pl)) return MB_OK;
     return fail(MB_ERR_UNSUPPORTED, "tensor-core backend: operands not TMA-addressable (need a unit stride, "
@@ -843,6 +929,29 @@ int make_plan(const mb_gemm_desc *d, const Op &o, int sms, bool have_ws, Plan &p
     const double t_simt = tile_flops / (40.0e12 * std::min(1.0, ctas / (double)sms));
     const double t_x3 = 36.0 * opnd / 6.0e12 + flops / 190.0e12 + 6.0e-6;
     if (t_x3 < t_simt && plan_c64x3(o, sms, d, have_ws, pl)) return MB_OK;
+  }
+  // 16/32/64-bit integers: byte planes on the 8-bit tensor cores when the
+  // estimate beats the IMAD kernel's.  Planes: L(L+1)/2 u8 GEMM-equivalents at
+  // ~2.2 POPS on 128-padded tiles, the plane split and L read-modify-writes of C
+  // at ~6 TB/s, ~4 us per launch; IMAD: the measured rates (int16 22.7, int32
+  // 26, int64 7.2 Tops on 2048^3) on its 128 x 128 (int64: 64 x 64) tiles.
+  if (limb_planes(o.dt) && g_int_limbs && have_ws) {
+    const int L = limb_planes(o.dt);
+    const int esz = elem_size(o.dt);
+    const double bt = (double)std::max<int64_t>(o.batch, 1);
+    const int64_t kp_max = (33024 / L) / 16 * 16;
+    const double chunks = (double)ceil_div(o.K, kp_max);
+    const double kp = (double)round_up(std::min<int64_t>(o.K, kp_max), 16) * chunks;
+    const double mp = (double)round_up(o.M, 128), np = (double)round_up(o.N, 128);
+    const double t_tc = 2.0 * mp * np * kp * bt * (L * (L + 1) / 2) / 2.2e15;
+    const double bytes = ((double)o.M * o.K * (o.sA ? bt : 1.0) + (double)o.N * o.K * (o.sB ? bt : 1.0)) * (esz + L) +
+                         2.0 * L * chunks * (double)o.M * o.N * esz * bt;
+    const double t_limb = t_tc + bytes / 6.0e12 + (2 + L) * chunks * 4.0e-6;
+    const int bm = o.dt == MB_I64 ? 64 : 128;
+    const double ctas = (double)ceil_div(o.M, bm) * ceil_div(o.N, bm) * bt;
+    const double rate = o.dt == MB_I16 ? 22.7e12 : o.dt == MB_I32 ? 26.0e12 : 7.2e12;
+    const double t_simt = 2.0 * bm * bm * (double)o.K * ctas / (rate * std::min(1.0, ctas / (double)sms));
+    if (t_limb < t_simt && plan_limb(o, sms, d, have_ws, pl)) return MB_OK;
   }
   if (is_tc_dtype(o.dt)) {
     if (plan_tc_any(o, sms, d, have_ws, pl)) return MB_OK;
@@ -1037,10 +1146,11 @@ int encode_map(CUtensorMap *m, int dt, const void *base, int64_t inner, int64_t 
   return MB_OK;
 }
 
-template <class T, int BN, int PAIR>
+template <class T, int BN, int PAIR, class TO = T>
 int launch_tc_bn(const Op &o, const Plan &pl, const EpiScalars &e, void *ws, int sms, cudaStream_t st) {
   using C_ = tc::Cfg<BN, sizeof(T), PAIR>;
   constexpr int ESZ = sizeof(T);
+  constexpr int OSZ = sizeof(TO);
   constexpr int BK = C_::BK;
   tc::TcParams p;
   memset(&p, 0, sizeof(p));
@@ -1079,9 +1189,9 @@ int launch_tc_bn(const Op &o, const Plan &pl, const EpiScalars &e, void *ws, int
   p.C = o.C; p.c_rs = o.c_rs; p.c_cs = o.c_cs; p.sC = o.sC;
   p.bias = o.bias; p.bias_rs = o.bias_rs; p.bias_cs = o.bias_cs; p.bias_bs = o.bias_bs;
   p.epi = e;
-  p.c_vec = (o.c_cs == 1 && aligned16(o.C) && (o.c_rs * ESZ) % 16 == 0 && (o.batch <= 1 || (o.sC * ESZ) % 16 == 0)) ? 1 : 0;
+  p.c_vec = (o.c_cs == 1 && aligned16(o.C) && (o.c_rs * OSZ) % 16 == 0 && (o.batch <= 1 || (o.sC * OSZ) % 16 == 0)) ? 1 : 0;
   // Row-major output that TMA can address: staged epilogue with TMA stores.
-  if (C_::TMA_STORE && p.c_vec && o.c_rs >= o.N && o.sC >= 0 && (o.batch <= 1 || o.sC >= o.c_rs * o.M || o.sC == 0) &&
+  if (C_::TMA_STORE && std::is_same_v<T, TO> && p.c_vec && o.c_rs >= o.N && o.sC >= 0 && (o.batch <= 1 || o.sC >= o.c_rs * o.M || o.sC == 0) &&
       o.N < (1ll << 31) && o.M < (1ll << 31)) {
     const int64_t bC = o.batch > 1 ? o.batch : 1;
     if (encode_map(&p.tmC, o.dt, o.C, o.N, o.M, bC, o.c_rs, o.sC, C_::CC, 32, CU_TENSOR_MAP_SWIZZLE_64B) == MB_OK)
@@ -1092,7 +1202,7 @@ int launch_tc_bn(const Op &o, const Plan &pl, const EpiScalars &e, void *ws, int
     p.ws = reinterpret_cast<char *>(ws) + kTicketBytes;
   }
   p.timeout_ns = wait_timeout_ns();
-  auto kern = tc::tc_gemm_kernel<T, BN, PAIR>;
+  auto kern = tc::tc_gemm_kernel<T, BN, PAIR, TO>;
   static int attr_done[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1280,6 +1390,66 @@ int launch_c64x3(const Op &o, const Plan &pl, const EpiScalars &e, void *ws, int
   return launch_simt<float2>(o, e, st, flag);
 }
 
+template <class TO>
+int launch_tc_limb(const Op &o, const Plan &pl, const EpiScalars &e, int sms, cudaStream_t st) {
+  if (pl.pair == 2) {
+    if (pl.bn == 128) return launch_tc_bn<uint8_t, 128, 2, TO>(o, pl, e, nullptr, sms, st);
+    if (pl.bn == 256) return launch_tc_bn<uint8_t, 256, 2, TO>(o, pl, e, nullptr, sms, st);
+  } else {
+    if (pl.bn == 64) return launch_tc_bn<uint8_t, 64, 1, TO>(o, pl, e, nullptr, sms, st);
+    if (pl.bn == 128) return launch_tc_bn<uint8_t, 128, 1, TO>(o, pl, e, nullptr, sms, st);
+    if (pl.bn == 256) return launch_tc_bn<uint8_t, 256, 1, TO>(o, pl, e, nullptr, sms, st);
+  }
+  return fail(MB_ERR_INVALID, "integer plane GEMM with tile_n %d pair %d", pl.bn, pl.pair);
+}
+
+// The byte-plane chain (see plan_limb): per K chunk, split A and B into planes,
+// then one u8 GEMM per shift s accumulating into C.
+template <class T>
+int launch_limb(const Op &o, const Plan &pl, const EpiScalars &e, void *ws, int sms, cudaStream_t st) {
+  char *w = reinterpret_cast<char *>(ws);
+  uint8_t *acat = reinterpret_cast<uint8_t *>(w + pl.limb_a_off), *brev = reinterpret_cast<uint8_t *>(w + pl.limb_b_off);
+  const int L = pl.limb_L;
+  const int64_t nchunks = ceil_div(o.K, pl.limb_kc);
+  // the caller's alpha (1 without an epilogue); alpha == 0 leaves beta * bias
+  const uint64_t alpha = e.enabled ? (e.alpha_nz ? (uint64_t)e.ialpha : 0ull) : 1ull;
+  auto split = [&](const void *src, uint8_t *dst, int64_t rows, int64_t kc, int64_t k0, int64_t rs, int64_t cs,
+                   int64_t bs, int64_t batches, int rev, const char *what) {
+    LimbArgs a{src, dst, rows, kc, k0, rs, cs, bs, batches, pl.limb_kp, pl.limb_ld, L, rev};
+    const int64_t tiles = batches * ceil_div(rows, 32) * ceil_div(pl.limb_kp, 32);
+    limb_split_kernel<T><<<(unsigned)std::max<int64_t>(1, std::min<int64_t>(tiles, (int64_t)sms * 16)), dim3(32, 8), 0,
+                           st>>>(a);
+    return cuda_check(cudaGetLastError(), what);
+  };
+  bool first = true;
+  for (int64_t ch = 0; ch < nchunks; ++ch) {
+    const int64_t k0 = ch * pl.limb_kc, kc = std::min<int64_t>(pl.limb_kc, o.K - k0);
+    int rc = split(o.A, acat, o.M, kc, k0, o.a_rs, o.a_cs, o.sA, pl.limb_a_batches, 0, "integer planes of A");
+    if (!rc) rc = split(o.B, brev, o.N, kc, k0, o.b_cs, o.b_rs, o.sB, pl.limb_b_batches, 1, "integer planes of B");
+    if (rc) return rc;
+    for (int s = 0; s < L; ++s) {
+      Op r = limb_gemm_op(o, pl, s, acat, brev);
+      EpiScalars es = e;
+      es.cplx = 0;
+      if (!first) {
+        // C += alpha * 2^(8s) * P_s (wrapping): the running sum is the bias
+        r.bias = o.C; r.bias_rs = o.c_rs; r.bias_cs = o.c_cs; r.bias_bs = o.sC;
+        es.enabled = 1; es.alpha_nz = 1; es.beta_nz = 1; es.ibeta = 1;
+        es.ialpha = (int64_t)(alpha << (8 * s));
+      } else if (e.enabled) {
+        es.ialpha = (int64_t)(alpha << (8 * s));  // s == 0: the caller's epilogue as given
+      }
+      Plan g;
+      if (!limb_gemm_plan(o, pl, s, sms, g)) return fail(MB_ERR_INVALID, "integer plane GEMM: no tile plan");
+      rc = launch_tc_limb<T>(g.swap ? swapped(r) : r, g, es, sms, st);
+      if (rc) return rc;
+      first = false;
+      if (alpha == 0) return MB_OK;  // beta * bias only
+    }
+  }
+  return MB_OK;
+}
+
 template <class F>
 int by_dtype(int dt, F &&f) {
   switch (dt) {
@@ -1425,6 +1595,11 @@ int mb_plan_query(const mb_gemm_desc *d, char *buf, int buflen) {
                pl.kind == PK_TC_C64X3 ? "tc_c64x3" : "tc_3xtf32", pl.bn, pl.splits, (long long)pl.dp_tiles, pl.tail_half, pl.pair, pl.sk, pl.swap, (long long)pl.tiles_m,
                (long long)pl.tiles_n, (long long)pl.ws_bytes);
       break;
+    case PK_TC_LIMB:
+      snprintf(tmp, sizeof(tmp), "tc_int_planes planes=%d kp=%lld chunks=%lld bn=%d pair=%d swap=%d ws=%lld", pl.limb_L,
+               (long long)pl.limb_kp, (long long)ceil_div(o.K, std::max<int64_t>(pl.limb_kc, 1)),
+               pl.bn, pl.pair, pl.swap, (long long)pl.ws_bytes);
+      break;
     case PK_TC_PACKED:
       snprintf(tmp, sizeof(tmp), "tc_packed pack_a=%d pack_b=%d bn=%d split=%d pair=%d sk=%d swap=%d tiles=%lldx%lld ws=%lld",
                pl.pk_a, pl.pk_b, pl.bn, pl.splits, pl.pair, pl.sk, pl.swap, (long long)pl.tiles_m,
@@ -1467,6 +1642,10 @@ int mb_gemm(const mb_gemm_desc *d, void *stream) {
       case PK_TC_C64X3:
         if constexpr (std::is_same_v<T, float2>) return launch_c64x3(o, pl, e, d->workspace, sms, st);
         else return fail(MB_ERR_UNSUPPORTED, "complex64 3xTF32 path for a non-complex64 dtype");
+      case PK_TC_LIMB:
+        if constexpr (std::is_same_v<T, int16_t> || std::is_same_v<T, int32_t> || std::is_same_v<T, int64_t>)
+          return launch_limb<T>(o, pl, e, d->workspace, sms, st);
+        else return fail(MB_ERR_UNSUPPORTED, "integer plane path for a non 16/32/64-bit integer dtype");
       default: return launch_simt<T>(o, e, st);
     }
   });
@@ -1634,7 +1813,8 @@ int mb_gemm_noalloc(const mb_gemm_desc *d, void *stream) {
   int rc = plan_for(&q, pl, o, sms);
   if (rc) return rc;
   if (pl.kind == PK_EMPTY) return MB_OK;
-  if ((pl.kind == PK_TC_C32 || pl.kind == PK_TC_PACKED || pl.kind == PK_TC_3XTF32 || pl.kind == PK_TC_C64X3) &&
+  if ((pl.kind == PK_TC_C32 || pl.kind == PK_TC_PACKED || pl.kind == PK_TC_3XTF32 || pl.kind == PK_TC_C64X3 ||
+       pl.kind == PK_TC_LIMB) &&
       pl.ws_bytes > (int64_t)MB_NOALLOC_SCRATCH_BYTES &&
       q.backend == MB_BACKEND_AUTO) {
     // complex32 on the tensor cores needs its expanded B' in scratch, packed
@@ -1676,6 +1856,10 @@ int mb_gemm_noalloc(const mb_gemm_desc *d, void *stream) {
       case PK_TC_C64X3:
         if constexpr (std::is_same_v<T, float2>) return launch_c64x3(o, pl, e, scratch, sms, st);
         else return fail(MB_ERR_UNSUPPORTED, "complex64 3xTF32 path for a non-complex64 dtype");
+      case PK_TC_LIMB:
+        if constexpr (std::is_same_v<T, int16_t> || std::is_same_v<T, int32_t> || std::is_same_v<T, int64_t>)
+          return launch_limb<T>(o, pl, e, scratch, sms, st);
+        else return fail(MB_ERR_UNSUPPORTED, "integer plane path for a non 16/32/64-bit integer dtype");
       default: return launch_simt<T>(o, e, st);
     }
   });

@@ -6,6 +6,8 @@
 #pragma once
 #include "mb_common.cuh"
 
+#include <type_traits>
+
 namespace mb {
 
 struct PackArgs {
@@ -143,6 +145,55 @@ __global__ void __launch_bounds__(256) split_tf32_kernel(const SplitArgs a) {
         const int64_t o = (b * a.rows + r) * a.ld + c;
         a.hi[o] = hi;
         a.lo[o] = lo;
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Integer products on the 8-bit tensor cores: byte planes of 16/32/64-bit
+// operands.  For one K chunk [k0, k0 + kc) of src (rows x K, element (r, k) at
+// src[b*bs + r*rs + k*cs]), dst[b][r][seg(l)*kp + c] = byte l of src(r, k0 + c)
+// (two's-complement bits, unsigned), zero for c >= kc, with seg(l) = l for A
+// and L-1-l for B (its planes stacked in reverse).  32 x 32 shared-memory tile
+// so the source read is coalesced along whichever of r / k is contiguous and
+// each plane row is written along k.  Block 32 x 8, grid-stride over tiles.
+struct LimbArgs {
+  const void *src;
+  uint8_t *dst;
+  int64_t rows, kc, k0;    // rows, K chunk length and start
+  int64_t rs, cs, bs;      // source strides (elements)
+  int64_t batch, kp, ld;   // batches; plane width (kc rounded up to 16); dst row pitch (L * kp)
+  int planes, rev;
+};
+
+template <class S>
+__global__ void __launch_bounds__(256) limb_split_kernel(const LimbArgs a) {
+  __shared__ S tile[32][33];
+  const int tx = threadIdx.x, ty = threadIdx.y;
+  const int64_t rt = (a.rows + 31) / 32, ct = (a.kp + 31) / 32;
+  const int64_t tiles = a.batch * rt * ct;
+  const bool c_fast = a.cs == 1 || (a.rs != 1 && (a.cs < 0 ? -a.cs : a.cs) <= (a.rs < 0 ? -a.rs : a.rs));
+  for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
+    const int64_t b = t / (rt * ct);
+    const int64_t rem = t - b * rt * ct;
+    const int64_t r0 = (rem / ct) * 32, c0 = (rem % ct) * 32;
+    const S *src = (const S *)a.src + b * a.bs;
+#pragma unroll
+    for (int i = ty; i < 32; i += 8) {
+      const int64_t r = r0 + (c_fast ? i : tx), c = c0 + (c_fast ? tx : i);
+      const S v = (r < a.rows && c < a.kc) ? src[r * a.rs + (a.k0 + c) * a.cs] : S(0);
+      if (c_fast) tile[i][tx] = v; else tile[tx][i] = v;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = ty; i < 32; i += 8) {
+      const int64_t r = r0 + i, c = c0 + tx;
+      if (r < a.rows && c < a.kp) {
+        const uint64_t v = (uint64_t)(typename std::make_unsigned<S>::type)tile[i][tx];
+        uint8_t *row = a.dst + (b * a.rows + r) * a.ld + c;
+        for (int l = 0; l < a.planes; ++l) row[(int64_t)(a.rev ? a.planes - 1 - l : l) * a.kp] = (uint8_t)(v >> (8 * l));
       }
     }
     __syncthreads();

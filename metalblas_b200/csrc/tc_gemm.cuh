@@ -631,7 +631,19 @@ __device__ __forceinline__ void store_row_chunk(const TcParams &p, int b, int m,
   T out[NC];
   bool cplx = false;
   if constexpr (std::is_same_v<T, __half>) cplx = p.epi.cplx != 0;
-  if (p.epi.enabled && !cplx) {
+  if constexpr (Elem<T>::is_int && sizeof(T) == 8) {
+    // 64-bit integer output of an 8-bit product (integer limbs): the s32
+    // accumulator sign-extends, then alpha*acc + beta*bias wraps modulo 2^64
+    const bool use_bias = p.epi.enabled && p.epi.beta_nz && m < p.M;
+    const T *brow = (const T *)p.bias + (int64_t)b * p.bias_bs + (int64_t)m * p.bias_rs;
+#pragma unroll
+    for (int j = 0; j < NC; ++j) {
+      const uint64_t acc = (uint64_t)(int64_t)(int32_t)r[j];
+      uint64_t x = !p.epi.enabled ? acc : (p.epi.alpha_nz ? (uint64_t)p.epi.ialpha * acc : 0ull);
+      if (use_bias && n0 + j < p.N) x += (uint64_t)p.epi.ibeta * (uint64_t)brow[(int64_t)(n0 + j) * p.bias_cs];
+      out[j] = (T)x;
+    }
+  } else if (p.epi.enabled && !cplx) {
     epi_real<T, NC>(p, b, m, n0, r);
 #pragma unroll
     for (int j = 0; j < NC; ++j) out[j] = Elem<T>::store(acc_from_bits<T>(r[j]));
@@ -762,10 +774,15 @@ __device__ __forceinline__ void split_finish(const TcParams &p, const Unit &w, i
 }
 
 // ---------------------------------------------------------------------------
-template <class T, int BN, int PAIR = 1>
+// TO: the output element type.  It is T except for the integer limb products,
+// whose u8 x u8 GEMMs write 16/32/64-bit integers (direct stores only).
+template <class T, int BN, int PAIR = 1, class TO = T>
 __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_constant__ TcParams p) {
   constexpr int ESZ = sizeof(T);
   using C_ = Cfg<BN, ESZ, PAIR>;
+  // columns per TMEM read on the direct-store and split paths: wider outputs
+  // take 16 so the converted row chunk stays within the register budget
+  constexpr int RCHO = (sizeof(TO) > (size_t)ESZ && C_::RCH > 16) ? 16 : C_::RCH;
   constexpr int TM_ROWS = BM * PAIR;  // output rows per tile (256 for a CTA pair)
   constexpr int BK = C_::BK, STAGES = C_::STAGES;
   constexpr uint32_t A_BYTES = C_::A_BYTES, STAGE_BYTES = C_::STAGE_BYTES;
@@ -1036,7 +1053,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(abuf * C_::ACC_COLS + col0);
       const int nbase = w.tn * BN + ucol0 + col0;            // global column of tbase
       if (!w.split) {
-        if constexpr (C_::TMA_STORE) {
+        if constexpr (C_::TMA_STORE && std::is_same_v<T, TO>) {
           if (p.c_tma) {
             // 64-byte rows staged with the SWIZZLE_64B pattern (16-byte chunk j
             // of row r at chunk j ^ ((r >> 1) & 3)), one TMA store per 32-row
@@ -1092,12 +1109,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
           }
         }
 #pragma unroll 1
-        for (int c = 0; c < wcols; c += RCH) {
+        for (int c = 0; c < wcols; c += RCHO) {
           uint32_t r[32];
-          tmem_ld<RCH>(tbase + c, r);
+          tmem_ld<RCHO>(tbase + c, r);
           tmem_wait_ld();
           const int n0 = nbase + c;
-          if (m < p.M && n0 < p.N) store_row_chunk<T, RCH>(p, w.b, m, n0, r);
+          if (m < p.M && n0 < p.N) store_row_chunk<TO, RCHO>(p, w.b, m, n0, r);
         }
         tc_fence_before();
         __syncwarp();
@@ -1111,18 +1128,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
         uint4 *part = reinterpret_cast<uint4 *>(reinterpret_cast<uint32_t *>(p.ws) +
                                                 ((int64_t)w.tail * p.splits + w.s) * slot_words + warp_off) + lane;
 #pragma unroll 1
-        for (int c = 0; c < wcols; c += RCH) {
+        for (int c = 0; c < wcols; c += RCHO) {
           uint32_t r[32];
-          tmem_ld<RCH>(tbase + c, r);
+          tmem_ld<RCHO>(tbase + c, r);
           tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < RCH; j += 4)
+          for (int j = 0; j < RCHO; j += 4)
             __stcg(part + ((c + j) >> 2) * 32, make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]));
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) release_tmem(abuf);
-        split_finish<T, BN, RCH>(p, w, ew, lane, m, nbase, wcols);
+        split_finish<TO, BN, RCHO>(p, w, ew, lane, m, nbase, wcols);
       }
       if (++abuf == 2) { abuf = 0; aphase ^= 1u; }
     }

@@ -24,7 +24,8 @@ def rand(shape, dtype, gen, device="cuda", full_range=False, lo=None, hi=None):
     if dtype in INTS:
         if full_range:
             info = torch.iinfo(dtype)
-            lo, hi = info.min, info.max + 1
+            # randint's exclusive bound must itself fit the type's C range
+            lo, hi = info.min, (info.max if dtype is torch.int64 else info.max + 1)
         elif lo is None:
             lo, hi = (0 if dtype is torch.uint8 else -4), 4
         t = torch.randint(lo, hi, tuple(shape), dtype=dtype, generator=gen)

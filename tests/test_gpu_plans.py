@@ -347,6 +347,45 @@ def test_complex64_3xtf32_matches_oracle():
     assert torch.equal(torch.isnan(got), torch.isnan(simd)) and torch.equal(torch.isinf(got), torch.isinf(simd))
 
 
+@pytest.mark.parametrize("dtype", [torch.int16, torch.int32, torch.int64], ids=NAME.get)
+def test_integer_byte_planes_bit_exact(dtype):
+    """16/32/64-bit integer products on the 8-bit tensor cores (byte planes,
+    one u8 GEMM per shift accumulated into C with wrapping arithmetic) are
+    bit-exact against the oracle over the full type range: layouts, thin M,
+    K not a multiple of 16, K long enough for several exact chunks (int64),
+    the alpha/beta/bias epilogue including alpha == 0, and batches with a
+    broadcast operand."""
+    import metalblas_b200 as mb
+    name = NAME[dtype]
+    gen = torch.Generator().manual_seed(17)
+    for (M, N, K) in [(256, 320, 768), (1000, 1000, 1000), (130, 70, 5000), (4, 600, 300), (300, 200, 17)]:
+        a = rand((M, K), dtype, gen, full_range=True)
+        b = rand((K, N), dtype, gen, full_range=True)
+        ref = orc.product(to_np(a), to_np(b), name)
+        for av, bv in ((a, b), (a.t().contiguous().t(), b), (a, b.t().contiguous().t()), (_offset(a), _offset(b))):
+            plan = mb.kernels.plan(av, bv, backend="mpp_tensor")
+            assert plan.startswith("tc_int_planes"), plan
+            ok, err = orc.check(to_np(mb.matmul(av, bv, backend="mpp_tensor")), ref, name)
+            assert ok, f"{(M, N, K)} err={err}"
+        ok, err = orc.check(to_np(mb.matmul(a, b)), ref, name)
+        assert ok, f"{(M, N, K)} auto err={err}"
+    a = rand((512, 384), dtype, gen, full_range=True)
+    b = rand((384, 640), dtype, gen, full_range=True)
+    bias = rand((640,), dtype, gen, full_range=True)
+    for beta, alpha in ((3, -7), (0, 1), (1, 0), (-2, 5)):
+        got = mb.addmm(bias, a, b, beta=beta, alpha=alpha)
+        ref = orc.fused(to_np(bias), to_np(a), to_np(b), beta, alpha, name)
+        ok, err = orc.check(to_np(got), ref, name)
+        assert ok, f"addmm beta={beta} alpha={alpha} err={err}"
+    A = rand((5, 200, 300), dtype, gen, full_range=True)
+    B = rand((1, 300, 260), dtype, gen, full_range=True)
+    bias3 = rand((5, 200, 260), dtype, gen, full_range=True)
+    got = mb.baddbmm(bias3, A, B.expand(5, 300, 260), beta=2, alpha=-3)
+    ref = orc.fused(to_np(bias3), to_np(A), np.broadcast_to(to_np(B), (5, 300, 260)), 2, -3, name)
+    ok, err = orc.check(to_np(got), ref, name)
+    assert ok, f"baddbmm err={err}"
+
+
 def test_nd_broadcast_batches_read_operands_in_place(monkeypatch):
     """matmul over multi-dim broadcast batches: when the
     expanded batch dims cannot be flattened into one stride, the leading dim is
