@@ -676,21 +676,20 @@ Op limb_gemm_op(const Op &o, const Plan &t, int s, const void *acat, const void 
   return r;  // C and bias stay the caller's; the epilogue chain sets them per GEMM
 }
 
-// Whole-tile plan (no split-K workspace) of GEMM s of the chain, over the tile
-// widths that have integer-output kernels.
+// Plan of GEMM s of the chain over the tile widths that have integer-output
+// kernels; split-K / stream-K tails are allowed (their u32 partial sums are
+// exact: the products are summed modulo 2^32, or stay below 2^31 for int64).
 bool limb_gemm_plan(const Op &o, const Plan &t, int s, int sms, Plan &g) {
   const void *ph = reinterpret_cast<const void *>(uintptr_t(1) << 20);  // aligned placeholder
   const Op r = limb_gemm_op(o, t, s, ph, ph);
   mb_gemm_desc q;
   mb_gemm_desc_init(&q);
-  q.split_k = 1;
-  q.stream_k = 1;
   bool ok = false;
   double best = 1e300;
   for (int bn : {64, 128, 256}) {
     q.tile_n = bn;
     Plan c;
-    if (!plan_tc_any(r, sms, &q, false, c)) continue;
+    if (!plan_tc_any(r, sms, &q, true, c)) continue;
     if (c.pair == 2 && c.bn != 128 && c.bn != 256) continue;
     if (c.est < best) { best = c.est; g = c; ok = true; }
   }
@@ -710,12 +709,18 @@ bool plan_limb(const Op &o, int sms, const mb_gemm_desc *d, bool have_ws, Plan &
   t.limb_ld = L * t.limb_kp;
   t.limb_a_batches = o.sA ? o.batch : 1;
   t.limb_b_batches = o.sB ? o.batch : 1;
+  // the GEMMs' tickets and split-K partials come first (at the workspace
+  // base, as for every plan), then the planes
+  int64_t gemm_ws = kTicketBytes;
+  Plan g;  // the last (widest) GEMM of the chain, for the plan's description
+  for (int s = 0; s < L; ++s) {
+    if (!limb_gemm_plan(o, t, s, sms, g)) return false;
+    gemm_ws = std::max<int64_t>(gemm_ws, g.ws_bytes);
+  }
   const int64_t a_bytes = t.limb_a_batches * o.M * t.limb_ld, b_bytes = t.limb_b_batches * o.N * t.limb_ld;
-  t.limb_a_off = round_up(kTicketBytes, 256);
+  t.limb_a_off = round_up(gemm_ws, 256);
   t.limb_b_off = round_up(t.limb_a_off + a_bytes, 256);
   t.ws_bytes = t.limb_b_off + b_bytes;
-  Plan g;  // the widest GEMM of the chain, for the plan's description
-  if (!limb_gemm_plan(o, t, L - 1, sms, g)) return false;
   t.bn = g.bn; t.pair = g.pair; t.swap = g.swap; t.tiles_m = g.tiles_m; t.tiles_n = g.tiles_n; t.est = g.est;
   t.kind = PK_TC_LIMB;
   pl = t;
@@ -1391,14 +1396,14 @@ int launch_c64x3(const Op &o, const Plan &pl, const EpiScalars &e, void *ws, int
 }
 
 template <class TO>
-int launch_tc_limb(const Op &o, const Plan &pl, const EpiScalars &e, int sms, cudaStream_t st) {
+int launch_tc_limb(const Op &o, const Plan &pl, const EpiScalars &e, void *ws, int sms, cudaStream_t st) {
   if (pl.pair == 2) {
-    if (pl.bn == 128) return launch_tc_bn<uint8_t, 128, 2, TO>(o, pl, e, nullptr, sms, st);
-    if (pl.bn == 256) return launch_tc_bn<uint8_t, 256, 2, TO>(o, pl, e, nullptr, sms, st);
+    if (pl.bn == 128) return launch_tc_bn<uint8_t, 128, 2, TO>(o, pl, e, ws, sms, st);
+    if (pl.bn == 256) return launch_tc_bn<uint8_t, 256, 2, TO>(o, pl, e, ws, sms, st);
   } else {
-    if (pl.bn == 64) return launch_tc_bn<uint8_t, 64, 1, TO>(o, pl, e, nullptr, sms, st);
-    if (pl.bn == 128) return launch_tc_bn<uint8_t, 128, 1, TO>(o, pl, e, nullptr, sms, st);
-    if (pl.bn == 256) return launch_tc_bn<uint8_t, 256, 1, TO>(o, pl, e, nullptr, sms, st);
+    if (pl.bn == 64) return launch_tc_bn<uint8_t, 64, 1, TO>(o, pl, e, ws, sms, st);
+    if (pl.bn == 128) return launch_tc_bn<uint8_t, 128, 1, TO>(o, pl, e, ws, sms, st);
+    if (pl.bn == 256) return launch_tc_bn<uint8_t, 256, 1, TO>(o, pl, e, ws, sms, st);
   }
   return fail(MB_ERR_INVALID, "integer plane GEMM with tile_n %d pair %d", pl.bn, pl.pair);
 }
@@ -1413,19 +1418,16 @@ int launch_limb(const Op &o, const Plan &pl, const EpiScalars &e, void *ws, int 
   const int64_t nchunks = ceil_div(o.K, pl.limb_kc);
   // the caller's alpha (1 without an epilogue); alpha == 0 leaves beta * bias
   const uint64_t alpha = e.enabled ? (e.alpha_nz ? (uint64_t)e.ialpha : 0ull) : 1ull;
-  auto split = [&](const void *src, uint8_t *dst, int64_t rows, int64_t kc, int64_t k0, int64_t rs, int64_t cs,
-                   int64_t bs, int64_t batches, int rev, const char *what) {
-    LimbArgs a{src, dst, rows, kc, k0, rs, cs, bs, batches, pl.limb_kp, pl.limb_ld, L, rev};
-    const int64_t tiles = batches * ceil_div(rows, 32) * ceil_div(pl.limb_kp, 32);
-    limb_split_kernel<T><<<(unsigned)std::max<int64_t>(1, std::min<int64_t>(tiles, (int64_t)sms * 16)), dim3(32, 8), 0,
-                           st>>>(a);
-    return cuda_check(cudaGetLastError(), what);
-  };
   bool first = true;
   for (int64_t ch = 0; ch < nchunks; ++ch) {
     const int64_t k0 = ch * pl.limb_kc, kc = std::min<int64_t>(pl.limb_kc, o.K - k0);
-    int rc = split(o.A, acat, o.M, kc, k0, o.a_rs, o.a_cs, o.sA, pl.limb_a_batches, 0, "integer planes of A");
-    if (!rc) rc = split(o.B, brev, o.N, kc, k0, o.b_cs, o.b_rs, o.sB, pl.limb_b_batches, 1, "integer planes of B");
+    // A (M x K) and Bᵀ (N x K, element (n, k) = B(k, n)) in one launch
+    const LimbArgs la{o.A, acat, o.M, kc, k0, o.a_rs, o.a_cs, o.sA, pl.limb_a_batches, pl.limb_kp, pl.limb_ld, L, 0};
+    const LimbArgs lb{o.B, brev, o.N, kc, k0, o.b_cs, o.b_rs, o.sB, pl.limb_b_batches, pl.limb_kp, pl.limb_ld, L, 1};
+    const int64_t tiles = limb_tiles(la) + limb_tiles(lb);
+    limb_split_kernel<T><<<(unsigned)std::max<int64_t>(1, std::min<int64_t>(tiles, (int64_t)sms * 16)), dim3(32, 8), 0,
+                           st>>>(la, lb);
+    int rc = cuda_check(cudaGetLastError(), "integer byte planes of A and B");
     if (rc) return rc;
     for (int s = 0; s < L; ++s) {
       Op r = limb_gemm_op(o, pl, s, acat, brev);
@@ -1441,7 +1443,7 @@ int launch_limb(const Op &o, const Plan &pl, const EpiScalars &e, void *ws, int 
       }
       Plan g;
       if (!limb_gemm_plan(o, pl, s, sms, g)) return fail(MB_ERR_INVALID, "integer plane GEMM: no tile plan");
-      rc = launch_tc_limb<T>(g.swap ? swapped(r) : r, g, es, sms, st);
+      rc = launch_tc_limb<T>(g.swap ? swapped(r) : r, g, es, ws, sms, st);
       if (rc) return rc;
       first = false;
       if (alpha == 0) return MB_OK;  // beta * bias only

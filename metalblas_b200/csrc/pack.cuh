@@ -156,9 +156,10 @@ __global__ void __launch_bounds__(256) split_tf32_kernel(const SplitArgs a) {
 // operands.  For one K chunk [k0, k0 + kc) of src (rows x K, element (r, k) at
 // src[b*bs + r*rs + k*cs]), dst[b][r][seg(l)*kp + c] = byte l of src(r, k0 + c)
 // (two's-complement bits, unsigned), zero for c >= kc, with seg(l) = l for A
-// and L-1-l for B (its planes stacked in reverse).  32 x 32 shared-memory tile
-// so the source read is coalesced along whichever of r / k is contiguous and
-// each plane row is written along k.  Block 32 x 8, grid-stride over tiles.
+// and L-1-l for B (its planes stacked in reverse).  A shared-memory tile makes
+// the source read coalesced along whichever of r / k is contiguous and each
+// plane row is written along k in 4-byte words (kp and ld are multiples of
+// 16, the destination 256-byte aligned).  Block 32 x 8, grid-stride over tiles.
 struct LimbArgs {
   const void *src;
   uint8_t *dst;
@@ -168,32 +169,65 @@ struct LimbArgs {
   int planes, rev;
 };
 
+// Tiles of one operand's planes (32 rows x 128 columns of K each).
+__host__ __device__ inline int64_t limb_tiles(const LimbArgs &a) {
+  return a.batch * ((a.rows + 31) / 32) * ((a.kp + 127) / 128);
+}
+
+// Both operands in one launch: tiles [0, tiles(A)) are A's, the rest B's.
 template <class S>
-__global__ void __launch_bounds__(256) limb_split_kernel(const LimbArgs a) {
-  __shared__ S tile[32][33];
+__global__ void __launch_bounds__(256) limb_split_kernel(const LimbArgs a0, const LimbArgs a1) {
+  // 32 rows x 128 columns of K per tile; each thread then writes one 4-byte
+  // word (4 consecutive k) per plane and row, 128 bytes per warp
+  __shared__ S tile[32][129];
   const int tx = threadIdx.x, ty = threadIdx.y;
-  const int64_t rt = (a.rows + 31) / 32, ct = (a.kp + 31) / 32;
-  const int64_t tiles = a.batch * rt * ct;
-  const bool c_fast = a.cs == 1 || (a.rs != 1 && (a.cs < 0 ? -a.cs : a.cs) <= (a.rs < 0 ? -a.rs : a.rs));
-  for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
+  const int64_t tiles0 = limb_tiles(a0), tiles = tiles0 + limb_tiles(a1);
+  for (int64_t tt = blockIdx.x; tt < tiles; tt += gridDim.x) {
+    const bool second = tt >= tiles0;
+    const LimbArgs &a = second ? a1 : a0;
+    const int64_t t = second ? tt - tiles0 : tt;
+    const int64_t rt = (a.rows + 31) / 32, ct = (a.kp + 127) / 128;
+    const bool c_fast = a.cs == 1 || (a.rs != 1 && (a.cs < 0 ? -a.cs : a.cs) <= (a.rs < 0 ? -a.rs : a.rs));
     const int64_t b = t / (rt * ct);
     const int64_t rem = t - b * rt * ct;
-    const int64_t r0 = (rem / ct) * 32, c0 = (rem % ct) * 32;
+    const int64_t r0 = (rem / ct) * 32, c0 = (rem % ct) * 128;
     const S *src = (const S *)a.src + b * a.bs;
+    if (c_fast) {
 #pragma unroll
-    for (int i = ty; i < 32; i += 8) {
-      const int64_t r = r0 + (c_fast ? i : tx), c = c0 + (c_fast ? tx : i);
-      const S v = (r < a.rows && c < a.kc) ? src[r * a.rs + (a.k0 + c) * a.cs] : S(0);
-      if (c_fast) tile[i][tx] = v; else tile[tx][i] = v;
+      for (int i = ty; i < 32; i += 8) {
+        const int64_t r = r0 + i;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int cc = u * 32 + tx;
+          const int64_t c = c0 + cc;
+          tile[i][cc] = (r < a.rows && c < a.kc) ? src[r * a.rs + (a.k0 + c) * a.cs] : S(0);
+        }
+      }
+    } else {
+      const int64_t r = r0 + tx;
+#pragma unroll
+      for (int u = 0; u < 16; ++u) {
+        const int cc = u * 8 + ty;
+        const int64_t c = c0 + cc;
+        tile[tx][cc] = (r < a.rows && c < a.kc) ? src[r * a.rs + (a.k0 + c) * a.cs] : S(0);
+      }
     }
     __syncthreads();
+    const int64_t c = c0 + 4 * tx;
 #pragma unroll
     for (int i = ty; i < 32; i += 8) {
-      const int64_t r = r0 + i, c = c0 + tx;
+      const int64_t r = r0 + i;
       if (r < a.rows && c < a.kp) {
-        const uint64_t v = (uint64_t)(typename std::make_unsigned<S>::type)tile[i][tx];
+        using U = typename std::make_unsigned<S>::type;
+        uint64_t v[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) v[e] = (uint64_t)(U)tile[i][4 * tx + e];
         uint8_t *row = a.dst + (b * a.rows + r) * a.ld + c;
-        for (int l = 0; l < a.planes; ++l) row[(int64_t)(a.rev ? a.planes - 1 - l : l) * a.kp] = (uint8_t)(v >> (8 * l));
+        for (int l = 0; l < a.planes; ++l) {
+          const uint32_t word = (uint32_t)((v[0] >> (8 * l)) & 0xff) | (uint32_t)((v[1] >> (8 * l)) & 0xff) << 8 |
+                                (uint32_t)((v[2] >> (8 * l)) & 0xff) << 16 | (uint32_t)((v[3] >> (8 * l)) & 0xff) << 24;
+          *reinterpret_cast<uint32_t *>(row + (int64_t)(a.rev ? a.planes - 1 - l : l) * a.kp) = word;
+        }
       }
     }
     __syncthreads();
