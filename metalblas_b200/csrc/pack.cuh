@@ -36,9 +36,25 @@ __global__ void __launch_bounds__(256) pack_matrix_kernel(const PackArgs a) {
   }
 }
 
+// 16 bytes starting `off` bytes into the 32 bytes w0:w1 (little-endian words).
+__device__ __forceinline__ uint4 bytes_at(const uint4 &w0, const uint4 &w1, uint32_t off) {
+  uint32_t x0, x1, x2, x3, x4;
+  switch (off >> 2) {
+    case 0: x0 = w0.x; x1 = w0.y; x2 = w0.z; x3 = w0.w; x4 = w1.x; break;
+    case 1: x0 = w0.y; x1 = w0.z; x2 = w0.w; x3 = w1.x; x4 = w1.y; break;
+    case 2: x0 = w0.z; x1 = w0.w; x2 = w1.x; x3 = w1.y; x4 = w1.z; break;
+    default: x0 = w0.w; x1 = w1.x; x2 = w1.y; x3 = w1.z; x4 = w1.w; break;
+  }
+  const uint32_t sh = (off & 3) * 8;
+  return make_uint4(__funnelshift_r(x0, x1, sh), __funnelshift_r(x1, x2, sh), __funnelshift_r(x2, x3, sh),
+                    __funnelshift_r(x3, x4, sh));
+}
+
 // Row-contiguous sources (cs == 1, the offset / odd-pitch views): each thread
-// moves one 16-byte group of a destination row, reading its elements one by
-// one (the source may be unaligned) and writing one aligned 16-byte store.  The
+// moves one 16-byte group of a destination row with one aligned 16-byte store.
+// A full group is read as the two aligned 16-byte words it straddles (both hold
+// bytes of the group, so they lie inside the source allocation) and shifted
+// into place; the last group of a row is read element by element.  The
 // destination pitch `ld` is a multiple of 16 bytes; the group past the end of a
 // row spills into its padding, which the tensor maps never read.
 template <class U>
@@ -56,8 +72,16 @@ __global__ void __launch_bounds__(256) pack_rows16_kernel(const PackArgs a) {
     const int64_t c0 = (rem - r * groups) * G;
     const U *s = src + b * a.bs + r * a.rs + c0;
     union { uint4 q; U e[G]; } v;
+    if (c0 + G <= a.cols) {
+      const uintptr_t addr = reinterpret_cast<uintptr_t>(s);
+      const uint32_t off = (uint32_t)(addr & 15);
+      const uint4 *w = reinterpret_cast<const uint4 *>(addr - off);
+      const uint4 w0 = __ldg(w);
+      v.q = off ? bytes_at(w0, __ldg(w + 1), off) : w0;
+    } else {
 #pragma unroll
-    for (int j = 0; j < G; ++j) v.e[j] = (c0 + j < a.cols) ? s[j] : U(0);
+      for (int j = 0; j < G; ++j) v.e[j] = (c0 + j < a.cols) ? s[j] : U(0);
+    }
     *reinterpret_cast<uint4 *>(dst + (b * a.rows + r) * a.ld + c0) = v.q;
   }
 }
