@@ -13,7 +13,7 @@
 // with b_im' = -b_im when B is conjugated and s = -1 when A is conjugated, so
 // C' = A' B' is exactly C = op(A) op(B) with fp32 accumulation on the fp16
 // tensor cores (kind::f16).  B' is built once per call in the workspace; A' is
-// A's own memory when A is row-major, otherwise a packed copy.
+// A's own memory when A is row-major, otherwise a packed copy (pack.cuh).
 #pragma once
 #include "mb_common.cuh"
 
@@ -44,18 +44,6 @@ __global__ void __launch_bounds__(256) c32_build_b_kernel(const C32Prep p, int64
     __half2 *out = p.dst + b * (2 * p.rows) * ld;
     out[(2 * k) * ld + n] = __halves2half2(re, im);
     out[(2 * k + 1) * ld + n] = __halves2half2(s_im, s_re);
-  }
-}
-
-// A (M x K complex, any strides) -> A' (M x 2K real fp16, row-major, row pitch
-// `ld` half2 pairs, dense per batch).  Grid-stride over batch * M * K elements.
-__global__ void __launch_bounds__(256) c32_pack_a_kernel(const C32Prep p, int64_t ld) {
-  const int64_t total = p.batch * p.rows * p.cols;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t k = i % p.cols;
-    const int64_t m = (i / p.cols) % p.rows;
-    const int64_t b = i / (p.cols * p.rows);
-    p.dst[b * p.rows * ld + m * ld + k] = p.src[b * p.bs + m * p.rs + k * p.cs];
   }
 }
 

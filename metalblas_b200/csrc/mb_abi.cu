@@ -1289,12 +1289,11 @@ int launch_c32(const Op &o, const Plan &pl, EpiScalars e, void *ws, int sms, cud
   int rc = cuda_check(cudaGetLastError(), "complex32 B' build");
   if (rc) return rc;
   if (pl.c32_pack_a) {
-    C32Prep pa{};
-    pa.src = reinterpret_cast<const __half2 *>(o.A); pa.dst = ap;
-    pa.rows = o.M; pa.cols = o.K; pa.rs = o.a_rs; pa.cs = o.a_cs; pa.bs = o.sA;
-    pa.batch = pl.c32_a_batches;
-    const int64_t na = pa.batch * pa.rows * pa.cols;
-    c32_pack_a_kernel<<<(unsigned)std::min<int64_t>(ceil_div(na, 256), grid_cap), 256, 0, st>>>(pa, pl.c32_lda);
+    // A' rows = A's rows as half2 pairs (4-byte elements), through the tiled pack
+    PackArgs pa{o.A, ap, o.M, o.K, o.a_rs, o.a_cs, o.sA, pl.c32_a_batches, pl.c32_lda};
+    const int64_t tiles = pa.batch * ceil_div(o.M, 32) * ceil_div(o.K, 32);
+    pack_matrix_kernel<uint32_t><<<(unsigned)std::max<int64_t>(1, std::min<int64_t>(tiles, grid_cap)), dim3(32, 8), 0,
+                                   st>>>(pa);
     rc = cuda_check(cudaGetLastError(), "complex32 A' pack");
     if (rc) return rc;
   }
@@ -1316,8 +1315,8 @@ int launch_packed(const Op &o, const Plan &pl, const EpiScalars &e, void *ws, in
       pack_rows16_kernel<U><<<(unsigned)std::max<int64_t>(1, std::min<int64_t>(ceil_div(n, 256), grid_cap)), 256, 0,
                               st>>>(a);
     } else {
-      const int64_t n = batches * rows * cols;
-      pack_matrix_kernel<U><<<(unsigned)std::max<int64_t>(1, std::min<int64_t>(ceil_div(n, 256), grid_cap)), 256, 0,
+      const int64_t tiles = batches * ceil_div(rows, 32) * ceil_div(cols, 32);
+      pack_matrix_kernel<U><<<(unsigned)std::max<int64_t>(1, std::min<int64_t>(tiles, grid_cap)), dim3(32, 8), 0,
                               st>>>(a);
     }
     return cuda_check(cudaGetLastError(), what);

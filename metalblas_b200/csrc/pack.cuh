@@ -18,21 +18,37 @@ struct PackArgs {
   int64_t batch, ld;    // batches copied; destination row pitch in elements
 };
 
-// Grid-stride over batch * rows * cols elements, columns fastest, so a warp
-// reads consecutive columns of one row (coalesced when cs == 1) and writes them
-// consecutively.  U is the element's storage type (same-size unsigned).
+// Any strides: 32 x 32 tiles through shared memory, read along whichever of
+// rows / columns has the smaller source stride (coalesced for a column-major
+// or transposed view) and written along the destination rows.  Block 32 x 8,
+// grid-stride over tiles.  U is the element's storage type (same-size unsigned).
 template <class U>
 __global__ void __launch_bounds__(256) pack_matrix_kernel(const PackArgs a) {
+  __shared__ U tile[32][33];
   const U *src = static_cast<const U *>(a.src);
   U *dst = static_cast<U *>(a.dst);
-  const int64_t per_batch = a.rows * a.cols;
-  const int64_t total = a.batch * per_batch;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t b = i / per_batch;
-    const int64_t rem = i - b * per_batch;
-    const int64_t r = rem / a.cols;
-    const int64_t c = rem - r * a.cols;
-    dst[(b * a.rows + r) * a.ld + c] = src[b * a.bs + r * a.rs + c * a.cs];
+  const int tx = threadIdx.x, ty = threadIdx.y;
+  const int64_t rt = (a.rows + 31) / 32, ct = (a.cols + 31) / 32;
+  const int64_t tiles = a.batch * rt * ct;
+  const bool c_fast = a.cs == 1 || (a.rs != 1 && (a.cs < 0 ? -a.cs : a.cs) <= (a.rs < 0 ? -a.rs : a.rs));
+  for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
+    const int64_t b = t / (rt * ct);
+    const int64_t rem = t - b * rt * ct;
+    const int64_t r0 = (rem / ct) * 32, c0 = (rem % ct) * 32;
+    const U *sb = src + b * a.bs;
+#pragma unroll
+    for (int i = ty; i < 32; i += 8) {
+      const int64_t r = r0 + (c_fast ? i : tx), c = c0 + (c_fast ? tx : i);
+      const U v = (r < a.rows && c < a.cols) ? sb[r * a.rs + c * a.cs] : U(0);
+      if (c_fast) tile[i][tx] = v; else tile[tx][i] = v;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = ty; i < 32; i += 8) {
+      const int64_t r = r0 + i, c = c0 + tx;
+      if (r < a.rows && c < a.cols) dst[(b * a.rows + r) * a.ld + c] = tile[i][tx];
+    }
+    __syncthreads();
   }
 }
 
