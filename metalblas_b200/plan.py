@@ -65,7 +65,9 @@ def _candidates(primary: str, d):
     if not primary.startswith("tc"):
         return []
     f = dict(kv.split("=") for kv in primary.split()[1:] if "=" in kv)
-    bn, split, swap = int(f["bn"]), int(f["split"]), int(f["swap"])
+    if "bn" not in f:
+        return []
+    bn, split, swap = int(f["bn"]), int(f.get("split", 1)), int(f.get("swap", 0))
     tc = _lib.MB_BACKEND_TC
     out = []
     for obn in (64, 128, 256):
