@@ -41,8 +41,11 @@ typedef enum mb_dtype {
  * (metalblas/float_dispatch.py:802-852). */
 typedef enum mb_backend {
     MB_BACKEND_AUTO = 0,   /* tile table picks                                  */
-    MB_BACKEND_GEMV = 1,   /* "gemv": bandwidth kernels, needs M==1 or N==1     */
-    MB_BACKEND_TC   = 2,   /* "mpp_tensor": tcgen05/TMEM tensor-core GEMM       */
+    MB_BACKEND_GEMV = 1,   /* "gemv": bandwidth kernels, needs M==1 or N==1
+                            * (or min(M, N) <= 4 for 16-bit floats, <= 32 fp32) */
+    MB_BACKEND_TC   = 2,   /* "mpp_tensor": tcgen05/TMEM tensor-core GEMM; fp32
+                            * and complex64 as 3xTF32, 16/32/64-bit integers as
+                            * byte planes on the int8 tensor cores (bit-exact)  */
     MB_BACKEND_SIMT = 3    /* "simd" (and "mpp" fallback): CUDA-core FFMA/IMAD  */
 } mb_backend;
 
