@@ -1346,7 +1346,7 @@ int launch_3xtf32(const Op &o, const Plan &pl, const EpiScalars &e, void *ws, in
   auto split = [&](const void *src, float *hi, float *lo, int64_t rows, int64_t cols, int64_t rs, int64_t cs,
                    int64_t bs, int64_t batches, const char *what) {
     SplitArgs a{static_cast<const float *>(src), hi, lo, flag, rows, cols, rs, cs, bs, batches, pl.x3_ldk};
-    const int64_t tiles = batches * ceil_div(rows, 32) * ceil_div(cols, 32);
+    const int64_t tiles = batches * ceil_div(rows, 32) * ceil_div(cols, 128);
     split_tf32_kernel<<<(unsigned)std::max<int64_t>(1, std::min<int64_t>(tiles, (int64_t)sms * 16)), dim3(32, 8), 0,
                         st>>>(a);
     return cuda_check(cudaGetLastError(), what);
@@ -1377,7 +1377,7 @@ int launch_c64x3(const Op &o, const Plan &pl, const EpiScalars &e, void *ws, int
                    int64_t bs, int64_t batches, int mode, const char *what) {
     SplitArgs a{static_cast<const float *>(src), hi, lo, flag, rows, cols, rs, cs, bs, batches, pl.x3_ldk,
                 mode, o.conj_a, o.conj_b};
-    const int64_t tiles = batches * ceil_div(rows, 32) * ceil_div(cols, 32);
+    const int64_t tiles = batches * ceil_div(rows, 32) * ceil_div(cols, 128);
     split_tf32_kernel<<<(unsigned)std::max<int64_t>(1, std::min<int64_t>(tiles, (int64_t)sms * 16)), dim3(32, 8), 0,
                         st>>>(a);
     return cuda_check(cudaGetLastError(), what);

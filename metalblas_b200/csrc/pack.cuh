@@ -153,40 +153,68 @@ __device__ __forceinline__ float split_load(const SplitArgs &a, const float *src
   return (c & 1) ? s * v.x : im;
 }
 
-// dst[b][r][c] = split(src(b, r, c)) through a 32 x 32 shared-memory tile, so
-// both the source read (along whichever of r / c is contiguous) and the
-// destination rows are coalesced.  Block 32 x 8, grid-stride over tiles.
+// dst[b][r][c] = split(src(b, r, c)) through a shared-memory tile, so both the
+// source read (along whichever of r / c is contiguous) and the destination rows
+// are coalesced.  Block 32 x 8, grid-stride over tiles.
 __global__ void __launch_bounds__(256) split_tf32_kernel(const SplitArgs a) {
-  __shared__ float tile[32][33];
+  // 32 rows x 128 columns per tile; each thread then splits 4 consecutive
+  // columns of a row and writes them with one 16-byte store per part
+  __shared__ float tile[32][129];
   const int tx = threadIdx.x, ty = threadIdx.y;
-  const int64_t rt = (a.rows + 31) / 32, ct = (a.cols + 31) / 32;
+  const int64_t rt = (a.rows + 31) / 32, ct = (a.cols + 127) / 128;
   const int64_t tiles = a.batch * rt * ct;
   const bool c_fast = a.cs == 1 || (a.rs != 1 && (a.cs < 0 ? -a.cs : a.cs) <= (a.rs < 0 ? -a.rs : a.rs));
   for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
     const int64_t b = t / (rt * ct);
     const int64_t rem = t - b * rt * ct;
-    const int64_t r0 = (rem / ct) * 32, c0 = (rem % ct) * 32;
+    const int64_t r0 = (rem / ct) * 32, c0 = (rem % ct) * 128;
     const float *src = a.src + b * a.bs * (a.mode ? 2 : 1);
+    if (c_fast) {
 #pragma unroll
-    for (int i = ty; i < 32; i += 8) {
-      const int64_t r = r0 + (c_fast ? i : tx), c = c0 + (c_fast ? tx : i);
-      const float v = (r < a.rows && c < a.cols) ? split_load(a, src, r, c) : 0.f;
-      if (c_fast) tile[i][tx] = v; else tile[tx][i] = v;
-    }
-    __syncthreads();
+      for (int i = ty; i < 32; i += 8) {
+        const int64_t r = r0 + i;
 #pragma unroll
-    for (int i = ty; i < 32; i += 8) {
-      const int64_t r = r0 + i, c = c0 + tx;
-      if (r < a.rows && c < a.cols) {
-        float hi, lo;
-        const float x = tile[i][tx];
-        if (!isfinite(x)) *a.nonfinite = 1;
-        tf32_split(x, hi, lo);
-        const int64_t o = (b * a.rows + r) * a.ld + c;
-        a.hi[o] = hi;
-        a.lo[o] = lo;
+        for (int u = 0; u < 4; ++u) {
+          const int cc = u * 32 + tx;
+          const int64_t c = c0 + cc;
+          tile[i][cc] = (r < a.rows && c < a.cols) ? split_load(a, src, r, c) : 0.f;
+        }
+      }
+    } else {
+      const int64_t r = r0 + tx;
+#pragma unroll
+      for (int u = 0; u < 16; ++u) {
+        const int cc = u * 8 + ty;
+        const int64_t c = c0 + cc;
+        tile[tx][cc] = (r < a.rows && c < a.cols) ? split_load(a, src, r, c) : 0.f;
       }
     }
+    __syncthreads();
+    const int64_t c = c0 + 4 * tx;
+    bool bad = false;
+#pragma unroll
+    for (int i = ty; i < 32; i += 8) {
+      const int64_t r = r0 + i;
+      if (r < a.rows && c < a.cols) {
+        float hi[4], lo[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float x = tile[i][4 * tx + e];
+          bad |= !isfinite(x);
+          tf32_split(x, hi[e], lo[e]);
+        }
+        const int64_t o = (b * a.rows + r) * a.ld + c;
+        if (c + 4 <= a.cols) {  // ld is a multiple of 4 floats and the parts are 256-byte aligned
+          *reinterpret_cast<float4 *>(a.hi + o) = make_float4(hi[0], hi[1], hi[2], hi[3]);
+          *reinterpret_cast<float4 *>(a.lo + o) = make_float4(lo[0], lo[1], lo[2], lo[3]);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            if (c + e < a.cols) { a.hi[o + e] = hi[e]; a.lo[o + e] = lo[e]; }
+        }
+      }
+    }
+    if (bad) *a.nonfinite = 1;
     __syncthreads();
   }
 }
