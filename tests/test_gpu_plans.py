@@ -358,7 +358,9 @@ def test_integer_byte_planes_bit_exact(dtype):
     import metalblas_b200 as mb
     name = NAME[dtype]
     gen = torch.Generator().manual_seed(17)
-    for (M, N, K) in [(256, 320, 768), (1000, 1000, 1000), (130, 70, 5000), (4, 600, 300), (300, 200, 17)]:
+    # K = 17000 runs in several exact chunks for every width (int16 2, int32 3, int64 5)
+    for (M, N, K) in [(256, 320, 768), (1000, 1000, 1000), (130, 70, 5000), (4, 600, 300), (300, 200, 17),
+                      (40, 48, 17000)]:
         a = rand((M, K), dtype, gen, full_range=True)
         b = rand((K, N), dtype, gen, full_range=True)
         ref = orc.product(to_np(a), to_np(b), name)
