@@ -309,8 +309,8 @@ int sk_max_parts(int64_t tail, int64_t kb, int64_t G) {
   return (int)mx;
 }
 
-void choose_tc_tile(const Op &o, int sms, int force_bn, int force_split, int force_pair, int force_sk, bool have_ws,
-                    Plan &pl) {
+void choose_tc_tile_uncached(const Op &o, int sms, int force_bn, int force_split, int force_pair, int force_sk,
+                             bool have_ws, Plan &pl) {
   const int esz = elem_size(o.dt);
   const int64_t BK = 128 / esz;
   // fp32 runs as 3xTF32: three tf32 MMAs (half the bf16 rate) per K-block and
@@ -440,6 +440,56 @@ void choose_tc_tile(const Op &o, int sms, int force_bn, int force_split, int for
                (int)seff, kbp, 0, 0);
     }
   }
+}
+
+// The tile choice is a pure function of the operands' shapes, strides and
+// alignment and of the overrides: memoised per thread so that a repeated call
+// (the usual case: the same layer every step) skips the cost-model search.
+struct TileKey {
+  int64_t v[20];
+  bool operator==(const TileKey &k) const { return memcmp(v, k.v, sizeof(v)) == 0; }
+};
+struct TileKeyHash {
+  size_t operator()(const TileKey &k) const {
+    uint64_t h = 1469598103934665603ull;
+    for (int64_t x : k.v) { h ^= (uint64_t)x; h *= 1099511628211ull; }
+    return (size_t)h;
+  }
+};
+struct TileChoice {
+  int bn, splits, a_mn, b_mn, tail_half, pair, sk;
+  int64_t tiles_m, tiles_n, kb_total, kb_per_split, dp_tiles, sk_ctas;
+  double est;
+};
+
+void choose_tc_tile(const Op &o, int sms, int force_bn, int force_split, int force_pair, int force_sk, bool have_ws,
+                    Plan &pl) {
+  const int esz = elem_size(o.dt);
+  TileKey k;
+  int64_t *v = k.v;
+  v[0] = o.dt; v[1] = o.M; v[2] = o.N; v[3] = o.K; v[4] = o.batch;
+  v[5] = o.a_rs; v[6] = o.a_cs; v[7] = o.b_rs; v[8] = o.b_cs;
+  v[9] = o.sA == 0 ? -1 : (o.sA * esz) % 16;  // broadcast, else whether TMA can step batches
+  v[10] = o.sB == 0 ? -1 : (o.sB * esz) % 16;
+  v[11] = (o.sA < 0) | ((o.sB < 0) << 1);
+  v[12] = (int64_t)(reinterpret_cast<uintptr_t>(o.A) & 15) | ((int64_t)(reinterpret_cast<uintptr_t>(o.B) & 15) << 8);
+  v[13] = sms; v[14] = force_bn; v[15] = force_split; v[16] = force_pair; v[17] = force_sk; v[18] = have_ws;
+  v[19] = 0;
+  thread_local std::unordered_map<TileKey, TileChoice, TileKeyHash> cache;
+  auto it = cache.find(k);
+  if (it == cache.end()) {
+    Plan t;
+    t.bn = 0;
+    choose_tc_tile_uncached(o, sms, force_bn, force_split, force_pair, force_sk, have_ws, t);
+    if (cache.size() >= 4096) cache.clear();
+    it = cache.emplace(k, TileChoice{t.bn, t.splits, t.a_mn, t.b_mn, t.tail_half, t.pair, t.sk, t.tiles_m, t.tiles_n,
+                                     t.kb_total, t.kb_per_split, t.dp_tiles, t.sk_ctas, t.est}).first;
+  }
+  const TileChoice &c = it->second;
+  if (!c.bn) return;  // no tile fits: pl untouched, as the search leaves it
+  pl.bn = c.bn; pl.splits = c.splits; pl.a_mn = c.a_mn; pl.b_mn = c.b_mn; pl.tail_half = c.tail_half;
+  pl.pair = c.pair; pl.sk = c.sk; pl.tiles_m = c.tiles_m; pl.tiles_n = c.tiles_n; pl.kb_total = c.kb_total;
+  pl.kb_per_split = c.kb_per_split; pl.dp_tiles = c.dp_tiles; pl.sk_ctas = c.sk_ctas; pl.est = c.est;
 }
 
 // Fill pl for the TC path on operands o (possibly swapped); false if TMA can't.
