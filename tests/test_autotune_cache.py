@@ -116,3 +116,20 @@ def test_gemv_rejects_bad_arguments(lib):
     assert call(rows=-1) == _lib.MB_ERR_INVALID
     assert call(ldw=4) == _lib.MB_ERR_INVALID
     assert call(dtype=42) == _lib.MB_ERR_UNSUPPORTED
+
+
+def test_tile_choice_memo_follows_alignment_and_strides():
+    """The planner memoises its tile choice per thread; a descriptor that
+    differs only in operand alignment or strides must get its own plan, and the
+    first descriptor its original plan back afterwards."""
+    d = _desc(2048, 2048, 2048)
+    aligned = _lib.plan_query(d)
+    assert aligned.startswith("tc ") and "a_mn=0" in aligned, aligned
+    d.A = (1 << 20) + 2  # not 16-byte aligned: TMA cannot read A in place
+    assert _lib.plan_query(d).startswith("tc_packed"), _lib.plan_query(d)
+    d.A = 1 << 20
+    assert _lib.plan_query(d) == aligned
+    d.a_rs, d.a_cs = 1, 2048  # column-major A: MN-major tiles
+    assert "a_mn=1" in _lib.plan_query(d), _lib.plan_query(d)
+    d.a_rs, d.a_cs = 2048, 1
+    assert _lib.plan_query(d) == aligned
