@@ -133,3 +133,24 @@ def test_tile_choice_memo_follows_alignment_and_strides():
     assert "a_mn=1" in _lib.plan_query(d), _lib.plan_query(d)
     d.a_rs, d.a_cs = 2048, 1
     assert _lib.plan_query(d) == aligned
+
+
+def test_routing_of_wide_integers_complex64_and_thin_fp32():
+    """The planner's routing rules, read from its plan text (no GPU): 16/32/64-bit
+    integers go to byte planes on the int8 tensor cores (in exact K chunks),
+    tiny ones stay on IMAD; complex64 runs as one real 3xTF32 GEMM unless a
+    complex alpha needs the complex epilogue; thin fp32 products take the
+    several-row column GEMV."""
+    assert _lib.plan_query(_desc(2048, 2048, 2048, torch.int32)).startswith("tc_int_planes planes=4")
+    assert _lib.plan_query(_desc(2048, 2048, 2048, torch.int16)).startswith("tc_int_planes planes=2")
+    assert "chunks=2" in _lib.plan_query(_desc(130, 70, 5000, torch.int64))
+    assert _lib.plan_query(_desc(64, 64, 64, torch.int32)) == "simt"
+    c = _desc(4096, 4096, 4096, torch.complex64)
+    assert _lib.plan_query(c).startswith("tc_c64x3"), _lib.plan_query(c)
+    c.epilogue, c.alpha_nz, c.beta_nz, c.alpha_re, c.alpha_im = 1, 1, 0, 2.0, 1.0  # complex alpha, no bias
+    assert _lib.plan_query(c) == "simt"
+    c.alpha_im = 0.0  # a real alpha keeps the tensor cores
+    assert _lib.plan_query(c).startswith("tc_c64x3")
+    assert "rows=4" in _lib.plan_query(_desc(4, 14336, 4096, torch.float32))
+    # the column GEMV fills whole waves of resident CTAs: 112 column blocks x 5 splits
+    assert _lib.plan_query(_desc(1, 28672, 16384)) == "gemv_cols vec=8 ksplit=5"
