@@ -131,8 +131,18 @@ int mb_gemm(const mb_gemm_desc *d, void *stream);
  * CUDA allocator.  Same descriptor and plan as mb_gemm, but d->workspace is
  * ignored: split-K scratch comes from a buffer compiled into the library,
  * MB_NOALLOC_SCRATCH_BYTES per GPU, held by every GPU that loads the library
- * until the process exits.  A plan that needs more scratch than that is
- * rejected with MB_ERR_WORKSPACE (set split_k = 1 to run it without scratch).
+ * until the process exits.  When the planner's first choice needs more
+ * scratch than that and the caller forced no K split (split_k <= 1, stream_k
+ * != 2), the call is planned again as mb_gemm plans without a workspace:
+ * bf16/fp16/int8/uint8 tensor-core products drop their split-K / stream-K
+ * tail, and the products whose tensor-core forms need operand copies in
+ * scratch (complex32, operands TMA cannot address, fp32 and complex64 as
+ * 3xTF32, 16/32/64-bit integers as byte planes) run on the CUDA-core FFMA /
+ * IMAD kernel under backend AUTO, several times slower than mb_gemm for large
+ * products, and are refused with MB_ERR_WORKSPACE under backend TC.  A forced
+ * split (split_k > 1 or stream_k == 2) whose scratch does not fit is refused
+ * with MB_ERR_WORKSPACE (split_k = 1 runs a plain tensor-core product without
+ * scratch).
  * The call allocates nothing: no cudaMalloc / cudaFree, no allocating library
  * routine.  The first call on a device looks up the buffer's device address
  * (per-device set-up); make that first call before any stream capture.  All

@@ -1864,25 +1864,39 @@ int mb_gemm_noalloc(const mb_gemm_desc *d, void *stream) {
   int rc = plan_for(&q, pl, o, sms);
   if (rc) return rc;
   if (pl.kind == PK_EMPTY) return MB_OK;
-  if ((pl.kind == PK_TC_C32 || pl.kind == PK_TC_PACKED || pl.kind == PK_TC_3XTF32 || pl.kind == PK_TC_C64X3 ||
-       pl.kind == PK_TC_LIMB) &&
-      pl.ws_bytes > (int64_t)MB_NOALLOC_SCRATCH_BYTES &&
-      q.backend == MB_BACKEND_AUTO) {
-    // complex32 on the tensor cores needs its expanded B' in scratch, packed
-    // operands their copies; when they do not fit, the CUDA-core kernel (no
-    // scratch, any layout) computes the product
-    q.backend = MB_BACKEND_SIMT;
-    rc = plan_for(&q, pl, o, sms);
-    if (rc) return rc;
+  const int64_t cap = (int64_t)MB_NOALLOC_SCRATCH_BYTES;
+  const bool split_forced = d->split_k > 1 || d->stream_k == 2;
+  if (pl.ws_bytes > cap && !split_forced) {
+    // The planner's first choice needs more scratch than the built-in buffer
+    // holds, and the caller did not ask for a K split: plan again as mb_gemm
+    // does without a workspace.  Plain tensor-core products then run without a
+    // split-K / stream-K tail; complex32, packed operands, 3xTF32 (fp32,
+    // complex64) and integer byte planes need scratch for their operand copies,
+    // so under AUTO those products move to the CUDA-core kernel (no scratch,
+    // any layout), and under an explicit tensor-core backend they are refused.
+    mb_gemm_desc r = q;
+    r.workspace_bytes = 0;
+    rc = plan_for(&r, pl, o, sms);
+    if (rc)
+      return fail(MB_ERR_WORKSPACE,
+                  "mb_gemm_noalloc: this product needs operand scratch beyond the built-in %lld bytes on the "
+                  "requested backend; call mb_gemm with a workspace or use backend AUTO",
+                  (long long)cap);
   }
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   void *scratch = nullptr;
   if (pl.ws_bytes > 0) {
-    if (pl.ws_bytes > (int64_t)MB_NOALLOC_SCRATCH_BYTES)
+    if (pl.ws_bytes > cap) {
+      if (pl.kind == PK_TC || pl.kind == PK_GEMV_COLS || pl.kind == PK_GEMV_ROWS)
+        return fail(MB_ERR_WORKSPACE,
+                    "mb_gemm_noalloc: this plan needs %lld bytes of split-K scratch but the built-in scratch "
+                    "holds %lld bytes; set split_k=1 (no scratch) or call mb_gemm with a workspace",
+                    (long long)pl.ws_bytes, (long long)cap);
       return fail(MB_ERR_WORKSPACE,
-                  "mb_gemm_noalloc: this plan needs %lld bytes of split-K scratch but the built-in scratch "
-                  "holds %lld bytes; set split_k=1 (no scratch) or call mb_gemm with a workspace",
-                  (long long)pl.ws_bytes, (long long)MB_NOALLOC_SCRATCH_BYTES);
+                  "mb_gemm_noalloc: this plan needs %lld bytes of scratch but the built-in scratch holds %lld "
+                  "bytes; call mb_gemm with a workspace",
+                  (long long)pl.ws_bytes, (long long)cap);
+    }
     rc = noalloc_scratch(&scratch);
     if (rc) return rc;
     rc = cuda_check(cudaMemsetAsync(scratch, 0, (size_t)kTicketBytes, st), "clear noalloc ticket counters");

@@ -126,3 +126,61 @@ def test_noalloc_rejects_plans_beyond_capacity():
     ref = orc.product(to_np(a[:8]), to_np(b), "bfloat16")
     ok, err = orc.check(to_np(c[:8]), ref, "bfloat16")
     assert ok, err
+
+
+def test_noalloc_replans_auto_shapes_beyond_capacity():
+    """A decode-sized bf16 product whose first-choice plan (a split-K tail)
+    needs more than the built-in scratch: with no split asked for, the call is
+    planned again without scratch and must still run, matching mb_gemm and the
+    oracle on a row sample."""
+    lib = _lib.load()
+    gen = torch.Generator().manual_seed(13)
+    a = rand((128, 16384), torch.bfloat16, gen)
+    b = rand((16384, 8192), torch.bfloat16, gen)
+    c = torch.empty(128, 8192, dtype=torch.bfloat16, device="cuda")
+    d = _desc(a, b, c)
+    d.workspace_bytes = -1
+    need = int(lib.mb_gemm_workspace_size(ctypes.byref(d)))
+    assert need > CAPACITY, f"expected a first-choice plan beyond the scratch, got {need} bytes"
+    ref, _, plan = _with_mb_gemm(a, b)
+    for call in range(2):
+        got = _with_noalloc(a, b)
+        ok, err = orc.check(to_np(got), to_np(ref).astype("float64"), "bfloat16")
+        assert ok, f"call {call}: differs from mb_gemm (error {err:.3e}; mb_gemm plan {plan})"
+    rows = [0, 37, 127]
+    want = orc.product(to_np(a[rows]), to_np(b), "bfloat16")
+    ok, err = orc.check(to_np(got[rows]), want, "bfloat16")
+    assert ok, f"oracle row sample: error {err:.3e}"
+
+
+def test_noalloc_fp32_cuda_core_fallback_against_oracle():
+    """fp32 at 1024^3 runs as 3xTF32 in mb_gemm, whose split operands need
+    more than the built-in scratch; under backend AUTO the allocation-free call
+    computes it on the CUDA-core FFMA kernel instead, within the fp32 bound
+    (relative Frobenius <= 1e-5 against the fp64 oracle)."""
+    lib = _lib.load()
+    gen = torch.Generator().manual_seed(14)
+    a = rand((1024, 1024), torch.float32, gen)
+    b = rand((1024, 1024), torch.float32, gen)
+    c = torch.empty(1024, 1024, dtype=torch.float32, device="cuda")
+    d = _desc(a, b, c)
+    d.workspace_bytes = -1
+    assert int(lib.mb_gemm_workspace_size(ctypes.byref(d))) > CAPACITY
+    want = orc.product(to_np(a), to_np(b), "float32")
+    for call in range(2):
+        got = _with_noalloc(a, b)
+        ok, err = orc.check(to_np(got), want, "float32")
+        assert ok, f"call {call}: error {err:.3e}"
+
+
+def test_noalloc_direct_oracle_check_with_epilogue():
+    """One split-K addmm through the allocation-free entry point checked against
+    the oracle itself (not only against mb_gemm)."""
+    gen = torch.Generator().manual_seed(15)
+    a = rand((256, 16384), torch.bfloat16, gen)
+    b = rand((16384, 1024), torch.bfloat16, gen)
+    bias = rand((1024,), torch.bfloat16, gen)
+    got = _with_noalloc(a, b, tile_n=64, split_k=4, epilogue=(bias, 0.5, 2.0))
+    want = orc.fused(to_np(bias)[None, :], to_np(a), to_np(b), 0.5, 2.0, "bfloat16")
+    ok, err = orc.check(to_np(got), want, "bfloat16")
+    assert ok, f"error {err:.3e}"
