@@ -37,7 +37,7 @@ import torch
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-PUBLISHED_M5_MAX_4096 = 42.95   # bf16 4096^3, Apple M5 Max, perf_benchs/M5_Max.md:17
+PUBLISHED_M5_MAX_4096 = 42.95   # the reference's published bf16 4096^3 rate, Apple M5 Max (perf_benchs/M5_Max.md:17)
 
 
 def _peaks():
@@ -171,21 +171,26 @@ WORKLOADS = {
 }
 
 
-def _inputs(w, rank, world):
+def _global_inputs(w, world):
+    """Host A [M, K] and the global B [K, N * world] of the weak-scaling run
+    (seed 0; A drawn first)."""
     g = torch.Generator().manual_seed(0)
     M, N, K, dt = w["M"], w["N"], w["K"], w["dtype"]
     if dt in (torch.int8, torch.uint8):
         info = torch.iinfo(dt)
         a = torch.randint(info.min, info.max + 1, (M, K), dtype=dt, generator=g)
-        b_full = torch.randint(info.min, info.max + 1, (K, N * world), dtype=dt, generator=g) if world > 1 else None
-        b = torch.randint(info.min, info.max + 1, (K, N), dtype=dt, generator=g) if world == 1 else None
+        b = torch.randint(info.min, info.max + 1, (K, N * world), dtype=dt, generator=g)
     else:
         a = torch.randn(M, K, generator=g).to(dt)
-        b_full = torch.randn(K, N * world, generator=g).to(dt) if world > 1 else None
-        b = torch.randn(K, N, generator=g).to(dt) if world == 1 else None
-    if world > 1:
-        b = b_full[:, rank * N:(rank + 1) * N].contiguous()
+        b = torch.randn(K, N * world, generator=g).to(dt)
     return a, b
+
+
+def _inputs(w, rank, world):
+    """Host A and this rank's column block of the global B."""
+    a, b = _global_inputs(w, world)
+    N = w["N"]
+    return a, (b[:, rank * N:(rank + 1) * N].contiguous() if world > 1 else b)
 
 
 def run_ours(args, w, rank, world, device):
@@ -240,28 +245,31 @@ def run_ours(args, w, rank, world, device):
         ok_rows = {"ok": bool(ok_rows), "rel_frobenius_or_mismatch": err, "rows_checked": int(len(idx))}
 
     bmm_line = run_bmm_sharded(args, rank, world, device) if not args.no_bmm else None
+    large = run_large_nshard(args, rank, world, device) if not args.no_multi else None
+    skinny = run_skinny(args, rank, world, device) if not args.no_multi else None
 
-    # gathered variant (N > 1): all-gather the output shards over NVLink each step
-    gathered = None
+    # gathered variants (N > 1): the whole row-major C [M, N * ranks] on every
+    # rank after every step.  "gathered": the product writes its column block
+    # into every rank's copy of C from its epilogue (fused peer stores over
+    # NVLink) and one barrier ends the step; "gathered_nccl": the product, then
+    # a NCCL all-gather of the blocks (the unfused baseline).
+    gathered = gathered_nccl = None
     if world > 1:
-        import torch.distributed as dist
-        G = torch.empty(world * M, N, dtype=dt, device=device)
-        for i in range(3):
-            mb.matmul(As[i % SETS], Bs[i % SETS], out=Cs[i % SETS])
-            dist.all_gather_into_tensor(G, Cs[i % SETS])
-        _barrier(world, device)
-        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        g0.record(stream)
-        for i in range(args.steps):
-            mb.matmul(As[i % SETS], Bs[i % SETS], out=Cs[i % SETS])
-            dist.all_gather_into_tensor(G, Cs[i % SETS])
-        g1.record(stream)
-        g1.synchronize()
-        _barrier(world, device)
-        gms = _max_over_ranks(g0.elapsed_time(g1) / args.steps, world, device)
+        from metalblas_b200 import shard
+        n_total = N * world
+        gms = _timed(lambda i: shard.sharded_matmul_n(As[i % SETS], Bs[i % SETS], n_total, gather=True),
+                     args.steps, world, device)
+        Cg = shard.sharded_matmul_n(As[0], Bs[0], n_total, gather=True)
+        chk = _check_gathered(Cg, a_h, lambda cols: _weak_b_cols(w, cols, world), dt, world, device, rank,
+                              row_step=max(1, M // 32), col_step=max(1, n_total // 2048))
         gathered = {"value": flops * world / (gms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": gms,
-                    "layout": "C as its N_ranks column blocks, [N_ranks, M, N/N_ranks], on every rank",
-                    "collective": "NCCL all_gather_into_tensor after each product"}
+                    "layout": f"row-major C [{M}, {n_total}] on every rank",
+                    "collective": "fused: tcgen05 epilogue stores each tile into every rank's C over NVLink "
+                                  "(mb_gemm_peer), then one barrier", "check": chk}
+        nms = _timed(lambda i: shard.sharded_matmul_n(As[i % SETS], Bs[i % SETS], n_total, gather=True,
+                                                      fused=False), args.steps, world, device)
+        gathered_nccl = {"value": flops * world / (nms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": nms,
+                         "collective": "product, then NCCL all_gather_into_tensor of the blocks (unfused)"}
 
     # e2e: host buffers -> public API -> host result, every step.  Three streams
     # (copy-in, compute, copy-out) and two device buffer sets, so step i's
@@ -320,6 +328,7 @@ def run_ours(args, w, rank, world, device):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         from oracle import cpu_baseline as cb
+        torch.set_num_threads(os.cpu_count() or 1)
         rows = cb.calibrate_rows(a_h, b_h, 2.0)
         reps = 5
         sec, rows = cb.time_rows(a_h, b_h, rows, reps)
@@ -337,8 +346,9 @@ def run_ours(args, w, rank, world, device):
                    "l2": "inputs rotate over 4 sets (256 MB > 2 x 126 MB L2)", "plan": plan,
                    "vs_baseline_ref": "Apple M5 Max 42.95 TFLOP/s (perf_benchs/M5_Max.md:17)"},
         "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gathered": gathered,
+        "gathered_nccl": gathered_nccl,
         "gpu_launches": args.steps, "check": ok_rows, "clocks": sampler.summary() if rank == 0 else None,
-        "bmm": bmm_line,
+        "bmm": bmm_line, "large": large, "skinny": skinny,
     }
 
 
@@ -358,33 +368,195 @@ def run_bmm_sharded(args, rank, world, device):
     As = [torch.randn(Bt, M, K, generator=g, device=device, dtype=torch.bfloat16) for _ in range(2)]
     Bs = [torch.randn(Bt, K, N, generator=g, device=device, dtype=torch.bfloat16) for _ in range(2)]
     steps = max(5, min(args.steps, 50))
-    stream = torch.cuda.current_stream(device)
-
-    def timed(fn):
-        for i in range(3):
-            fn(i % 2)
-        _barrier(world, device)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for i in range(steps):
-            fn(i % 2)
-        e1.record(stream)
-        e1.synchronize()
-        _barrier(world, device)
-        return _max_over_ranks(e0.elapsed_time(e1) / steps, world, device)
-
-    ms = timed(lambda i: shard.sharded_bmm(As[i], Bs[i], gather=False))
+    ms = _timed(lambda i: shard.sharded_bmm(As[i % 2], Bs[i % 2], gather=False), steps, world, device)
     flops = 2.0 * Bt * M * N * K
     out = {"workload": "bf16 bmm [256,1024,1024]@[256,1024,1024], batch sharded over ranks (strong scaling)",
            "value": flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms, "steps": steps,
            "batches_per_rank": nb, "plan": mb.kernels.plan(As[0][s:e], Bs[0][s:e]),
            "api": "metalblas_b200.shard.sharded_bmm"}
     if world > 1:
-        gms = timed(lambda i: shard.sharded_bmm(As[i], Bs[i], gather=True, chunks=4))
+        gms = _timed(lambda i: shard.sharded_bmm(As[i % 2], Bs[i % 2], gather=True), steps, world, device)
+        Cg = shard.sharded_bmm(As[0], Bs[0], gather=True)
+        # one batch from every rank's slab, checked against the oracle on rank 0;
+        # every rank's copy of the sample must hold the same bytes
+        pick = [shard.shard_range(Bt, world, r)[0] for r in range(world)]
+        chk = _check_batches(Cg, As[0], Bs[0], pick, world, device, rank)
         out["gathered"] = {"value": flops / (gms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": gms,
-                           "collective": "NCCL all_gather_into_tensor in 4 rounds straight into the output, "
-                                         "each overlapping the next round's products"}
+                           "collective": "fused: each rank's bmm epilogue stores its slab into every rank's "
+                                         "[256,1024,1024] output over NVLink (mb_gemm_peer), then one barrier",
+                           "check": chk}
+        nms = _timed(lambda i: shard.sharded_bmm(As[i % 2], Bs[i % 2], gather=True, chunks=4, fused=False),
+                     steps, world, device)
+        out["gathered_nccl"] = {"value": flops / (nms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": nms,
+                                "collective": "NCCL all_gather_into_tensor in 4 rounds, each overlapping the "
+                                              "next round's products (unfused)"}
     return out
+
+
+def run_large_nshard(args, rank, world, device):
+    """BASELINE config 5, large GEMM: bf16 16384 x 16384 x 16384 (N(0,1), seed 6)
+    with N sharded over the ranks (strong scaling: rank r computes the
+    16384 x 16384/N column block).  "value" keeps the output sharded;
+    "gathered" returns the row-major 16384 x 16384 C on every rank each step,
+    the gather fused into the product's epilogue.  At N = 1 both are the plain
+    GEMM.  Inputs 1 GiB > L2."""
+    import metalblas_b200 as mb
+    from metalblas_b200 import shard
+    Mx = Nx = Kx = 16384
+    g = torch.Generator(device=device).manual_seed(6)
+    A = torch.randn(Mx, Kx, generator=g, device=device, dtype=torch.bfloat16)
+    B = torch.randn(Kx, Nx, generator=g, device=device, dtype=torch.bfloat16)
+    s, e = shard.shard_range(Nx, world, rank)
+    Bb = B[:, s:e]                       # this rank's column block, read in place (ldb = 16384)
+    C = torch.empty(Mx, e - s, dtype=torch.bfloat16, device=device)
+    steps = max(3, min(args.steps, 20))
+    flops = 2.0 * Mx * Nx * Kx
+    ms = _timed(lambda i: mb.matmul(A, Bb, out=C), steps, world, device)
+    out = {"workload": "bf16 GEMM 16384^3, N sharded over ranks (strong scaling)",
+           "value": flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms, "steps": steps,
+           "columns_per_rank": e - s, "plan": mb.kernels.plan(A, Bb), "l2": "inputs 1 GiB > L2"}
+    if world == 1:
+        Cg, gms = C, ms
+    else:
+        gms = _timed(lambda i: shard.sharded_matmul_n(A, Bb, Nx, gather=True), steps, world, device)
+        Cg = shard.sharded_matmul_n(A, Bb, Nx, gather=True)
+    chk = _check_gathered(Cg, A, lambda cols: B[:, cols], torch.bfloat16, world, device, rank,
+                          row_step=1024, col_step=8)
+    out["gathered"] = {"value": flops / (gms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": gms,
+                       "layout": "row-major C [16384, 16384] on every rank",
+                       "collective": ("fused: tcgen05 epilogue stores each tile into every rank's C over "
+                                      "NVLink (mb_gemm_peer), then one barrier") if world > 1 else "none (1 GPU)",
+                       "check": chk}
+    del A, B, C
+    return out
+
+
+def run_skinny(args, rank, world, device):
+    """BASELINE config 5, skinny: bf16 128 x 8192 x 65536 (N(0,1), seed 6),
+    HBM-bound (reads B, 1 GiB, once).  Two shardings over the ranks:
+    "n_sharded" — N split, the 128 x 8192 output gathered to every rank by the
+    fused epilogue (the north star's "N sharded ... output gathered");
+    "k_sharded" — K split, each rank's 128 x 8192 partial summed in fp32 by one
+    NCCL all-reduce (the reference's split-K, float_dispatch.py:183-219, across
+    GPUs).  At N = 1 both are the plain GEMM."""
+    import metalblas_b200 as mb
+    from metalblas_b200 import shard
+    Mx, Nx, Kx = 128, 8192, 65536
+    g = torch.Generator(device=device).manual_seed(6)
+    A = torch.randn(Mx, Kx, generator=g, device=device, dtype=torch.bfloat16)
+    B = torch.randn(Kx, Nx, generator=g, device=device, dtype=torch.bfloat16)
+    steps = max(5, min(args.steps, 50))
+    flops = 2.0 * Mx * Nx * Kx
+    byts = 2.0 * (Mx * Kx + Kx * Nx + Mx * Nx)
+    out = {"workload": "bf16 skinny GEMM 128x8192x65536", "unit": "GB/s", "steps": steps,
+           "bytes_per_step": byts, "l2": "B 1 GiB > L2"}
+    s, e = shard.shard_range(Nx, world, rank)
+    if world == 1:
+        C = torch.empty(Mx, Nx, dtype=torch.bfloat16, device=device)
+        ms = _timed(lambda i: mb.matmul(A, B, out=C), steps, world, device)
+        Cn = Ck = C
+        kms = ms
+        out["plan"] = mb.kernels.plan(A, B)
+    else:
+        Bb = B[:, s:e]
+        ms = _timed(lambda i: shard.sharded_matmul_n(A, Bb, Nx, gather=True), steps, world, device)
+        Cn = shard.sharded_matmul_n(A, Bb, Nx, gather=True).clone()
+        ks, ke = shard.shard_range(Kx, world, rank)
+        Ak, Bk = A[:, ks:ke], B[ks:ke]
+        kms = _timed(lambda i: shard.sharded_matmul_k(Ak, Bk), steps, world, device)
+        Ck = shard.sharded_matmul_k(Ak, Bk)
+        out["plan"] = mb.kernels.plan(A, Bb)
+        out["plan_k"] = mb.kernels.plan(Ak, Bk)
+    cn = _check_gathered(Cn, A, lambda cols: B[:, cols], torch.bfloat16, world, device, rank, row_step=8,
+                         col_step=16)
+    ck = _check_gathered(Ck, A, lambda cols: B[:, cols], torch.bfloat16, world, device, rank, row_step=8,
+                         col_step=16)
+    out["n_sharded"] = {"value": byts / (ms * 1e-3) / 1e9, "ms_per_step": ms,
+                        "tflops": flops / (ms * 1e-3) / 1e12,
+                        "collective": "fused gather (mb_gemm_peer) + barrier" if world > 1 else "none (1 GPU)",
+                        "check": cn}
+    out["k_sharded"] = {"value": byts / (kms * 1e-3) / 1e9, "ms_per_step": kms,
+                        "tflops": flops / (kms * 1e-3) / 1e12,
+                        "collective": "NCCL all_reduce of fp32 partials" if world > 1 else "none (1 GPU)",
+                        "check": ck}
+    del A, B
+    return out
+
+
+def _timed(fn, steps, world, device, warm=3):
+    """Device time per call of fn(i): warm-up calls, then `steps` calls between
+    CUDA events on the current stream, barrier + synchronize on both sides, max
+    over ranks."""
+    stream = torch.cuda.current_stream(device)
+    for i in range(warm):
+        fn(i)
+    _barrier(world, device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(steps):
+        fn(i)
+    e1.record(stream)
+    e1.synchronize()
+    _barrier(world, device)
+    return _max_over_ranks(e0.elapsed_time(e1) / steps, world, device)
+
+
+def _rank_consistency(sample, world, device):
+    """Every rank's copy of a gathered sample holds the same values: a weighted
+    float64 checksum, all-gathered and compared."""
+    if world == 1:
+        return True
+    import torch.distributed as dist
+    x = sample.double()
+    wts = torch.arange(1, x.numel() + 1, dtype=torch.float64, device=x.device).reshape(x.shape)
+    cs = torch.stack([x.sum(), (x * wts).sum()]).reshape(1, 2)
+    allc = torch.empty(world, 2, dtype=torch.float64, device=device)
+    dist.all_gather_into_tensor(allc, cs)
+    return bool(torch.equal(allc, allc[:1].expand(world, 2)))
+
+
+def _check_gathered(C, A, b_cols, dt, world, device, rank, row_step, col_step):
+    """Oracle check (rank 0) of a row x column sample of a gathered product
+    C = A @ B, the sample spanning every rank's block; plus the cross-rank
+    consistency of the same sample.  b_cols(cols) returns B[:, cols]."""
+    from oracle import oracle as orc
+    rows = torch.arange(0, C.shape[0], row_step, device=C.device)
+    cols = torch.arange(0, C.shape[1], col_step, device=C.device)
+    sample = C[rows][:, cols]
+    same = _rank_consistency(sample, world, device)
+    res = {"rows_checked": int(len(rows)), "cols_checked": int(len(cols)), "ranks_identical": same}
+    if rank == 0:
+        name = {torch.bfloat16: "bfloat16", torch.float16: "float16", torch.int8: "int8"}[dt]
+        a_s = A[rows.to(A.device)].cpu() if A.is_cuda else A[rows.cpu()]
+        b_s = b_cols(cols.to(A.device) if A.is_cuda else cols.cpu())
+        b_s = b_s.cpu()
+        as_np = a_s.float().numpy() if dt is not torch.int8 else a_s.numpy()
+        bs_np = b_s.float().numpy() if dt is not torch.int8 else b_s.numpy()
+        got = sample.cpu()
+        ok, err = orc.check(got.float().numpy() if dt is not torch.int8 else got.numpy(),
+                            orc.product(as_np, bs_np, name), name)
+        res.update({"ok": bool(ok) and same, "rel_frobenius_or_mismatch": float(err)})
+    return res
+
+
+def _check_batches(C, A, B, pick, world, device, rank):
+    """Oracle check (rank 0) of whole batches `pick` of a gathered bmm, plus
+    cross-rank consistency of those batches."""
+    from oracle import oracle as orc
+    idx = torch.tensor(pick, device=C.device)
+    sample = C[idx]
+    same = _rank_consistency(sample, world, device)
+    res = {"batches_checked": list(map(int, pick)), "ranks_identical": same}
+    if rank == 0:
+        ref = orc.product(A[idx].float().cpu().numpy(), B[idx].float().cpu().numpy(), "bfloat16")
+        ok, err = orc.check(sample.float().cpu().numpy(), ref, "bfloat16")
+        res.update({"ok": bool(ok) and same, "rel_frobenius_or_mismatch": float(err)})
+    return res
+
+
+def _weak_b_cols(w, cols, world):
+    """Columns `cols` of the weak-scaling run's global B [K, N * world] (host)."""
+    return _global_inputs(w, world)[1][:, cols.cpu()]
 
 
 def run_reference(args, w, rank, world):
@@ -392,6 +564,9 @@ def run_reference(args, w, rank, world):
     a bounded row sample of the same product per step."""
     from oracle import cpu_baseline as cb
     M, N, K, dt = w["M"], w["N"], w["K"], w["dtype"]
+    # torch.distributed.run sets OMP_NUM_THREADS=1 for every rank; the
+    # reference's CPU path runs on rank 0 alone, with every host core
+    torch.set_num_threads(os.cpu_count() or 1)
     a, b = _inputs(w, 0, 1)
     budget = 90.0  # seconds for the whole run
     per_step = budget / max(1, args.steps + args.warmup)
@@ -892,6 +1067,8 @@ def main():
     ap.add_argument("--workload", default="bf16_gemm_4096", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-bmm", action="store_true", help="skip the batch-sharded bmm measurement")
+    ap.add_argument("--no-multi", action="store_true",
+                    help="skip the 16384^3 N-sharded and skinny 128x8192x65536 measurements")
     ap.add_argument("--suite", action="store_true",
                     help="measure every BASELINE config on one GPU, one JSON line per case")
     ap.add_argument("--configs", default="C1,C2,C3,C4,C5")
@@ -925,6 +1102,9 @@ def main():
     finally:
         if world > 1:
             import torch.distributed as dist
+            from metalblas_b200 import peer
+            torch.cuda.synchronize(device)
+            peer.release_arenas()
             dist.destroy_process_group()
 
 

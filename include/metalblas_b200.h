@@ -153,6 +153,45 @@ int mb_gemm(const mb_gemm_desc *d, void *stream);
 #define MB_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
 int mb_gemm_noalloc(const mb_gemm_desc *d, void *stream);
 
+/* ---------------------------------------------------------------------------
+ * Multi-GPU: the product fused with its output gather over NVLink.
+ *
+ * The reference is single-device; its sharded counterpart here splits a large
+ * GEMM along N (or a bmm along the batch) over the GPUs of one node, and the
+ * north star's "output gathered over NVLink" step is folded into the GEMM's
+ * epilogue: every finished output tile is stored into this GPU's C (TMA store)
+ * AND into each peer GPU's copy of C at the same element offset (plain 16-byte
+ * st.global over NVLink, 64-byte row runs per warp store).  Loads and tensor
+ * maps only ever address this GPU's memory; nothing multicasts.
+ *
+ * mb_gemm_peer computes what mb_gemm computes for `d` and also writes every
+ * element of C, at the same offset from peers->C[i], for i < peers->count.
+ * peers->C[i] must be device addresses valid in the calling process (a peer
+ * buffer mapped with mb_ipc_open) laid out with d's C strides.  Runs on the
+ * tensor-core plan only (bf16 / fp16 / int8 / uint8 operands TMA can address):
+ * other plans return MB_ERR_UNSUPPORTED.  The peers see complete results only
+ * after every GPU's launch has finished: order a cross-GPU barrier (a NCCL
+ * all-reduce of one word on the same stream serves) between this call and any
+ * reader, and do not start a call that overwrites a peer's C while that peer
+ * may still read it (alternate two buffers, or barrier before the call). */
+#define MB_MAX_PEERS 7
+typedef struct mb_peer_targets {
+    int32_t count;                 /* peers that receive the output (0..MB_MAX_PEERS) */
+    void *C[MB_MAX_PEERS];         /* each peer's copy of C, same strides as desc->C */
+} mb_peer_targets;
+int mb_gemm_peer(const mb_gemm_desc *d, const mb_peer_targets *peers, void *stream);
+
+/* CUDA IPC plumbing for the peer buffers (one process per GPU).
+ * mb_ipc_get_handle: the IPC handle (MB_IPC_HANDLE_BYTES opaque bytes) of the
+ * device allocation that contains `ptr`, and ptr's byte offset within it.
+ * mb_ipc_open: map another process's allocation into this one (peer access
+ * enabled on first use); *base receives the mapped base address (add the
+ * owner's offset).  mb_ipc_close: unmap a base returned by mb_ipc_open. */
+#define MB_IPC_HANDLE_BYTES 64
+int mb_ipc_get_handle(const void *ptr, void *handle, int64_t *offset);
+int mb_ipc_open(const void *handle, void **base);
+int mb_ipc_close(void *base);
+
 /* Bytes of workspace mb_gemm needs for this descriptor's plan (0 if none).
  * Replaces the split-K partial pool of metalblas/float_dispatch.py:183-192. */
 int64_t mb_gemm_workspace_size(const mb_gemm_desc *d);

@@ -38,7 +38,10 @@ EXPORTS = (
     "mb_debug_wait_timeout", "mb_abi_version", "mb_built_sm", "mb_gemv",
     "mb_autotune_record", "mb_autotune_lookup", "mb_autotune_cache_load", "mb_autotune_cache_save",
     "mb_autotune_cache_clear", "mb_autotune_cache_size", "mb_peak_probe",
+    "mb_gemm_peer", "mb_ipc_get_handle", "mb_ipc_open", "mb_ipc_close",
 )
+
+MB_MAX_PEERS = 7
 
 
 class GemmDesc(ctypes.Structure):
@@ -63,6 +66,24 @@ class GemmDesc(ctypes.Structure):
         ("cta_pair", ctypes.c_int32),
         ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_int64),
     ]
+
+
+class PeerTargets(ctypes.Structure):
+    """Mirror of ``mb_peer_targets``."""
+
+    _fields_ = [("count", ctypes.c_int32), ("C", ctypes.c_void_p * MB_MAX_PEERS)]
+
+
+def peer_targets(addrs) -> PeerTargets:
+    """An mb_peer_targets holding the given device addresses."""
+    addrs = list(addrs)
+    if len(addrs) > MB_MAX_PEERS:
+        raise ValueError(f"at most {MB_MAX_PEERS} peers, got {len(addrs)}")
+    t = PeerTargets()
+    t.count = len(addrs)
+    for i, a in enumerate(addrs):
+        t.C[i] = int(a)
+    return t
 
 
 class PlanOverride(ctypes.Structure):
@@ -129,6 +150,14 @@ def load():
         lib.mb_autotune_cache_size.restype = ctypes.c_int64
         lib.mb_peak_probe.argtypes = [I32, ctypes.POINTER(ctypes.c_double)]
         lib.mb_peak_probe.restype = ctypes.c_int
+        lib.mb_gemm_peer.argtypes = [P, ctypes.POINTER(PeerTargets), V]
+        lib.mb_gemm_peer.restype = ctypes.c_int
+        lib.mb_ipc_get_handle.argtypes = [V, V, ctypes.POINTER(I64)]
+        lib.mb_ipc_get_handle.restype = ctypes.c_int
+        lib.mb_ipc_open.argtypes = [V, ctypes.POINTER(V)]
+        lib.mb_ipc_open.restype = ctypes.c_int
+        lib.mb_ipc_close.argtypes = [V]
+        lib.mb_ipc_close.restype = ctypes.c_int
         _lib = lib
         return lib
 

@@ -1201,8 +1201,9 @@ int encode_map(CUtensorMap *m, int dt, const void *base, int64_t inner, int64_t 
   return MB_OK;
 }
 
-template <class T, int BN, int PAIR, class TO = T>
-int launch_tc_bn(const Op &o, const Plan &pl, const EpiScalars &e, void *ws, int sms, cudaStream_t st) {
+template <class T, int BN, int PAIR, class TO = T, bool PEER = false>
+int launch_tc_bn(const Op &o, const Plan &pl, const EpiScalars &e, void *ws, int sms, cudaStream_t st,
+                 const mb_peer_targets *peers = nullptr) {
   using C_ = tc::Cfg<BN, sizeof(T), PAIR>;
   constexpr int ESZ = sizeof(T);
   constexpr int OSZ = sizeof(TO);
@@ -1257,7 +1258,11 @@ int launch_tc_bn(const Op &o, const Plan &pl, const EpiScalars &e, void *ws, int
     p.ws = reinterpret_cast<char *>(ws) + kTicketBytes;
   }
   p.timeout_ns = wait_timeout_ns();
-  auto kern = tc::tc_gemm_kernel<T, BN, PAIR, TO>;
+  if constexpr (PEER) {
+    p.npeers = peers->count;
+    for (int i = 0; i < peers->count; ++i) p.peer_C[i] = peers->C[i];
+  }
+  auto kern = tc::tc_gemm_kernel<T, BN, PAIR, TO, PEER>;
   static int attr_done[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1292,9 +1297,29 @@ int launch_tc_bn(const Op &o, const Plan &pl, const EpiScalars &e, void *ws, int
   return cuda_check(cudaGetLastError(), "tc_gemm launch");
 }
 
-template <class T>
-int launch_tc(const Op &o, const Plan &pl, const EpiScalars &e, void *ws, int sms, cudaStream_t st) {
-  if constexpr (std::is_same_v<T, float>) {
+template <class T, bool PEER = false>
+int launch_tc(const Op &o, const Plan &pl, const EpiScalars &e, void *ws, int sms, cudaStream_t st,
+              const mb_peer_targets *peers = nullptr) {
+  if constexpr (PEER && !std::is_same_v<T, float>) {
+    // the tile shapes the table picks for 16-bit and 8-bit products
+    if (pl.pair == 2) {
+      switch (pl.bn) {
+        case 128: return launch_tc_bn<T, 128, 2, T, true>(o, pl, e, ws, sms, st, peers);
+        case 256: return launch_tc_bn<T, 256, 2, T, true>(o, pl, e, ws, sms, st, peers);
+      }
+      return fail(MB_ERR_INVALID, "bad tile_n %d for a CTA pair", pl.bn);
+    }
+    switch (pl.bn) {
+      case 16: return launch_tc_bn<T, 16, 1, T, true>(o, pl, e, ws, sms, st, peers);
+      case 32: return launch_tc_bn<T, 32, 1, T, true>(o, pl, e, ws, sms, st, peers);
+      case 64: return launch_tc_bn<T, 64, 1, T, true>(o, pl, e, ws, sms, st, peers);
+      case 128: return launch_tc_bn<T, 128, 1, T, true>(o, pl, e, ws, sms, st, peers);
+      case 256: return launch_tc_bn<T, 256, 1, T, true>(o, pl, e, ws, sms, st, peers);
+    }
+    return fail(MB_ERR_INVALID, "bad tile_n %d", pl.bn);
+  } else if constexpr (PEER) {
+    return fail(MB_ERR_UNSUPPORTED, "peer replication is not built for fp32 (3xTF32) products");
+  } else if constexpr (std::is_same_v<T, float>) {
     // 3xTF32 keeps BN/2 fp32 running sums per epilogue thread: BN <= 128
     if (pl.pair == 2 && pl.bn == 128) return launch_tc_bn<T, 128, 2>(o, pl, e, ws, sms, st);
     switch (pl.pair == 1 ? pl.bn : 0) {
@@ -1700,6 +1725,70 @@ int mb_gemm(const mb_gemm_desc *d, void *stream) {
       default: return launch_simt<T>(o, e, st);
     }
   });
+}
+
+int mb_gemm_peer(const mb_gemm_desc *d, const mb_peer_targets *peers, void *stream) {
+  static_assert(MB_MAX_PEERS == tc::kMaxPeers, "peer table size");
+  if (!peers) return fail(MB_ERR_INVALID, "null peer table");
+  if (peers->count < 0 || peers->count > MB_MAX_PEERS)
+    return fail(MB_ERR_INVALID, "peer count %d outside 0..%d", peers->count, MB_MAX_PEERS);
+  for (int i = 0; i < peers->count; ++i)
+    if (!peers->C[i]) return fail(MB_ERR_INVALID, "null peer output %d", i);
+  Plan pl; Op o; int sms;
+  int rc = plan_for(d, pl, o, sms);
+  if (rc) return rc;
+  if (pl.kind == PK_EMPTY) return MB_OK;
+  if (pl.kind != PK_TC)
+    return fail(MB_ERR_UNSUPPORTED, "peer replication runs on the tensor-core plan only (bf16/fp16/int8/uint8 "
+                                    "operands TMA can address); this product plans as kind %d", pl.kind);
+  if (pl.ws_bytes > 0 && (d->workspace == nullptr || d->workspace_bytes < pl.ws_bytes))
+    return fail(MB_ERR_WORKSPACE, "workspace of %lld bytes required", (long long)pl.ws_bytes);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const EpiScalars e = make_epi(d);
+  return by_dtype(d->dtype, [&](auto *tag) -> int {
+    using T = std::remove_pointer_t<decltype(tag)>;
+    if constexpr (IsTc<T>::v)
+      return launch_tc<T, true>(pl.swap ? swapped(o) : o, pl, e, d->workspace, sms, st, peers);
+    else return fail(MB_ERR_UNSUPPORTED, "tensor-core path for non-TC dtype");
+  });
+}
+
+int mb_ipc_get_handle(const void *ptr, void *handle, int64_t *offset) {
+  static_assert(sizeof(cudaIpcMemHandle_t) == MB_IPC_HANDLE_BYTES, "IPC handle size");
+  if (!ptr || !handle || !offset) return fail(MB_ERR_INVALID, "null argument");
+  typedef CUresult (*AddrRangeFn)(CUdeviceptr *, size_t *, CUdeviceptr);
+  static AddrRangeFn range_fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      range_fn = reinterpret_cast<AddrRangeFn>(f);
+  });
+  if (!range_fn) return fail(MB_ERR_LAUNCH, "cuMemGetAddressRange unavailable");
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range_fn(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS)
+    return fail(MB_ERR_INVALID, "pointer is not a device allocation");
+  cudaIpcMemHandle_t h;
+  int rc = cuda_check(cudaIpcGetMemHandle(&h, reinterpret_cast<void *>(base)), "cudaIpcGetMemHandle");
+  if (rc) return rc;
+  memcpy(handle, &h, sizeof(h));
+  *offset = (int64_t)(reinterpret_cast<CUdeviceptr>(ptr) - base);
+  return MB_OK;
+}
+
+int mb_ipc_open(const void *handle, void **base) {
+  if (!handle || !base) return fail(MB_ERR_INVALID, "null argument");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  return cuda_check(cudaIpcOpenMemHandle(base, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+}
+
+int mb_ipc_close(void *base) {
+  if (!base) return fail(MB_ERR_INVALID, "null argument");
+  return cuda_check(cudaIpcCloseMemHandle(base), "cudaIpcCloseMemHandle");
 }
 
 int mb_gemv(int32_t dtype, int32_t trans, int64_t rows, int64_t cols, const void *W, int64_t ldw, const void *x,

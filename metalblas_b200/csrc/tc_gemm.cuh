@@ -58,6 +58,7 @@ namespace mb {
 namespace tc {
 
 constexpr int BM = 128;                 // UMMA M (cta_group::1)
+constexpr int kMaxPeers = 7;            // peer copies of C a replicating kernel writes (8 GPUs per node)
 constexpr int NUM_EPI_WARPS = 8;
 constexpr int NUM_THREADS = 64 + 32 * NUM_EPI_WARPS;
 constexpr int SMEM_LIMIT = 232448;      // max dynamic shared memory per CTA on sm_100
@@ -91,6 +92,12 @@ struct TcParams {
   int sk;                // tail tiles partitioned stream-K (splits = partial slots per tile)
   long long sk_iters;    // tail tiles * kb_total: the K-block iterations shared out
   unsigned long long timeout_ns;
+  // Peer replication (kernels instantiated with PEER = true): every output
+  // element is also stored, with plain st.global over NVLink, at the same
+  // element offset from each peer_C[i] (another GPU's copy of C, mapped into
+  // this process).  Loads and tensor maps only ever touch this GPU's memory.
+  int npeers;
+  void *peer_C[kMaxPeers];
 };
 
 template <int BN, int ESZ, int PAIR = 1>
@@ -623,11 +630,29 @@ __device__ __forceinline__ void epi_real(const TcParams &p, int b, int m, int n0
   }
 }
 
-// Direct stores of NC (<= 32) consecutive columns of one output row (r is
-// consumed: the epilogue is applied to it in place).
+// Write NC consecutive output values of row m (columns n0..) to a copy of C at
+// `base` (C's strides): 16-byte stores when the row run is aligned and whole,
+// else one store per element.
 template <class T, int NC>
+__device__ __forceinline__ void put_row_chunk(const TcParams &p, T *base, int b, int m, int n0, const T (&out)[NC]) {
+  T *C = base + (int64_t)b * p.sC;
+  constexpr int PER16 = 16 / sizeof(T);
+  if (NC % PER16 == 0 && p.c_vec && n0 + NC <= p.N) {
+    uint4 *dst = reinterpret_cast<uint4 *>(C + (int64_t)m * p.c_rs + n0);
+#pragma unroll
+    for (int v = 0; v < NC / PER16; ++v) dst[v] = *reinterpret_cast<const uint4 *>(&out[v * PER16]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < NC; ++j)
+      if (n0 + j < p.N) C[(int64_t)m * p.c_rs + (int64_t)(n0 + j) * p.c_cs] = out[j];
+  }
+}
+
+// Direct stores of NC (<= 32) consecutive columns of one output row (r is
+// consumed: the epilogue is applied to it in place).  PEER: the same values
+// also go to every peer copy of C.
+template <class T, int NC, bool PEER = false>
 __device__ __forceinline__ void store_row_chunk(const TcParams &p, int b, int m, int n0, uint32_t (&r)[32]) {
-  T *C = (T *)p.C + (int64_t)b * p.sC;
   T out[NC];
   bool cplx = false;
   if constexpr (std::is_same_v<T, __half>) cplx = p.epi.cplx != 0;
@@ -650,15 +675,51 @@ __device__ __forceinline__ void store_row_chunk(const TcParams &p, int b, int m,
   } else {
     epi_values<T, NC>(p, b, m, n0, r, out);
   }
-  constexpr int PER16 = 16 / sizeof(T);
-  if (NC % PER16 == 0 && p.c_vec && n0 + NC <= p.N) {
-    uint4 *dst = reinterpret_cast<uint4 *>(C + (int64_t)m * p.c_rs + n0);
+  put_row_chunk<T, NC>(p, (T *)p.C, b, m, n0, out);
+  if constexpr (PEER) {
+#pragma unroll 1
+    for (int i = 0; i < p.npeers; ++i) put_row_chunk<T, NC>(p, (T *)p.peer_C[i], b, m, n0, out);
+  }
+}
+
+// Peer copies of one staged 32-row x 64-byte output box (the SWIZZLE_64B
+// staging layout of the TMA-store epilogue: 16-byte chunk c of row r at chunk
+// c ^ ((r >> 1) & 3)).  Lane l moves chunk l & 3 of rows l / 4, l / 4 + 8, ...,
+// so each warp-wide store writes eight whole 64-byte row runs.  Rows past M and
+// columns past N are skipped, as the TMA store clips them.
+template <class T>
+__device__ __forceinline__ void peer_store_box(const TcParams &p, uint32_t stg, int lane, int b, int row0, int col0) {
+  constexpr int EPC = 16 / (int)sizeof(T);   // elements per 16-byte chunk
+  const int rr = lane >> 2, ch = lane & 3;
+  const int n = col0 + ch * EPC;
+  if (n >= p.N) return;
+  uint4 v[4];
 #pragma unroll
-    for (int v = 0; v < NC / PER16; ++v) dst[v] = *reinterpret_cast<const uint4 *>(&out[v * PER16]);
-  } else {
+  for (int i = 0; i < 4; ++i) {
+    const int r = i * 8 + rr;
+    const uint32_t addr = stg + (uint32_t)(r * STAGING_ROW) + ((uint32_t)(ch ^ ((r >> 1) & 3)) << 4);
+    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v[i].x), "=r"(v[i].y), "=r"(v[i].z), "=r"(v[i].w)
+                 : "r"(addr));
+  }
+  const bool whole = n + EPC <= p.N;
+#pragma unroll 1
+  for (int pi = 0; pi < p.npeers; ++pi) {
+    T *C = (T *)p.peer_C[pi] + (int64_t)b * p.sC;
 #pragma unroll
-    for (int j = 0; j < NC; ++j)
-      if (n0 + j < p.N) C[(int64_t)m * p.c_rs + (int64_t)(n0 + j) * p.c_cs] = out[j];
+    for (int i = 0; i < 4; ++i) {
+      const int m = row0 + i * 8 + rr;
+      if (m >= p.M) break;
+      T *dst = C + (int64_t)m * p.c_rs + n;
+      if (whole) {
+        *reinterpret_cast<uint4 *>(dst) = v[i];
+      } else {
+        const T *e = reinterpret_cast<const T *>(&v[i]);
+#pragma unroll
+        for (int j = 0; j < EPC; ++j)
+          if (n + j < p.N) dst[j] = e[j];
+      }
+    }
   }
 }
 
@@ -713,7 +774,7 @@ __device__ __forceinline__ void pack32(const TcParams &p, int b, int m, int n0, 
 // Split-K / stream-K epilogue after a warp published its partial: take a ticket
 // for (tail tile, warp); the warp that draws the last one sums every partial of
 // its 32 rows x wcols columns in K order and stores the result.
-template <class T, int BN, int RCH>
+template <class T, int BN, int RCH, bool PEER = false>
 __device__ __forceinline__ void split_finish(const TcParams &p, const Unit &w, int ew, int lane, int m, int nbase,
                                              int wcols) {
   const int64_t slot_words = (int64_t)BM * BN;
@@ -767,7 +828,7 @@ __device__ __forceinline__ void split_finish(const TcParams &p, const Unit &w, i
         }
       }
       const int n0 = nbase + c;
-      if (m < p.M && n0 < p.N) store_row_chunk<T, RCH>(p, w.b, m, n0, r);
+      if (m < p.M && n0 < p.N) store_row_chunk<T, RCH, PEER>(p, w.b, m, n0, r);
     }
     if (lane == 0) *ticket = 0u;
   }
@@ -776,7 +837,8 @@ __device__ __forceinline__ void split_finish(const TcParams &p, const Unit &w, i
 // ---------------------------------------------------------------------------
 // TO: the output element type.  It is T except for the integer limb products,
 // whose u8 x u8 GEMMs write 16/32/64-bit integers (direct stores only).
-template <class T, int BN, int PAIR = 1, class TO = T>
+// PEER: also write every output element to the peer copies of C (TcParams::peer_C).
+template <class T, int BN, int PAIR = 1, class TO = T, bool PEER = false>
 __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_constant__ TcParams p) {
   constexpr int ESZ = sizeof(T);
   using C_ = Cfg<BN, ESZ, PAIR>;
@@ -1025,7 +1087,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
 #pragma unroll
               for (int j = 0; j < RCH; ++j) r[j] = __float_as_uint(run[c + j]);
               const int n0 = nbase + c;
-              if (m < p.M && n0 < p.N) store_row_chunk<T, RCH>(p, w.b, m, n0, r);
+              if (m < p.M && n0 < p.N) store_row_chunk<T, RCH, PEER>(p, w.b, m, n0, r);
             }
           }
         } else {
@@ -1037,7 +1099,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
             if (c < wcols)
               __stcg(part + (c >> 2) * 32, make_uint4(__float_as_uint(run[c]), __float_as_uint(run[c + 1]),
                                                       __float_as_uint(run[c + 2]), __float_as_uint(run[c + 3])));
-          split_finish<T, BN, RCH>(p, w, ew, lane, m, nbase, wcols);
+          split_finish<T, BN, RCH, PEER>(p, w, ew, lane, m, nbase, wcols);
         }
         continue;
       }
@@ -1101,6 +1163,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
                   tma_store_3d(&p.tmC, stg, n0 - (SUBS - 1) * 32, m0 + q * 32, w.b);
                   bulk_commit();
                 }
+                if constexpr (PEER) peer_store_box<T>(p, stg, lane, w.b, m0 + q * 32, n0 - (SUBS - 1) * 32);
                 sbuf ^= 1;
               }
             }
@@ -1114,7 +1177,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
           tmem_ld<RCHO>(tbase + c, r);
           tmem_wait_ld();
           const int n0 = nbase + c;
-          if (m < p.M && n0 < p.N) store_row_chunk<TO, RCHO>(p, w.b, m, n0, r);
+          if (m < p.M && n0 < p.N) store_row_chunk<TO, RCHO, PEER>(p, w.b, m, n0, r);
         }
         tc_fence_before();
         __syncwarp();
@@ -1139,11 +1202,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
         tc_fence_before();
         __syncwarp();
         if (lane == 0) release_tmem(abuf);
-        split_finish<TO, BN, RCHO>(p, w, ew, lane, m, nbase, wcols);
+        split_finish<TO, BN, RCHO, PEER>(p, w, ew, lane, m, nbase, wcols);
       }
       if (++abuf == 2) { abuf = 0; aphase ^= 1u; }
     }
     if (lane == 0) bulk_wait0();  // every TMA store of this warp has completed
+    // peer stores are performed system-wide before the CTA retires
+    if constexpr (PEER) __threadfence_system();
     __syncwarp();
   }
 

@@ -13,6 +13,12 @@ CUDA tensors and every product runs through one C-ABI call, ``mb_gemm``
   non-row-major ``out`` through a temporary, metalblas/dispatch.py:106-114);
 * baddbmm is fused for every dtype (the reference computes complex baddbmm with
   torch arithmetic, metalblas/complex_dispatch.py:132-144).
+
+The thin public wrappers keep the reference's interface on purpose: their
+signatures and assertion messages, the vector-promotion prologue of
+``_matmul_nd``, ``addbmm``'s empty-batch branch and the ``dot`` / ``vdot`` /
+``outer`` / ``mv`` bodies follow metalblas/dispatch.py of Isalia20/metalBLAS
+(MIT License, Copyright (c) 2026 Irakli Salia).
 """
 from __future__ import annotations
 
@@ -136,19 +142,24 @@ def _stream_of(dev) -> int:
 
 
 def _launch(A, B, C, M, N, K, batch, a3, b3, c3, *, epilogue=None, backend=_lib.MB_BACKEND_AUTO,
-            tile_n=0, split_k=0, swap_ab=0, cta_pair=0, stream_k=0, autotune=True):
+            tile_n=0, split_k=0, swap_ab=0, cta_pair=0, stream_k=0, autotune=True, peers=None):
     """Fill an mb_gemm_desc and call mb_gemm on the current stream of C's device.
 
     a3/b3/c3 are (row stride, col stride, batch stride) in elements.
     epilogue: (bias, (rs, cs, bs), beta, alpha, beta_nz, alpha_nz) or None.
+    peers: device addresses of other GPUs' copies of C (same strides): the call
+    goes to mb_gemm_peer, which also stores every output element there.
     """
     dev = C.device
     if torch.cuda.current_device() != dev.index:
         with torch.cuda.device(dev):
             return _launch(A, B, C, M, N, K, batch, a3, b3, c3, epilogue=epilogue, backend=backend,
                            tile_n=tile_n, split_k=split_k, swap_ab=swap_ab, cta_pair=cta_pair, stream_k=stream_k,
-                           autotune=autotune)
+                           autotune=autotune, peers=peers)
     stream = _stream_of(dev)
+    if peers is not None:
+        return _launch_peer(A, B, C, M, N, K, batch, a3, b3, c3, epilogue, backend, tile_n, split_k, peers,
+                            dev, stream)
     pa = A.data_ptr() if A is not None else 0
     pb = B.data_ptr() if B is not None else 0
     pc = C.data_ptr()
@@ -222,22 +233,83 @@ def _launch(A, B, C, M, N, K, batch, a3, b3, c3, *, epilogue=None, backend=_lib.
     return C
 
 
+def _fill_desc(A, B, C, M, N, K, batch, a3, b3, c3, epilogue, backend, tile_n, split_k):
+    d = _lib.new_desc()
+    d.dtype = _lib.DTYPE_CODE[C.dtype]
+    d.backend = backend
+    d.M, d.N, d.K, d.batch = int(M), int(N), int(K), int(batch)
+    d.A = A.data_ptr() if A is not None else None
+    d.B = B.data_ptr() if B is not None else None
+    d.C = C.data_ptr()
+    d.a_rs, d.a_cs, d.sA = a3
+    d.b_rs, d.b_cs, d.sB = b3
+    d.c_rs, d.c_cs, d.sC = c3
+    d.conj_a, d.conj_b = int(A is not None and A.is_conj()), int(B is not None and B.is_conj())
+    if epilogue is not None:
+        bias, bstr, beta, alpha, bnz, anz = epilogue
+        d.epilogue = 1
+        d.alpha_nz, d.beta_nz = int(bool(anz)), int(bool(bnz))
+        d.bias = bias.data_ptr() if bnz else None
+        d.bias_rs, d.bias_cs, d.bias_bs = bstr
+        if C.dtype in INTS:
+            d.ialpha, d.ibeta = _int64(alpha), _int64(beta)
+        else:
+            d.alpha_re, d.alpha_im = float(complex(alpha).real), float(complex(alpha).imag)
+            d.beta_re, d.beta_im = float(complex(beta).real), float(complex(beta).imag)
+    d.tile_n, d.split_k = int(tile_n), int(split_k)
+    return d
+
+
+def _launch_peer(A, B, C, M, N, K, batch, a3, b3, c3, epilogue, backend, tile_n, split_k, peers, dev, stream):
+    """mb_gemm_peer: the tensor-core product, every output tile also stored into
+    the peers' copies of C (the fused output gather of shard.py).  The tile
+    table plans it (the autotuner's timing runs would write into the peers)."""
+    lib = _lib.load()
+    d = _fill_desc(A, B, C, M, N, K, batch, a3, b3, c3, epilogue, backend, tile_n, split_k)
+    nbytes = int(lib.mb_gemm_workspace_size(ctypes.byref(d)))
+    if nbytes > 0:
+        ws = _workspace(dev, stream, nbytes)
+        d.workspace, d.workspace_bytes = ws.data_ptr(), ws.numel()
+    targets = _lib.peer_targets(peers)
+    _lib.raise_for(lib.mb_gemm_peer(ctypes.byref(d), ctypes.byref(targets), ctypes.c_void_p(stream)),
+                   "mb_gemm_peer")
+    return C
+
+
+_TC_TILE_N = (16, 32, 64, 128, 256)
+
+
 def _parse_tile(backend, tile):
-    """tile= override.  For "mpp_tensor" it is (BM, BN[, split_k]) of the tcgen05
-    kernel: BM must be 128 (the UMMA M), BN one of 16/32/64/128/256.  The
-    CUDA-core tiles of "simd"/"mpp" are fixed; their tuples are checked for
+    """tile= override, returned as (tile_n, split_k) of the tcgen05 kernel.
+
+    For "mpp_tensor":
+      * the reference's own tuples ``(BM, BN, NSG[, ...])`` (three or more
+        entries, metalblas/float_dispatch.py:613-655 picks them, :826-831
+        takes ``tile[:3]``) are accepted and mapped to the nearest sm_100a
+        tile: the smallest N-tile in 16/32/64/128/256 that covers BN (256 for
+        larger BN).  BM and NSG describe Apple threadgroups and simdgroups; the
+        B200 tile is always 128 rows (256 on a CTA pair) with fixed warp roles,
+        so they are checked and otherwise unused.  A fourth entry, if given,
+        is this build's split-K override.
+      * ``(128, BN)`` names the sm_100a tile directly (BN one of the N-tiles).
+    The CUDA-core tiles of "simd"/"mpp" are fixed; their tuples are checked for
     shape only, as the reference does (metalblas/float_dispatch.py:826-844)."""
     if tile is None:
         return 0, 0
     tile = tuple(int(x) for x in tile)
     if backend == "mpp_tensor":
-        assert len(tile) >= 2, "mpp_tensor tile is (BM, BN[, split_k])"
-        if tile[0] != 128 or tile[1] not in (16, 32, 64, 128, 256):
-            raise ValueError(f"mpp_tensor tile {tile}: BM must be 128 and BN one of 16, 32, 64, 128, 256")
-        split = tile[2] if len(tile) > 2 else 0
+        assert len(tile) >= 2, "mpp_tensor tile is (BM, BN, NSG) or (128, BN)"
+        if any(x <= 0 for x in tile[:3]):
+            raise ValueError(f"mpp_tensor tile {tile}: entries must be positive")
+        if len(tile) == 2:
+            if tile[0] != 128 or tile[1] not in _TC_TILE_N:
+                raise ValueError(f"mpp_tensor tile {tile}: (128, BN) needs BN one of 16, 32, 64, 128, 256")
+            return tile[1], 0
+        bn = next((n for n in _TC_TILE_N if n >= tile[1]), _TC_TILE_N[-1])
+        split = tile[3] if len(tile) > 3 else 0
         if split < 0:
             raise ValueError("split_k must be >= 0")
-        return tile[1], split
+        return bn, split
     assert len(tile) >= 3, "tile must have at least 3 entries"
     return 0, 0
 
@@ -251,7 +323,7 @@ def _complex_inputs(a, b):
     return a, b, dtype
 
 
-def _mm2d(a, b, out, epilogue=None, backend=None, tile=None):
+def _mm2d(a, b, out, epilogue=None, backend=None, tile=None, peers=None):
     if a.is_complex() or b.is_complex():
         a, b, _ = _complex_inputs(a, b)
     assert a.is_cuda and b.is_cuda, "metalblas_b200 expects cuda tensors"
@@ -280,7 +352,7 @@ def _mm2d(a, b, out, epilogue=None, backend=None, tile=None):
     return _launch(A, B, out, M, N, K, 1,
                    (A.stride(0), A.stride(1), 0), (B.stride(0), B.stride(1), 0),
                    (out.stride(0), out.stride(1), 0),
-                   epilogue=epilogue, backend=be, tile_n=tile_n, split_k=split_k)
+                   epilogue=epilogue, backend=be, tile_n=tile_n, split_k=split_k, peers=peers)
 
 
 def _flat3(t, size, rows, cols):
@@ -346,7 +418,8 @@ def matmul(a: torch.Tensor, b: torch.Tensor, *, backend: str | None = None,
     """Compute ``a @ b`` on a CUDA device (metalblas/dispatch.py:174-185).
 
     backend: None/"auto" (tile table + autotune cache), "gemv" (needs M==1 or
-    N==1), "mpp_tensor" (tcgen05 kernel, tile=(128, BN[, split_k])), "mpp"
+    N==1), "mpp_tensor" (tcgen05 kernel; tile= the reference's (BM, BN, NSG),
+    mapped to the nearest sm_100a tile, or (128, BN)), "mpp"
     (tcgen05 when the dtype and layout allow, else CUDA cores) or "simd"
     (CUDA-core FFMA/IMAD kernel).  swizzle_log is accepted for compatibility;
     rasterisation is done by the persistent tile scheduler.
@@ -387,7 +460,7 @@ def _bmm_shape(a, b, op):
     return Bb, M, N, K, a.dtype
 
 
-def _bmm(a, b, out, epilogue=None):
+def _bmm(a, b, out, epilogue=None, peers=None):
     Bb, M, N, K, dtype = _bmm_shape(a, b, "bmm")
     if dtype not in _lib.DTYPE_CODE:
         raise NotImplementedError(f"dtype {dtype} not supported")
@@ -402,7 +475,7 @@ def _bmm(a, b, out, epilogue=None):
     B = _plain(_matrix_view(b, K, N))
     return _launch(A, B, out, M, N, K, Bb,
                    (A.stride(1), A.stride(2), A.stride(0)), (B.stride(1), B.stride(2), B.stride(0)),
-                   (out.stride(1), out.stride(2), out.stride(0)), epilogue=epilogue)
+                   (out.stride(1), out.stride(2), out.stride(0)), epilogue=epilogue, peers=peers)
 
 
 def bmm(a: torch.Tensor, b: torch.Tensor, *, out: torch.Tensor | None = None) -> torch.Tensor:

@@ -2,8 +2,8 @@
 
 The reference has no CPU implementation of matmul (its kernels are Metal); its
 correctness oracle and the north star's stated CPU baseline are host-CPU
-``torch.matmul`` on the same inputs (tests/test_basic.py:37-42
-section 2).  ``bench.py`` times this function for its ``cpu_baseline`` object and
+``torch.matmul`` on the same inputs (tests/test_basic.py:37-42), timed on the
+host's own cores.  ``bench.py`` times this function for its ``cpu_baseline`` object and
 for ``--impl reference``; nothing in the product imports it.
 """
 from __future__ import annotations

@@ -4,7 +4,8 @@ The reference (Isalia20/metalBLAS) ships no fixtures; its correctness oracle is
 the set of CPU functions in its tests/test_basic.py: ``_product`` (:37-42),
 ``_wrap`` (:27-34) and ``_fused_ref`` (:110-121).  Its Metal kernels cannot run
 off macOS, but those oracle functions run on any CPU.  This script imports that
-file from a reference checkout (``--reference``, default /root/reference),
+file from a reference checkout (``--reference`` or the METALBLAS_REFERENCE
+environment variable, required),
 draws seeded CPU inputs with the reference's distributions (``_rand``,
 tests/test_basic.py:20-24: integers in [-4,4) or [0,4) for uint8, N(0,1)
 otherwise) plus full-range 8-bit integers (the BASELINE integer config, which
@@ -76,8 +77,11 @@ def to_np(t):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("METALBLAS_REFERENCE"),
+                    help="path of a metalBLAS checkout (or set METALBLAS_REFERENCE)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("--reference (or METALBLAS_REFERENCE) is required")
     ref = load_reference_oracle(args.reference)
     gen = Gen(1234)
     arrays, index = {}, []

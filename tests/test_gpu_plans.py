@@ -389,7 +389,7 @@ def test_integer_byte_planes_bit_exact(dtype):
 
 
 def test_nd_broadcast_batches_read_operands_in_place(monkeypatch):
-    """matmul over multi-dim broadcast batches: when the
+    """matmul over multi-dim broadcast batches (the reference reshapes, which copies): when the
     expanded batch dims cannot be flattened into one stride, the leading dim is
     walked instead of copying the operand; every launch reads the caller's own
     storage."""

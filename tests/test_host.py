@@ -58,10 +58,20 @@ def test_int64_scalar_wraps():
 
 def test_parse_tile():
     assert dispatch._parse_tile("mpp_tensor", (128, 256)) == (256, 0)
-    assert dispatch._parse_tile("mpp_tensor", (128, 64, 4)) == (64, 4)
+    # the reference's (BM, BN, NSG) tuples map to the nearest sm_100a N-tile
+    assert dispatch._parse_tile("mpp_tensor", (128, 64, 4)) == (64, 0)
+    assert dispatch._parse_tile("mpp_tensor", (64, 64, 2)) == (64, 0)
+    assert dispatch._parse_tile("mpp_tensor", (48, 128, 4)) == (128, 0)
+    assert dispatch._parse_tile("mpp_tensor", (32, 32, 4)) == (32, 0)
+    assert dispatch._parse_tile("mpp_tensor", (16, 96, 2)) == (128, 0)
+    assert dispatch._parse_tile("mpp_tensor", (128, 512, 8)) == (256, 0)
+    # a fourth entry is the split-K override
+    assert dispatch._parse_tile("mpp_tensor", (128, 64, 4, 3)) == (64, 3)
     assert dispatch._parse_tile(None, None) == (0, 0)
     with pytest.raises(ValueError):
-        dispatch._parse_tile("mpp_tensor", (64, 64, 2))
+        dispatch._parse_tile("mpp_tensor", (64, 64))       # (BM, BN) form needs BM = 128
+    with pytest.raises(ValueError):
+        dispatch._parse_tile("mpp_tensor", (64, 0, 2))
     with pytest.raises(AssertionError):
         dispatch._parse_tile("simd", (64, 64))
 
@@ -88,3 +98,12 @@ def test_vector_argument_checks():
 def test_outer_is_broadcast_multiply_on_host_types():
     a, b = torch.arange(3.0), torch.arange(4.0)
     assert torch.equal(mb.outer(a, b), torch.outer(a, b))
+
+
+def test_metalblas_alias_module():
+    """``import metalblas`` binds the reference's package name to this build."""
+    import metalblas
+    import metalblas_b200
+    for name in metalblas_b200.__all__:
+        assert getattr(metalblas, name) is getattr(metalblas_b200, name)
+    assert metalblas.kernels.plan is metalblas_b200.kernels.plan

@@ -83,3 +83,67 @@ def test_sharded_products_world2_gloo():
             p.kill()
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     assert dict(results) == {0: (True, True, True, True), 1: (True, True, True, True)}
+
+
+def _peer_worker(rank, world, port, results):
+    """The IPC-handle exchange and the fused-path agreement of peer.py / shard.py
+    over gloo (no CUDA needed: handles are opaque bytes here)."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from metalblas_b200 import peer
+        handle = bytes((rank * 37 + i) % 256 for i in range(peer.HANDLE_BYTES))
+        recs = peer.exchange(peer.pack_payload(handle, 4096 * (rank + 1) + 7), None, torch.device("cpu"))
+        got = [peer.unpack_payload(r) for r in recs]
+        want = [(bytes((r * 37 + i) % 256 for i in range(peer.HANDLE_BYTES)), 4096 * (r + 1) + 7)
+                for r in range(world)]
+        ok_exchange = got == want
+        # every rank must take the same path: the agreement is the minimum
+        ok_agree = shard._agree(("k", 1), rank == 0, None, torch.device("cpu")) is False
+        ok_cached = shard._agree(("k", 1), True, None, torch.device("cpu")) is False   # decided once
+        ok_agree2 = shard._agree(("k", 2), True, None, torch.device("cpu")) is True
+        results[rank] = (ok_exchange, ok_agree and ok_cached and ok_agree2)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_peer_exchange_world2_gloo():
+    ctx = mp.get_context("spawn")
+    manager = ctx.Manager()
+    results = manager.dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_peer_worker, args=(r, 2, port, results)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    assert dict(results) == {0: (True, True), 1: (True, True)}
+
+
+def test_peer_payload_and_slots():
+    from metalblas_b200 import peer
+    h = bytes(range(64))
+    t = peer.pack_payload(h, -12345)
+    assert t.dtype == torch.uint8 and t.numel() == peer.HANDLE_BYTES + 8
+    assert peer.unpack_payload(t) == (h, -12345)
+    with pytest.raises(ValueError):
+        peer.pack_payload(b"short", 0)
+    assert peer.slot_bytes(1) == peer.SLOT_ALIGN
+    assert peer.slot_bytes(peer.SLOT_ALIGN) == peer.SLOT_ALIGN
+    assert peer.slot_bytes(peer.SLOT_ALIGN + 1) == 2 * peer.SLOT_ALIGN
+    # without a process group the world is one rank and the barrier is a no-op
+    assert peer.world_of(None) == (1, 0)
+    peer.barrier(None)
+
+
+def test_fused_gather_needs_cuda_and_the_default_product():
+    a = torch.zeros(4, 4, dtype=torch.bfloat16)
+    assert not shard._fusable((a, a), None, None, 2)              # CPU tensors
+    assert not shard._fusable((a, a), torch.matmul, None, 2)      # custom local product
+    assert not shard._fusable((a, a), None, None, 1)              # one rank: nothing to gather
+    assert not shard._fusable((a, a), None, None, 9)              # more peers than the kernel's table
