@@ -1965,6 +1965,7 @@ int mb_gemm_noalloc(const mb_gemm_desc *d, void *stream) {
     // any layout), and under an explicit tensor-core backend they are refused.
     mb_gemm_desc r = q;
     r.workspace_bytes = 0;
+    pl = Plan{};  // a fresh plan: the planners fill only the fields their kind uses
     rc = plan_for(&r, pl, o, sms);
     if (rc)
       return fail(MB_ERR_WORKSPACE,
