@@ -52,8 +52,8 @@ def test_config1_gemm_and_addmm(mb):
 
 # ------------------------------------------------------------------ config 2
 GEMV = [(M, K, N) for M in (1, 4, 16) for K in (4096, 8192, 16384) for N in (4096, 14336, 28672)]
-GEMV_CASES = ([(s, torch.bfloat16, lay) for s in GEMV for lay in ("x@W", "x@Wt", "x@Wcm")]
-              + [(s, torch.float16, "x@W") for s in GEMV])
+GEMV_CASES = [(s, dt, lay) for dt in (torch.bfloat16, torch.float16) for s in GEMV
+              for lay in ("x@W", "x@Wt", "x@Wcm")]
 
 
 @pytest.mark.parametrize("shape,dtype,layout", GEMV_CASES,
@@ -72,6 +72,44 @@ def test_config2_gemv_sweep(mb, shape, dtype, layout):
     cols = torch.randperm(N, generator=torch.Generator().manual_seed(3))[:256].sort().values
     ref = orc.product(to_np(x), to_np(W[:, cols.cuda()]), NAME[dtype])
     _check(to_np(y[:, cols.cuda()]), ref, dtype, f"gemv {shape} {layout}")
+
+
+# Batched thin products, the reference's batched gemv_bt layout
+# (metalblas/shaders/gemv_bt.h:67-74: a batch of [M <= 16, K] @ [K, N] with W
+# row-major, or read transposed from [N, K] storage).
+BATCHED_THIN = [(B, M, K, N, dt, lay) for dt in (torch.bfloat16, torch.float16) for (B, M, K, N) in
+                ((8, 4, 4096, 4096), (8, 16, 4096, 4096), (4, 4, 8192, 14336), (4, 16, 8192, 14336))
+                for lay in ("W", "Wt")]
+
+
+@pytest.mark.parametrize("B,M,K,N,dtype,layout", BATCHED_THIN,
+                         ids=[f"{NAME[c[4]]}-{c[5]}-{c[0]}x{c[1]}x{c[2]}x{c[3]}" for c in BATCHED_THIN])
+def test_config2_batched_thin(mb, B, M, K, N, dtype, layout):
+    """[B, M, K] @ [B, K, N] with M in {4, 16}: W ~ N(0, 0.02), x ~ N(0, 1), seed 1;
+    "Wt": each batch's W stored [N, K] and read transposed."""
+    x = _gpu_randn((B, M, K), dtype, 1)
+    if layout == "W":
+        W = _gpu_randn((B, K, N), dtype, 2, 0.02)
+    else:
+        W = _gpu_randn((B, N, K), dtype, 2, 0.02).transpose(1, 2)
+    y = mb.bmm(x, W)
+    cols = torch.randperm(N, generator=torch.Generator().manual_seed(3))[:256].sort().values.cuda()
+    for b in (0, B - 1):
+        ref = orc.product(to_np(x[b]), to_np(W[b][:, cols]), NAME[dtype])
+        _check(to_np(y[b][:, cols]), ref, dtype, f"batched thin {B}x{M}x{K}x{N} {layout} batch {b}")
+
+
+def test_config2_w_at_x(mb):
+    """y = W @ x (the gemv_nt orientation, metalblas/shaders/gemv_nt.h:16-101):
+    W [N, K] row-major, bf16 and fp16, through mv."""
+    for dtype in (torch.bfloat16, torch.float16):
+        for (N, K) in ((4096, 4096), (14336, 8192), (28672, 16384)):
+            W = _gpu_randn((N, K), dtype, 2, 0.02)
+            x = _gpu_randn((K,), dtype, 1)
+            y = mb.mv(W, x)
+            rows = torch.randperm(N, generator=torch.Generator().manual_seed(3))[:256].sort().values.cuda()
+            ref = orc.product(to_np(W[rows]), to_np(x)[:, None], NAME[dtype])[:, 0]
+            _check(to_np(y[rows]), ref, dtype, f"W@x {N}x{K}")
 
 
 # ------------------------------------------------------------------ config 3
