@@ -292,6 +292,12 @@ const bool g_pair_enabled = [] {
   const char *s = getenv("METALBLAS_PAIR");
   return !(s && s[0] == '0');
 }();
+// Stream-K tails on CTA pairs in the tile table (METALBLAS_PAIR_SK=0 leaves
+// them out; stream_k = 2 with cta_pair = 2 still requests one).
+const bool g_pair_sk = [] {
+  const char *s = getenv("METALBLAS_PAIR_SK");
+  return !(s && s[0] == '0');
+}();
 
 // HBM bytes per clock per SM when every SM streams (6537 GB/s / 148 / 1.965 GHz).
 constexpr double kHbmBytesPerClkPerSm = 22.4;
@@ -383,13 +389,13 @@ void choose_tc_tile_uncached(const Op &o, int sms, int force_bn, int force_split
     // measured no faster at 4096^3 and slower at 8192^3, so only on request)
     const bool want_pair = s3 ? (bn == 128 && force_pair == 2)
                               : (force_pair == 2 || (force_pair == 0 && g_pair_enabled && o.M > 128 && kb_total >= 8));
-    if ((bn == 128 || bn == 256) && pair_fits && want_pair && (!force_split || force_split == 1) && force_sk != 2) {
+    if ((bn == 128 || bn == 256) && pair_fits && want_pair && (!force_split || force_split == 1)) {
       const int pairs = sms / 2;
       const int64_t ptiles = o.batch * ceil_div(o.M, 256) * ceil_div(o.N, bn);
       const double punit = kb_total * kbcp(bn) + 4.0 * bn;
       const int64_t w = ceil_div(ptiles, pairs);
-      consider(w * punit, (double)ptiles * 2, (double)w, 0.0, bn, am, bm, 1, kb_total, ptiles, 0, 2);
-      const bool half_ok = bn == 256 && bm && (bn / 4) * esz >= 128;
+      if (force_sk != 2) consider(w * punit, (double)ptiles * 2, (double)w, 0.0, bn, am, bm, 1, kb_total, ptiles, 0, 2);
+      const bool half_ok = bn == 256 && bm && (bn / 4) * esz >= 128 && force_sk != 2;
       if (half_ok && ptiles > pairs && ptiles % pairs) {
         const int64_t dp = (ptiles / pairs) * pairs;
         const int64_t tail_units = 2 * (ptiles - dp);
@@ -397,6 +403,23 @@ void choose_tc_tile_uncached(const Op &o, int sms, int force_bn, int force_split
         const double waves = (double)(dp / pairs + ceil_div(tail_units, pairs));
         consider((dp / pairs) * punit + ceil_div(tail_units, pairs) * phalf, (double)(dp + tail_units) * 2, waves,
                  0.0, bn, am, bm, 1, kb_total, dp, 1, 2);
+      }
+      // stream-K tail on pairs: whole 256-row tiles for the full waves, the
+      // tiles left over cut into equal K-block ranges, one per pair (each CTA
+      // of a pair publishes and reduces its own 128 rows)
+      if (have_ws && g_pair_sk && force_sk != 1 && !force_split && !s3 && ptiles % pairs) {
+        const int64_t dp = (ptiles / pairs) * pairs;
+        const int64_t tail = ptiles - dp;
+        const int64_t iters = tail * kb_total;
+        if ((iters >= 4 * (int64_t)pairs || (force_sk == 2 && iters >= pairs)) &&
+            tail * 2 * tc::NUM_EPI_WARPS <= kMaxTickets) {
+          const int maxp = sk_max_parts(tail, kb_total, pairs);
+          const double share = (double)ceil_div(iters, pairs) * kbcp(bn);
+          const double fix = maxp > 1 ? 8.0 * 4.0 * bn + 8.0 * maxp * bn : 4.0 * bn;
+          const double extra = maxp > 1 ? (double)tail * maxp * 256.0 * bn * 8.0 : 0.0;
+          consider((dp / pairs) * punit + share + fix, (double)(dp + pairs) * 2, (double)(dp / pairs + 1), extra,
+                   bn, am, bm, maxp, kb_total, dp, 0, 2, 1);
+        }
       }
     }
     // stream-K tail: whole tiles for the full waves, the tiles left over cut
@@ -500,7 +523,8 @@ bool plan_tc(const Op &o, int sms, const mb_gemm_desc *d, bool have_ws, Plan &pl
   pl.kind = PK_TC;
   const int64_t tiles = o.batch * pl.tiles_m * pl.tiles_n;
   if (pl.splits > 1 && tiles > pl.dp_tiles) {
-    pl.ws_bytes = kTicketBytes + (tiles - pl.dp_tiles) * pl.splits * 128 * pl.bn * 4;
+    // one BM x BN slot per piece and per CTA of a pair
+    pl.ws_bytes = kTicketBytes + (tiles - pl.dp_tiles) * pl.splits * pl.pair * 128 * pl.bn * 4;
   } else if (!pl.tail_half) {
     pl.splits = 1;
     pl.dp_tiles = tiles;
@@ -1237,7 +1261,6 @@ int launch_tc_bn(const Op &o, const Plan &pl, const EpiScalars &e, void *ws, int
   p.tail_half = pl.tail_half;
   p.num_units = (int)units;
   if (pl.sk) {
-    if constexpr (PAIR != 1) return fail(MB_ERR_INVALID, "stream-K needs single-CTA tiles");
     p.sk = 1;
     p.sk_iters = (long long)(tiles - pl.dp_tiles) * pl.kb_total;
   }
@@ -1278,7 +1301,8 @@ int launch_tc_bn(const Op &o, const Plan &pl, const EpiScalars &e, void *ws, int
     kern<<<grid, tc::NUM_THREADS, C_::SMEM_BYTES, st>>>(p);
   } else {
     // one cluster (CTA pair) per unit slot; the pair shares each 256-row tile
-    const int pairs = (int)std::min<int64_t>(units, sms / 2);
+    // (stream-K ranges are cut for exactly sk_ctas / 2 pairs)
+    const int pairs = pl.sk ? (int)(pl.sk_ctas / 2) : (int)std::min<int64_t>(units, sms / 2);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * pairs, 1, 1);
     cfg.blockDim = dim3(tc::NUM_THREADS, 1, 1);

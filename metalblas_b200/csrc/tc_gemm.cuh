@@ -87,8 +87,8 @@ struct TcParams {
   EpiScalars epi;
   int c_vec;             // c_cs == 1 and every row start is 16-byte aligned
   int c_tma;             // write C through tmC
-  void *ws;              // split-K partials: tail_tiles * splits * BM * BN * 4 bytes
-  unsigned *tickets;     // NUM_EPI_WARPS per tail tile, zero on entry and exit
+  void *ws;              // split-K partials: tail_tiles * splits * PAIR * BM * BN * 4 bytes
+  unsigned *tickets;     // NUM_EPI_WARPS per tail tile and CTA of a pair, zero on entry and exit
   int sk;                // tail tiles partitioned stream-K (splits = partial slots per tile)
   long long sk_iters;    // tail tiles * kb_total: the K-block iterations shared out
   unsigned long long timeout_ns;
@@ -771,12 +771,20 @@ __device__ __forceinline__ void pack32(const TcParams &p, int b, int m, int n0, 
   for (int j = 0; j < 32 * (int)sizeof(T) / 4; ++j) pk[j] = reinterpret_cast<const uint32_t *>(out)[j];
 }
 
+// Partial-sum slot of piece s of tail tile `tail` for CTA `rank` of its pair:
+// slots are BM x BN 4-byte values, ordered (tail, piece, rank).  A CTA pair
+// shares a 256-row tile, and each CTA publishes and reduces its own 128 rows.
+template <int PAIR>
+__device__ __forceinline__ int64_t slot_of(const TcParams &p, int tail, int s, int rank) {
+  return ((int64_t)tail * p.splits + s) * PAIR + rank;
+}
+
 // Split-K / stream-K epilogue after a warp published its partial: take a ticket
 // for (tail tile, warp); the warp that draws the last one sums every partial of
 // its 32 rows x wcols columns in K order and stores the result.
-template <class T, int BN, int RCH, bool PEER = false>
+template <class T, int BN, int RCH, bool PEER = false, int PAIR = 1>
 __device__ __forceinline__ void split_finish(const TcParams &p, const Unit &w, int ew, int lane, int m, int nbase,
-                                             int wcols) {
+                                             int wcols, int rank) {
   const int64_t slot_words = (int64_t)BM * BN;
   const int64_t warp_off = (int64_t)ew * 32 * wcols;
   // Each warp owns 32 rows x wcols columns of the tile and reduces them on
@@ -785,14 +793,14 @@ __device__ __forceinline__ void split_finish(const TcParams &p, const Unit &w, i
   __threadfence();
   __syncwarp();
   unsigned tk = 0;
-  unsigned *ticket = p.tickets + (int64_t)w.tail * NUM_EPI_WARPS + ew;
+  unsigned *ticket = p.tickets + ((int64_t)w.tail * PAIR + rank) * NUM_EPI_WARPS + ew;
   if (lane == 0) tk = atomicAdd(ticket, 1u);
   tk = __shfl_sync(0xffffffffu, tk, 0);
   if (tk == (unsigned)(w.nparts - 1)) {
     __threadfence();
     const uint4 *base = reinterpret_cast<const uint4 *>(reinterpret_cast<const uint32_t *>(p.ws) +
-                                                        (int64_t)w.tail * p.splits * slot_words + warp_off) + lane;
-    const int64_t slot_vec = slot_words / 4;
+                                                        slot_of<PAIR>(p, w.tail, 0, rank) * slot_words + warp_off) + lane;
+    const int64_t slot_vec = PAIR * slot_words / 4;   // from piece s to piece s + 1
     constexpr int NV = RCH / 4;                  // uint4 per lane per partial and chunk
     constexpr int PB = NV >= 8 ? 2 : (NV >= 4 ? 4 : 8);  // partials in flight: 16 loads per lane
 #pragma unroll 1
@@ -1092,14 +1100,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
           }
         } else {
           uint4 *part = reinterpret_cast<uint4 *>(reinterpret_cast<uint32_t *>(p.ws) +
-                                                  ((int64_t)w.tail * p.splits + w.s) * ((int64_t)BM * BN) +
+                                                  slot_of<PAIR>(p, w.tail, w.s, (int)rank) * ((int64_t)BM * BN) +
                                                   (int64_t)ew * 32 * wcols) + lane;
 #pragma unroll
           for (int c = 0; c < C_::RUN; c += 4)
             if (c < wcols)
               __stcg(part + (c >> 2) * 32, make_uint4(__float_as_uint(run[c]), __float_as_uint(run[c + 1]),
                                                       __float_as_uint(run[c + 2]), __float_as_uint(run[c + 3])));
-          split_finish<T, BN, RCH, PEER>(p, w, ew, lane, m, nbase, wcols);
+          split_finish<T, BN, RCH, PEER, PAIR>(p, w, ew, lane, m, nbase, wcols, (int)rank);
         }
         continue;
       }
@@ -1189,7 +1197,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
         const int64_t slot_words = (int64_t)BM * BN;
         const int64_t warp_off = (int64_t)ew * 32 * wcols;
         uint4 *part = reinterpret_cast<uint4 *>(reinterpret_cast<uint32_t *>(p.ws) +
-                                                ((int64_t)w.tail * p.splits + w.s) * slot_words + warp_off) + lane;
+                                                slot_of<PAIR>(p, w.tail, w.s, (int)rank) * slot_words + warp_off) + lane;
 #pragma unroll 1
         for (int c = 0; c < wcols; c += RCHO) {
           uint32_t r[32];
@@ -1202,7 +1210,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
         tc_fence_before();
         __syncwarp();
         if (lane == 0) release_tmem(abuf);
-        split_finish<TO, BN, RCHO, PEER>(p, w, ew, lane, m, nbase, wcols);
+        split_finish<TO, BN, RCHO, PEER, PAIR>(p, w, ew, lane, m, nbase, wcols, (int)rank);
       }
       if (++abuf == 2) { abuf = 0; aphase ^= 1u; }
     }

@@ -27,7 +27,9 @@ VARIANTS = [(0, 0, 0, 0), (64, 1, -1, 1), (64, 4, -1, 0), (128, 2, -1, 0), (256,
             (128, 3, -1, 0), (0, 0, 1, 0), (32, 4, 1, 0), (16, 2, 1, 0), (64, 1, 1, 0),
             (256, 1, -1, 2), (128, 1, -1, 2), (256, 0, -1, 2),
             # stream-K tail (forced), plain and swapped
-            (0, 0, -1, 0, 2), (64, 0, -1, 0, 2), (256, 0, -1, 0, 2), (16, 0, 1, 0, 2), (128, 0, 1, 0, 2)]
+            (0, 0, -1, 0, 2), (64, 0, -1, 0, 2), (256, 0, -1, 0, 2), (16, 0, 1, 0, 2), (128, 0, 1, 0, 2),
+            # stream-K tail on CTA pairs (each CTA of a pair reduces its own 128 rows)
+            (256, 0, -1, 2, 2), (128, 0, -1, 2, 2)]
 
 
 def _run(a, b, tile_n, split, swap, pair=0, sk=0, epilogue=None):
@@ -109,6 +111,43 @@ def test_stream_k_many_parts_and_repeat():
     fref = orc.fused(to_np(bias), to_np(A), to_np(B), 0.5, 2.0, "float16")
     ok, err = orc.check(to_np(C), fref, "float16")
     assert ok, f"batched stream-K baddbmm err={err}"
+    assert kernels.device_status() == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.int8], ids=NAME.get)
+def test_pair_stream_k(dtype):
+    """Stream-K tails on CTA pairs: the BASELINE config-1 shape (64 256-row tiles
+    on 74 pairs, all in the tail), a tile cut into one piece per pair, a shape
+    with whole-tile waves before the tail, and an epilogue with a bias row;
+    each run twice so the tickets must have returned to zero."""
+    from metalblas_b200 import kernels
+    gen = torch.Generator().manual_seed(12)
+    full = dtype is torch.int8
+    for (M, N, K, bn) in ((2048, 2048, 4096, 256), (256, 256, 65536, 256), (4096, 4096, 1024, 256),
+                          (1000, 1000, 3000, 128)):
+        a = rand((M, K), dtype, gen, full_range=full)
+        b = rand((K, N), dtype, gen, full_range=full)
+        ref = orc.product(to_np(a), to_np(b), NAME[dtype])
+        for _ in range(2):
+            c = _run(a, b, bn, 0, -1, pair=2, sk=2)
+            assert c is not None
+            ok, err = orc.check(to_np(c), ref, NAME[dtype])
+            assert ok, f"{dtype} {M}x{N}x{K} bn={bn} pair stream-K err={err}"
+    a = rand((2048, 4096), dtype, gen, full_range=full)
+    b = rand((4096, 2048), dtype, gen, full_range=full)
+    bias = rand((2048,), dtype, gen, full_range=full)
+    beta, alpha = (3, -2) if full else (0.5, 2.0)
+    c = _run(a, b, 256, 0, -1, pair=2, sk=2, epilogue=(bias, (0, 1, 0), beta, alpha, True, True))
+    ref = orc.fused(to_np(bias), to_np(a), to_np(b), beta, alpha, NAME[dtype])
+    ok, err = orc.check(to_np(c), ref, NAME[dtype])
+    assert ok, f"pair stream-K addmm err={err}"
+    d = _lib.new_desc()
+    d.dtype, d.backend = _lib.DTYPE_CODE[dtype], _lib.MB_BACKEND_TC
+    d.M, d.N, d.K = 2048, 2048, 4096
+    d.A, d.B, d.C = a.data_ptr(), b.data_ptr(), c.data_ptr()
+    d.a_rs, d.a_cs, d.b_rs, d.b_cs, d.c_rs, d.c_cs = 4096, 1, 2048, 1, 2048, 1
+    d.tile_n, d.cta_pair, d.stream_k, d.workspace_bytes = 256, 2, 2, -1
+    assert "pair=2 sk=1" in _lib.plan_query(d)
     assert kernels.device_status() == 0
 
 
