@@ -298,6 +298,12 @@ const bool g_pair_sk = [] {
   const char *s = getenv("METALBLAS_PAIR_SK");
   return !(s && s[0] == '0');
 }();
+// 512-wide CTA-pair tiles in the tile table (METALBLAS_PAIR_WIDE=0 leaves
+// them out; tile_n = 512 still requests one).
+const bool g_pair_wide = [] {
+  const char *s = getenv("METALBLAS_PAIR_WIDE");
+  return !(s && s[0] == '0');
+}();
 
 // HBM bytes per clock per SM when every SM streams (6537 GB/s / 148 / 1.965 GHz).
 constexpr double kHbmBytesPerClkPerSm = 22.4;
@@ -327,7 +333,7 @@ void choose_tc_tile_uncached(const Op &o, int sms, int force_bn, int force_split
     return s3 ? std::max(6.0 * bn, 2.0 * (128.0 + bn / 2.0) * 128.0 / 35.0) : kblock_cycles_pair(bn);
   };
   const int64_t kb_total = ceil_div(o.K, BK);
-  static const int bns[] = {16, 32, 64, 128, 256};
+  static const int bns[] = {16, 32, 64, 128, 256, 512};
   double best = 1e300;
   const double opnd_bytes =
       (double)(o.M * o.K * (o.sA ? o.batch : 1) + o.N * o.K * (o.sB ? o.batch : 1)) * esz +
@@ -360,12 +366,14 @@ void choose_tc_tile_uncached(const Op &o, int sms, int force_bn, int force_split
   for (int bn : bns) {
     if (force_bn && bn != force_bn) continue;
     if (s3 && bn > 128) continue;  // 3xTF32: see launch_tc<float>
+    // 512 columns: CTA pairs only, whole tiles only (below)
+    const bool wide = bn > 256;
     int am, bm;
     if (!tc_layout_ok(o, bn, am, bm, nullptr)) continue;
     if (!force_bn && bn > 16 && round_up(o.N, 16) <= bn / 2) continue;  // a smaller tile already covers N
     const int64_t tiles = o.batch * ceil_div(o.M, 128) * ceil_div(o.N, bn);
     const double unit_full = kb_total * kbc(bn) + 4.0 * bn;
-    if ((!force_split || force_split == 1) && force_pair != 2 && force_sk != 2) {
+    if (!wide && (!force_split || force_split == 1) && force_pair != 2 && force_sk != 2) {
       // whole tiles
       const int64_t w = ceil_div(tiles, sms);
       consider(w * unit_full, (double)tiles, (double)w, 0.0, bn, am, bm, 1, kb_total, tiles, 0);
@@ -389,12 +397,17 @@ void choose_tc_tile_uncached(const Op &o, int sms, int force_bn, int force_split
     // measured no faster at 4096^3 and slower at 8192^3, so only on request)
     const bool want_pair = s3 ? (bn == 128 && force_pair == 2)
                               : (force_pair == 2 || (force_pair == 0 && g_pair_enabled && o.M > 128 && kb_total >= 8));
-    if ((bn == 128 || bn == 256) && pair_fits && want_pair && (!force_split || force_split == 1)) {
+    if ((bn == 128 || bn == 256 || (wide && (g_pair_wide || force_bn == 512))) && pair_fits && want_pair &&
+        (!force_split || force_split == 1)) {
       const int pairs = sms / 2;
       const int64_t ptiles = o.batch * ceil_div(o.M, 256) * ceil_div(o.N, bn);
-      const double punit = kb_total * kbcp(bn) + 4.0 * bn;
+      // The 512-wide tile's one accumulator leaves its epilogue exposed
+      // (about 12 cycles per column): it pays off through its 25% fewer
+      // operand bytes per FLOP when there are tiles enough to fill the pairs.
+      const double punit = kb_total * kbcp(bn) + (wide ? 12.0 : 4.0) * bn;
       const int64_t w = ceil_div(ptiles, pairs);
       if (force_sk != 2) consider(w * punit, (double)ptiles * 2, (double)w, 0.0, bn, am, bm, 1, kb_total, ptiles, 0, 2);
+      if (wide) continue;
       const bool half_ok = bn == 256 && bm && (bn / 4) * esz >= 128 && force_sk != 2;
       if (half_ok && ptiles > pairs && ptiles % pairs) {
         const int64_t dp = (ptiles / pairs) * pairs;
@@ -422,6 +435,7 @@ void choose_tc_tile_uncached(const Op &o, int sms, int force_bn, int force_split
         }
       }
     }
+    if (wide) continue;
     // stream-K tail: whole tiles for the full waves, the tiles left over cut
     // into equal K-block ranges, one per CTA (every CTA busy to the end)
     if (have_ws && force_pair != 2 && force_sk != 1 && !force_split && tiles % sms) {
@@ -1072,8 +1086,8 @@ int validate(const mb_gemm_desc *d) {
   if (d->dtype < MB_F32 || d->dtype > MB_I64) return fail(MB_ERR_UNSUPPORTED, "dtype %d not supported", d->dtype);
   if (d->M < 0 || d->N < 0 || d->K < 0 || d->batch < 0) return fail(MB_ERR_INVALID, "negative extent");
   if (d->backend < MB_BACKEND_AUTO || d->backend > MB_BACKEND_SIMT) return fail(MB_ERR_INVALID, "unknown backend %d", d->backend);
-  if (d->tile_n && (d->tile_n % 16 || d->tile_n < 16 || d->tile_n > 256 || (d->tile_n & (d->tile_n - 1))))
-    return fail(MB_ERR_INVALID, "tile_n must be one of 16, 32, 64, 128, 256");
+  if (d->tile_n && (d->tile_n % 16 || d->tile_n < 16 || d->tile_n > 512 || (d->tile_n & (d->tile_n - 1))))
+    return fail(MB_ERR_INVALID, "tile_n must be one of 16, 32, 64, 128, 256 (or 512 on a CTA pair)");
   if (d->split_k < 0 || d->split_k > 65535) return fail(MB_ERR_INVALID, "split_k out of range");
   if (d->cta_pair < 0 || d->cta_pair > 2) return fail(MB_ERR_INVALID, "cta_pair must be 0, 1 or 2");
   const bool empty = d->M == 0 || d->N == 0 || d->batch == 0;
@@ -1239,7 +1253,12 @@ int launch_tc_bn(const Op &o, const Plan &pl, const EpiScalars &e, void *ws, int
   if (!pl.a_mn) rc = encode_map(&p.tmA, o.dt, o.A, o.K, o.M, bA, o.a_rs, o.sA, BK, tc::BM);
   else rc = encode_map(&p.tmA, o.dt, o.A, o.M, o.K, bA, o.a_cs, o.sA, 128 / ESZ, BK);
   if (rc) return rc;
-  if (!pl.b_mn) rc = encode_map(&p.tmB, o.dt, o.B, o.K, o.N, bB, o.b_cs, o.sB, BK, BN / PAIR);
+  if constexpr (BN > 256) {
+    // the 512-wide pair tile runs whole tiles only
+    if (pl.tail_half || pl.splits > 1 || pl.sk) return fail(MB_ERR_INVALID, "512-wide tiles run whole tiles only");
+  }
+  // K-major B: one box per MMA of this CTA's share of the tile's columns
+  if (!pl.b_mn) rc = encode_map(&p.tmB, o.dt, o.B, o.K, o.N, bB, o.b_cs, o.sB, BK, C_::UMMA_N / PAIR);
   else rc = encode_map(&p.tmB, o.dt, o.B, o.N, o.K, bB, o.b_rs, o.sB, 128 / ESZ, BK);
   if (rc) return rc;
   if constexpr (C_::NPART == 2) {
@@ -1330,6 +1349,7 @@ int launch_tc(const Op &o, const Plan &pl, const EpiScalars &e, void *ws, int sm
       switch (pl.bn) {
         case 128: return launch_tc_bn<T, 128, 2, T, true>(o, pl, e, ws, sms, st, peers);
         case 256: return launch_tc_bn<T, 256, 2, T, true>(o, pl, e, ws, sms, st, peers);
+        case 512: return launch_tc_bn<T, 512, 2, T, true>(o, pl, e, ws, sms, st, peers);
       }
       return fail(MB_ERR_INVALID, "bad tile_n %d for a CTA pair", pl.bn);
     }
@@ -1358,6 +1378,7 @@ int launch_tc(const Op &o, const Plan &pl, const EpiScalars &e, void *ws, int sm
     switch (pl.bn) {
       case 128: return launch_tc_bn<T, 128, 2>(o, pl, e, ws, sms, st);
       case 256: return launch_tc_bn<T, 256, 2>(o, pl, e, ws, sms, st);
+      case 512: return launch_tc_bn<T, 512, 2>(o, pl, e, ws, sms, st);
     }
     return fail(MB_ERR_INVALID, "bad tile_n %d for a CTA pair", pl.bn);
   }

@@ -125,13 +125,20 @@ struct Cfg {
   static constexpr int BAR_BYTES = 256;
   static constexpr int STAGES_RAW = (SMEM_LIMIT - 1024 - STAGING_BYTES - BAR_BYTES) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
+  // The 512-wide CTA-pair tile issues two N = 256 MMAs per K-step (tile
+  // columns [0, 256) and [256, 512)); its accumulator fills all 512 TMEM
+  // columns, so it has one accumulator instead of two.
+  static constexpr int UMMA_N = BN > 256 ? 256 : BN;  // N per tcgen05.mma
+  static constexpr int NMMA = BN / UMMA_N;            // MMAs per K-step
+  static constexpr int NACC = 2 * BN <= 512 ? 2 : 1;  // TMEM accumulators (two: epilogue overlaps the next tile)
   static constexpr int ACC_COLS = BN;           // fp32/s32: one column per N
-  static constexpr int TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
+  static constexpr int TMEM_COLS = (NACC * BN <= 32) ? 32 : (NACC * BN <= 64) ? 64 : (NACC * BN <= 128) ? 128
+                                 : (NACC * BN <= 256) ? 256 : 512;
   static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + STAGING_BYTES + BAR_BYTES;
   // columns per tcgen05.ld on the direct-store and split-K paths (16 for 16- and
   // 32-bit outputs keeps the epilogue within the register budget of 320 threads)
   static constexpr int RCH = QUART < (ESZ >= 2 ? 16 : 32) ? (QUART < 8 ? 8 : QUART) : (ESZ >= 2 ? 16 : 32);
-  static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N for M=128");
+  static_assert(BN % 16 == 0 && BN >= 16 && (BN <= 256 || (BN == 512 && PAIR == 2 && ESZ <= 2)), "UMMA N");
   static_assert(STAGES >= 2, "need a pipeline");
   static_assert(SMEM_BYTES <= SMEM_LIMIT, "shared memory");
   static_assert(3 * STAGES + 5 <= BAR_BYTES / 8 - 2, "barrier area");
@@ -949,7 +956,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
 #pragma unroll
             for (int j = 0; j < BM * ESZ / 128; ++j) load(sa + j * (BK * 128), &p.tmA, a_row0 + j * (128 / ESZ), kb * BK, ba);
           }
-          if (!p.b_mn) {
+          if constexpr (C_::NMMA == 2) {
+            // 512-wide pair tile: for MMA h this CTA holds tile columns
+            // [h * 256 + rank * 128, + 128), at byte offset h * 16 KB of the stage
+            constexpr int HB = (C_::UMMA_N / PAIR) * 128;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int col = w.tn * BN + h * C_::UMMA_N + (int)rank * (C_::UMMA_N / PAIR);
+              if (!p.b_mn) {
+                load(sb + h * HB, &p.tmB, kb * BK, col, bb);
+              } else {
+#pragma unroll
+                for (int j = 0; j < (C_::UMMA_N / PAIR) * ESZ / 128; ++j)
+                  load(sb + h * HB + j * (BK * 128), &p.tmB, col + j * (128 / ESZ), kb * BK, bb);
+              }
+            }
+          } else if (!p.b_mn) {
             load(sb, &p.tmB, kb * BK, w.tn * BN + (int)rank * (BN / PAIR), bb);
           } else {
             for (int j = 0; j < b_boxes; ++j) load(sb + j * (BK * 128), &p.tmB, b_col0 + j * (128 / ESZ), kb * BK, bb);
@@ -976,7 +998,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (rank == 0 && lane == 0) {
-      const uint32_t idesc_full = make_idesc<T, BN, TM_ROWS>(p.a_mn, p.b_mn);
+      const uint32_t idesc_full = make_idesc<T, C_::UMMA_N, TM_ROWS>(p.a_mn, p.b_mn);
       const uint32_t idesc_half = make_idesc<T, (BN >= 32 ? BN / 2 : BN), TM_ROWS>(p.a_mn, p.b_mn);
       // Canonical SW128 layouts: K-major SBO = 8 rows * 128 B; MN-major
       // LBO = next 128-byte MN column block (one TMA box), SBO = 8 K rows.
@@ -1011,6 +1033,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
               const uint64_t ad = sdesc(sa + ks * a_kstep, a_lbo, 1024);
               const uint64_t bd = sdesc(sb + ks * b_kstep, b_lbo, 1024);
               umma_g<ESZ, PAIR>(d_tmem, ad, bd, idesc, (kb > c0 || ks > 0) ? 1u : 0u);
+              if constexpr (C_::NMMA == 2) {
+                // tile columns [256, 512): this CTA's share of B 16 KB further on,
+                // accumulated in TMEM columns 256..511
+                const uint64_t bd2 = sdesc(sb + (C_::UMMA_N / PAIR) * 128 + ks * b_kstep, b_lbo, 1024);
+                umma_g<ESZ, PAIR>(d_tmem + C_::UMMA_N, ad, bd2, idesc, (kb > c0 || ks > 0) ? 1u : 0u);
+              }
               if constexpr (C_::NPART == 2) {
                 // 3xTF32: + A_hi B_lo + A_lo B_hi (A_lo B_lo is below fp32 resolution).
                 // Both operands are K-major here, so B_lo is one whole B share
@@ -1027,7 +1055,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
           }
           if (aborted) break;
           umma_commit_g<PAIR>(tfull_bar(abuf));  // accumulators ready for the epilogue(s)
-          if (++abuf == 2) { abuf = 0; aphase ^= 1u; }
+          if (++abuf == C_::NACC) { abuf = 0; aphase ^= 1u; }
         }
         if (aborted) break;
       }
@@ -1084,7 +1112,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
           tc_fence_before();
           __syncwarp();
           if (lane == 0) release_tmem(abuf);
-          if (++abuf == 2) { abuf = 0; aphase ^= 1u; }
+          if (++abuf == C_::NACC) { abuf = 0; aphase ^= 1u; }
         }
         if (!ok) break;
         if (!w.split) {
@@ -1175,7 +1203,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
                 sbuf ^= 1;
               }
             }
-            if (++abuf == 2) { abuf = 0; aphase ^= 1u; }
+            if (++abuf == C_::NACC) { abuf = 0; aphase ^= 1u; }
             continue;
           }
         }
@@ -1212,7 +1240,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
         if (lane == 0) release_tmem(abuf);
         split_finish<TO, BN, RCHO, PEER, PAIR>(p, w, ew, lane, m, nbase, wcols, (int)rank);
       }
-      if (++abuf == 2) { abuf = 0; aphase ^= 1u; }
+      if (++abuf == C_::NACC) { abuf = 0; aphase ^= 1u; }
     }
     if (lane == 0) bulk_wait0();  // every TMA store of this warp has completed
     // peer stores are performed system-wide before the CTA retires

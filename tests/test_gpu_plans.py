@@ -29,7 +29,9 @@ VARIANTS = [(0, 0, 0, 0), (64, 1, -1, 1), (64, 4, -1, 0), (128, 2, -1, 0), (256,
             # stream-K tail (forced), plain and swapped
             (0, 0, -1, 0, 2), (64, 0, -1, 0, 2), (256, 0, -1, 0, 2), (16, 0, 1, 0, 2), (128, 0, 1, 0, 2),
             # stream-K tail on CTA pairs (each CTA of a pair reduces its own 128 rows)
-            (256, 0, -1, 2, 2), (128, 0, -1, 2, 2)]
+            (256, 0, -1, 2, 2), (128, 0, -1, 2, 2),
+            # 512-wide CTA-pair tile (two N = 256 MMAs per K-step, one accumulator)
+            (512, 1, -1, 2)]
 
 
 def _run(a, b, tile_n, split, swap, pair=0, sk=0, epilogue=None):
@@ -149,6 +151,39 @@ def test_pair_stream_k(dtype):
     d.tile_n, d.cta_pair, d.stream_k, d.workspace_bytes = 256, 2, 2, -1
     assert "pair=2 sk=1" in _lib.plan_query(d)
     assert kernels.device_status() == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.int8], ids=NAME.get)
+def test_pair_wide_tile(dtype):
+    """The 512-wide CTA-pair tile: several tiles per pair (accumulator reuse
+    across tiles), ragged edges in M, N and K, B read K-major (x @ W^T) and
+    MN-major, an addmm epilogue and a batched, broadcast product."""
+    gen = torch.Generator().manual_seed(13)
+    full = dtype is torch.int8
+    for (M, N, K) in ((4096, 4096, 1024), (1000, 1500, 3000), (2304, 8192, 512)):
+        a = rand((M, K), dtype, gen, full_range=full)
+        for b in (rand((K, N), dtype, gen, full_range=full), rand((N, K), dtype, gen, full_range=full).t()):
+            ref = orc.product(to_np(a), to_np(b), NAME[dtype])
+            c = _run(a, b, 512, 1, -1, pair=2)
+            assert c is not None
+            ok, err = orc.check(to_np(c), ref, NAME[dtype])
+            assert ok, f"{dtype} {M}x{N}x{K} b_strides={b.stride()} wide tile err={err}"
+    a = rand((2048, 2048), dtype, gen, full_range=full)
+    b = rand((2048, 4096), dtype, gen, full_range=full)
+    bias = rand((4096,), dtype, gen, full_range=full)
+    beta, alpha = (3, -2) if full else (0.5, 2.0)
+    c = _run(a, b, 512, 1, -1, pair=2, epilogue=(bias, (0, 1, 0), beta, alpha, True, True))
+    ref = orc.fused(to_np(bias), to_np(a), to_np(b), beta, alpha, NAME[dtype])
+    ok, err = orc.check(to_np(c), ref, NAME[dtype])
+    assert ok, f"wide tile addmm err={err}"
+    A = rand((6, 600, 700), dtype, gen, full_range=full)
+    B = rand((1, 700, 1100), dtype, gen, full_range=full)
+    C = torch.empty(6, 600, 1100, dtype=dtype, device="cuda")
+    dispatch._launch(A, B, C, 600, 1100, 700, 6, (700, 1, 600 * 700), (1100, 1, 0), (1100, 1, 600 * 1100),
+                     backend=_lib.MB_BACKEND_TC, tile_n=512, cta_pair=2, autotune=False)
+    ref = orc.product(to_np(A), np.broadcast_to(to_np(B), (6, 700, 1100)), NAME[dtype])
+    ok, err = orc.check(to_np(C), ref, NAME[dtype])
+    assert ok, f"wide tile broadcast bmm err={err}"
 
 
 def test_complex32_workspace_does_not_clobber_tickets():
