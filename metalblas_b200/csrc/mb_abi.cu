@@ -285,6 +285,11 @@ double kblock_cycles(int bn) { return std::max(2.0 * bn, (128.0 + bn) * 128.0 / 
 // per K-block but loads only half of B's columns.  Calibrated on the B200:
 // 1.09-1.23x the single-CTA rate at BN=256 (4096^3 .. 8192^3, 2048x14336x4096).
 double kblock_cycles_pair(int bn) { return std::max(2.0 * bn, (128.0 + bn / 2.0) * 128.0 / 35.0); }
+// The 512-wide pair tile (two N = 256 MMAs per K-step) moves 48 KB per SM per
+// K-block for twice the work of the 256-wide one: measured 1.68-1.83x its
+// K-block time on the B200 (4096^3, 2048 x 14336 x 4096, 16384^3), i.e. the
+// operand stream at ~30.5 B/clk/SM.
+double kblock_cycles_pair_wide() { return (128.0 + 256.0) * 128.0 / 30.5; }
 
 // CTA-pair kernels in the tile table (METALBLAS_PAIR=0 leaves them out; they
 // can always be requested per call through mb_gemm_desc.cta_pair = 2).
@@ -330,6 +335,7 @@ void choose_tc_tile_uncached(const Op &o, int sms, int force_bn, int force_split
   const bool s3 = o.dt == MB_F32;
   auto kbc = [&](int bn) { return s3 ? std::max(6.0 * bn, 2.0 * (128.0 + bn) * 128.0 / 45.0) : kblock_cycles(bn); };
   auto kbcp = [&](int bn) {
+    if (bn > 256) return kblock_cycles_pair_wide();
     return s3 ? std::max(6.0 * bn, 2.0 * (128.0 + bn / 2.0) * 128.0 / 35.0) : kblock_cycles_pair(bn);
   };
   const int64_t kb_total = ceil_div(o.K, BK);
