@@ -320,7 +320,8 @@ def run_ours(args, w, rank, world, device):
 
     peak, hbm, src = _peaks()
     achieved = flops / (ms * 1e-3) / 1e12
-    traffic = _profile_traffic(f"tc_gemm_{w['dtype_name']}_{M}x{N}x{K}.txt")
+    traffic = _profile_traffic((f"tc_gemm_{w['dtype_name']}_wide512_{M}x{N}x{K}.txt" if "bn=512" in plan
+                                else f"tc_gemm_{w['dtype_name']}_{M}x{N}x{K}.txt"))
     roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                 "frac": achieved / peak, "peak_source": f"{src} bf16_tflops (burst)",
                 "traffic": traffic, "kernel": "mb::tc::tc_gemm_kernel", "per_launch_flop": flops}
