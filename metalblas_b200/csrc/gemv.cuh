@@ -212,6 +212,19 @@ __global__ void __launch_bounds__(NW * 32) gemv_cols_kernel(const GemvParams p) 
   const int64_t kend = min(p.K, kbeg + p.kchunk);
   const T *W = (const T *)p.W + b * p.sW;
   const T *X = (const T *)p.X + b * p.sX;
+  pdl_trigger();
+  if constexpr (VEC > 1) {
+    // The first 32 KB of this CTA's stripe of W (COLS columns of its rows,
+    // one 16-byte aligned run per row) into L2 while the previous kernel
+    // drains: enough to keep DRAM busy across the kernel boundary, too little
+    // to evict what the running kernels read.
+    constexpr int PF_ROWS = 32768 / (COLS * (int)sizeof(T));
+    const int64_t cb = cblk * COLS;
+    if (cb + COLS <= p.R && row0 == 0)
+      for (int64_t kk = kbeg + threadIdx.x; kk < min(kend, kbeg + PF_ROWS); kk += NW * 32)
+        prefetch_l2_bulk(W + kk * p.w_ld + cb, COLS * (uint32_t)sizeof(T));
+  }
+  pdl_wait();
   const int mrows = MR == 1 ? 1 : p.mrows;          // rows of x in all
   const int rows = MR == 1 ? 1 : min(MR, mrows - row0);  // rows in this CTA's block
   int64_t xoff[MR];
@@ -362,6 +375,8 @@ __global__ void __launch_bounds__(NW * 32) gemv_rows_kernel(const GemvParams p) 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t b = blockIdx.z;
   const int64_t r = (int64_t)blockIdx.x * NW + warp;
+  pdl_trigger();
+  pdl_wait();
   if (r >= p.R) return;
   const T *W = (const T *)p.W + b * p.sW + r * p.w_ld;
   const T *X = (const T *)p.X + b * p.sX;
@@ -451,6 +466,17 @@ gemv_rows_smem_kernel(const GemvParams p) {
 
   const int64_t kbeg = (int64_t)blockIdx.y * p.kchunk;
   const int64_t kend = min(p.K, kbeg + p.kchunk);
+  pdl_trigger();
+  if constexpr (VEC > 1) {
+    // the first 4 KB of each of this warp's rows over [kbeg, kend) into L2
+    // while the previous kernel drains (lane 0 of each row)
+    const int64_t kv = min((int64_t)4096, ((kend - kbeg) * (int64_t)sizeof(T)) & ~int64_t(15));
+#pragma unroll
+    for (int r = 0; r < RPW; ++r)
+      if (lane == 0 && live[r] && kv > 0 && (reinterpret_cast<uintptr_t>(wrow[r] + kbeg) & 15) == 0)
+        prefetch_l2_bulk(wrow[r] + kbeg, (uint32_t)kv);
+  }
+  pdl_wait();
   for (int64_t kc = kbeg; kc < kend; kc += KC) {
     const int kn = (int)min((int64_t)KC, kend - kc);
     __syncthreads();  // previous chunk fully consumed

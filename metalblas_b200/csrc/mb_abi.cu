@@ -1117,6 +1117,41 @@ EpiScalars make_epi(const mb_gemm_desc *d) {
 }
 
 // --------------------------------------------------------------------------- launches
+// Programmatic dependent launch for the GEMV and tcgen05 kernels (see
+// pdl_trigger / pdl_wait in mb_common.cuh); METALBLAS_PDL=0 launches them
+// with plain stream order.
+const bool g_pdl = [] {
+  const char *s = getenv("METALBLAS_PDL");
+  return !(s && s[0] == '0');
+}();
+
+template <class... KArgs, class... Args>
+int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, int cluster_x,
+               const char *what, Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (cluster_x > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = cluster_x;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  if (g_pdl) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cuda_check(cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...), what);
+}
+
 template <class T>
 int launch_simt(const Op &o, const EpiScalars &e, cudaStream_t st, const int *gate = nullptr) {
   SimtParams p{};
@@ -1172,6 +1207,7 @@ int launch_gemv(const Plan &pl, const EpiScalars &e, void *ws, cudaStream_t st) 
   }
   const unsigned gz = (unsigned)std::min<int64_t>(g.batch, 65535);
   if (g.batch > 65535) return fail(MB_ERR_INVALID, "batch too large for GEMV");
+  auto go = [&](auto kern, dim3 grid) { return launch_pdl(kern, grid, dim3(NW * 32), 0, st, 1, "gemv launch", g); };
   if (pl.kind == PK_GEMV_COLS) {
     dim3 grid((unsigned)(pl.gemv_ctas_x * std::max(g.mrb, 1)), (unsigned)g.ksplit, gz);
     constexpr bool thin = std::is_same<T, __nv_bfloat16>::value || std::is_same<T, __half>::value ||
@@ -1180,23 +1216,25 @@ int launch_gemv(const Plan &pl, const EpiScalars &e, void *ws, cudaStream_t st) 
       if constexpr (thin) {
         const int mr = gemv_mr(std::is_same<T, float>::value ? MB_F32 : MB_BF16, g.mrows);
         if (mr == 8) {
-          if constexpr (std::is_same<T, float>::value) gemv_cols_kernel<T, V, NW, 8><<<grid, NW * 32, 0, st>>>(g);
-        } else if (mr == 4) gemv_cols_kernel<T, V, NW, 4><<<grid, NW * 32, 0, st>>>(g);
-        else if (mr == 2) gemv_cols_kernel<T, V, NW, 2><<<grid, NW * 32, 0, st>>>(g);
-        else gemv_cols_kernel<T, V, NW><<<grid, NW * 32, 0, st>>>(g);
+          if constexpr (std::is_same<T, float>::value) return go(gemv_cols_kernel<T, V, NW, 8>, grid);
+        } else if (mr == 4) return go(gemv_cols_kernel<T, V, NW, 4>, grid);
+        else if (mr == 2) return go(gemv_cols_kernel<T, V, NW, 2>, grid);
+        else return go(gemv_cols_kernel<T, V, NW>, grid);
       } else {
-        gemv_cols_kernel<T, V, NW><<<grid, NW * 32, 0, st>>>(g);
+        return go(gemv_cols_kernel<T, V, NW>, grid);
       }
-    } else gemv_cols_kernel<T, 1, NW><<<dim3((unsigned)ceil_div(g.R, 32), (unsigned)g.ksplit, gz), NW * 32, 0, st>>>(g);
+    } else {
+      return go(gemv_cols_kernel<T, 1, NW>, dim3((unsigned)ceil_div(g.R, 32), (unsigned)g.ksplit, gz));
+    }
   } else {
     if (pl.vec > 1 && g.x_vec) {
       constexpr int RPW = kGemvRowsPerWarp;  // x staged in shared memory
       dim3 grid((unsigned)ceil_div(g.R, NW * RPW), (unsigned)g.ksplit, gz);
-      gemv_rows_smem_kernel<T, V, NW, RPW><<<grid, NW * 32, 0, st>>>(g);
+      return go(gemv_rows_smem_kernel<T, V, NW, RPW>, grid);
     } else {
       dim3 grid((unsigned)ceil_div(g.R, NW), 1, gz);
-      if (pl.vec > 1) gemv_rows_kernel<T, V, NW><<<grid, NW * 32, 0, st>>>(g);
-      else gemv_rows_kernel<T, 1, NW><<<grid, NW * 32, 0, st>>>(g);
+      if (pl.vec > 1) return go(gemv_rows_kernel<T, V, NW>, grid);
+      else return go(gemv_rows_kernel<T, 1, NW>, grid);
     }
   }
   return cuda_check(cudaGetLastError(), "gemv launch");
@@ -1323,27 +1361,14 @@ int launch_tc_bn(const Op &o, const Plan &pl, const EpiScalars &e, void *ws, int
   if constexpr (PAIR == 1) {
     // stream-K ranges are cut for exactly sk_ctas CTAs
     const int grid = pl.sk ? (int)pl.sk_ctas : (int)std::min<int64_t>(units, sms);
-    kern<<<grid, tc::NUM_THREADS, C_::SMEM_BYTES, st>>>(p);
+    return launch_pdl(kern, dim3(grid), dim3(tc::NUM_THREADS), C_::SMEM_BYTES, st, 1, "tc_gemm launch", p);
   } else {
     // one cluster (CTA pair) per unit slot; the pair shares each 256-row tile
     // (stream-K ranges are cut for exactly sk_ctas / 2 pairs)
     const int pairs = pl.sk ? (int)(pl.sk_ctas / 2) : (int)std::min<int64_t>(units, sms / 2);
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(2 * pairs, 1, 1);
-    cfg.blockDim = dim3(tc::NUM_THREADS, 1, 1);
-    cfg.dynamicSmemBytes = C_::SMEM_BYTES;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    rc = cuda_check(cudaLaunchKernelEx(&cfg, kern, p), "tc_gemm (CTA pair) launch");
-    if (rc) return rc;
+    return launch_pdl(kern, dim3(2 * pairs), dim3(tc::NUM_THREADS), C_::SMEM_BYTES, st, 2,
+                      "tc_gemm (CTA pair) launch", p);
   }
-  return cuda_check(cudaGetLastError(), "tc_gemm launch");
 }
 
 template <class T, bool PEER = false>

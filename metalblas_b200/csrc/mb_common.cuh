@@ -158,4 +158,20 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
+// Programmatic dependent launch.  The GEMV and tcgen05 kernels are launched
+// with programmatic stream serialization: a kernel may start while the
+// previous kernel on its stream is still finishing, once every CTA of that
+// kernel has called pdl_trigger (or exited).  pdl_wait blocks until the
+// previous kernel has completed and its memory operations are visible; every
+// thread calls it before its first global load or store of data another
+// kernel may write, so only set-up work (barriers, TMEM, tensor-map and L2
+// prefetches) overlaps.  Both are no-ops for a launch without the attribute.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// L2 prefetch of `bytes` (a multiple of 16) at a 16-byte aligned address: a
+// hint with no effect on the memory model, so it may run before pdl_wait.
+__device__ __forceinline__ void prefetch_l2_bulk(const void *p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 }  // namespace mb

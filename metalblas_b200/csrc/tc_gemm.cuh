@@ -894,6 +894,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
     else return mbar_wait(bar, parity, abort_flag, p.timeout_ns);
   };
 
+  // The next kernel on the stream may begin its own set-up now; this kernel's
+  // set-up (barriers, TMEM, tensor maps) overlaps the previous kernel's end,
+  // and pdl_wait below orders every global access after that kernel.
+  pdl_trigger();
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(full_bar(s), 1);
@@ -919,6 +923,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
   if constexpr (PAIR == 2) cluster_sync_all();  // peer barriers initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
