@@ -1051,6 +1051,53 @@ def _offset_view(t):
     return big[1:, 1:]
 
 
+# `bench.py --one CASE`: one product, a few warm-up calls and `--steps` timed
+# calls (CUDA events), one JSON line.  Small enough to run under ncu; the
+# profiles/ summaries name these commands.
+ONE_CASES = {
+    "bf16_gemm_4096": ("gemm", torch.bfloat16, 4096, 4096, 4096, None),
+    "fp16_gemm_4096": ("gemm", torch.float16, 4096, 4096, 4096, None),
+    "c32_gemm_4096": ("gemm", torch.complex32, 4096, 4096, 4096, None),
+    "c64_gemm_4096": ("gemm", torch.complex64, 4096, 4096, 4096, None),
+    "fp32_gemm_4096": ("gemm", torch.float32, 4096, 4096, 4096, None),
+    "gemv_bf16_1x4096x4096": ("gemm", torch.bfloat16, 1, 4096, 4096, None),
+    "gemv_bf16_1x4096x4096_wt": ("gemm", torch.bfloat16, 1, 4096, 4096, "wt"),
+    "gemv_bf16_16x4096x4096": ("gemm", torch.bfloat16, 16, 4096, 4096, None),
+}
+
+
+def run_one(args):
+    import metalblas_b200 as mb
+    kind, dt, M, N, K, lay = ONE_CASES[args.one]
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+
+    def rnd(*shape):
+        if dt.is_complex:
+            return torch.complex(torch.randn(*shape, generator=g, device=dev),
+                                 torch.randn(*shape, generator=g, device=dev)).to(dt)
+        return torch.randn(*shape, generator=g, device=dev).to(dt)
+    byts = (M * K + K * N + M * N) * torch.empty((), dtype=dt).element_size()
+    sets = _nsets(byts, cap=16)
+    A = [rnd(M, K) for _ in range(sets)]
+    B = [(rnd(N, K).t() if lay == "wt" else rnd(K, N)) for _ in range(sets)]
+    C = [torch.empty(M, N, dtype=dt, device=dev) for _ in range(sets)]
+    for i in range(max(args.warmup, 3)):
+        mb.matmul(A[i % sets], B[i % sets], out=C[i % sets])
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.steps):
+        mb.matmul(A[i % sets], B[i % sets], out=C[i % sets])
+    e1.record()
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    flops = (8.0 if dt.is_complex else 2.0) * M * N * K
+    print(json.dumps({"one": args.one, "ms": ms, "tflops": flops / (ms * 1e-3) / 1e12,
+                      "gbs": byts / (ms * 1e-3) / 1e9, "plan": mb.kernels.plan(A[0], B[0]),
+                      "l2": f"{sets} rotating input sets"}), flush=True)
+
+
 def run_suite(args):
     assert torch.cuda.is_available(), "bench.py --suite needs a CUDA device"
     torch.cuda.set_device(0)
@@ -1074,9 +1121,14 @@ def main():
                     help="measure every BASELINE config on one GPU, one JSON line per case")
     ap.add_argument("--configs", default="C1,C2,C3,C4,C5")
     ap.add_argument("--cpu-seconds", type=float, default=1.0, help="host time per CPU-baseline sample")
+    ap.add_argument("--one", choices=sorted(ONE_CASES), help="time one product (small enough to run under ncu)")
     args = ap.parse_args()
     if args.suite:
         run_suite(args)
+        return
+    if args.one:
+        torch.cuda.set_device(0)
+        run_one(args)
         return
     w = dict(WORKLOADS[args.workload])
     w["name"] = args.workload

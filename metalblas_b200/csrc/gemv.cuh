@@ -212,7 +212,6 @@ __global__ void __launch_bounds__(NW * 32) gemv_cols_kernel(const GemvParams p) 
   const int64_t kend = min(p.K, kbeg + p.kchunk);
   const T *W = (const T *)p.W + b * p.sW;
   const T *X = (const T *)p.X + b * p.sX;
-  pdl_trigger();
   if constexpr (VEC > 1) {
     // The first 32 KB of this CTA's stripe of W (COLS columns of its rows,
     // one 16-byte aligned run per row) into L2 while the previous kernel
@@ -310,6 +309,9 @@ __global__ void __launch_bounds__(NW * 32) gemv_cols_kernel(const GemvParams p) 
     }
   }
 
+  // W is streamed: the next kernel on the stream may start its set-up and
+  // prefetch (launched once every CTA of this grid has passed here).
+  pdl_trigger();
   // Sum the warps' partials row by row through one shared buffer.  ksplit == 1
   // stores the result; otherwise the partial is published for the last CTA.
   const int64_t cbase = cblk * COLS;
@@ -375,9 +377,8 @@ __global__ void __launch_bounds__(NW * 32) gemv_rows_kernel(const GemvParams p) 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t b = blockIdx.z;
   const int64_t r = (int64_t)blockIdx.x * NW + warp;
-  pdl_trigger();
   pdl_wait();
-  if (r >= p.R) return;
+  if (r >= p.R) { pdl_trigger(); return; }
   const T *W = (const T *)p.W + b * p.sW + r * p.w_ld;
   const T *X = (const T *)p.X + b * p.sX;
 
@@ -425,6 +426,7 @@ __global__ void __launch_bounds__(NW * 32) gemv_rows_kernel(const GemvParams p) 
     for (int64_t kk = lane; kk < p.K; kk += 32)
       E::mad(acc, E::load(W[kk], p.conj_w), E::load(X[kk * p.x_s], p.conj_x));
   }
+  pdl_trigger();  // W is streamed: the next kernel may start its set-up
 #pragma unroll
   for (int m = 16; m >= 1; m >>= 1) acc_add(acc, shfl_xor(acc, m));
   if (lane == 0) gemv_store<T>(p, b, r, acc);
@@ -466,7 +468,6 @@ gemv_rows_smem_kernel(const GemvParams p) {
 
   const int64_t kbeg = (int64_t)blockIdx.y * p.kchunk;
   const int64_t kend = min(p.K, kbeg + p.kchunk);
-  pdl_trigger();
   if constexpr (VEC > 1) {
     // the first 4 KB of each of this warp's rows over [kbeg, kend) into L2
     // while the previous kernel drains (lane 0 of each row)
@@ -516,6 +517,7 @@ gemv_rows_smem_kernel(const GemvParams p) {
       for (int r = 0; r < RPW; ++r)
         if (live[r]) E::mad(acc[r], E::load(wrow[r][kc + kk], p.conj_w), E::load(xs[kk], p.conj_x));
   }
+  pdl_trigger();  // W is streamed: the next kernel may start its set-up
 #pragma unroll
   for (int r = 0; r < RPW; ++r)
 #pragma unroll

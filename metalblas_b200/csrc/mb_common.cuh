@@ -161,7 +161,10 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 // Programmatic dependent launch.  The GEMV and tcgen05 kernels are launched
 // with programmatic stream serialization: a kernel may start while the
 // previous kernel on its stream is still finishing, once every CTA of that
-// kernel has called pdl_trigger (or exited).  pdl_wait blocks until the
+// kernel has called pdl_trigger (or exited).  The GEMV kernels trigger when
+// their stream of W is done (earlier, the next grid could take free CTA slots
+// and its prefetches be evicted before use); the tcgen05 kernel, whose CTAs
+// fill their SMs, triggers on entry.  pdl_wait blocks until the
 // previous kernel has completed and its memory operations are visible; every
 // thread calls it before its first global load or store of data another
 // kernel may write, so only set-up work (barriers, TMEM, tensor-map and L2
