@@ -1435,8 +1435,9 @@ int launch_c32(const Op &o, const Plan &pl, EpiScalars e, void *ws, int sms, cud
   pb.src = reinterpret_cast<const __half2 *>(o.B); pb.dst = bp;
   pb.rows = o.K; pb.cols = o.N; pb.rs = o.b_rs; pb.cs = o.b_cs; pb.bs = o.sB;
   pb.batch = pl.c32_b_batches; pb.conj_a = o.conj_a; pb.conj_b = o.conj_b;
-  const int64_t nb = pb.batch * pb.rows * pb.cols;
-  c32_build_b_kernel<<<(unsigned)std::min<int64_t>(ceil_div(nb, 256), grid_cap), 256, 0, st>>>(pb, pl.c32_ldb);
+  if (pb.batch > 65535) return fail(MB_ERR_INVALID, "batch too large for the complex32 path");
+  const dim3 bgrid((unsigned)ceil_div(pb.cols, 1024), (unsigned)std::min<int64_t>(pb.rows, 65535), (unsigned)pb.batch);
+  c32_build_b_kernel<<<bgrid, 256, 0, st>>>(pb, pl.c32_ldb);
   int rc = cuda_check(cudaGetLastError(), "complex32 B' build");
   if (rc) return rc;
   if (pl.c32_pack_a) {
