@@ -297,11 +297,14 @@ const bool g_pair_enabled = [] {
   const char *s = getenv("METALBLAS_PAIR");
   return !(s && s[0] == '0');
 }();
-// Stream-K tails on CTA pairs in the tile table (METALBLAS_PAIR_SK=0 leaves
-// them out; stream_k = 2 with cta_pair = 2 still requests one).
+// Stream-K tails on CTA pairs: off in the tile table unless METALBLAS_PAIR_SK=1
+// (measured on the B200 they lost to the table's other plans on most shapes
+// the cost model would give them: 1024x1024x8192 467 vs 541 TFLOP/s,
+// 2048x2048x8192 1035 vs 1337; the fix-up of a piece's partials is exposed).
+// stream_k = 2 with cta_pair = 2 still requests one.
 const bool g_pair_sk = [] {
   const char *s = getenv("METALBLAS_PAIR_SK");
-  return !(s && s[0] == '0');
+  return s && s[0] == '1';
 }();
 // 512-wide CTA-pair tiles in the tile table (METALBLAS_PAIR_WIDE=0 leaves
 // them out; tile_n = 512 still requests one).
