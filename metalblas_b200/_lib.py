@@ -162,6 +162,38 @@ def load():
         return lib
 
 
+_fast = None
+_fast_tried = False
+
+
+def fast():
+    """The host fast path (csrc/fastpath.cpp, built in tree as _mbfast*.so) with
+    this library's mb_gemm registered, or None when it is not built.  Without
+    it every call takes the Python path; the products are the same."""
+    global _fast, _fast_tried
+    if _fast_tried:
+        return _fast
+    lib = load()  # before taking the lock: load() takes it too
+    with _lock:
+        if _fast_tried:
+            return _fast
+        import importlib.util
+        import sysconfig
+        path = os.path.join(_PKG, "_mbfast" + sysconfig.get_config_var("EXT_SUFFIX"))
+        mod = None
+        if os.path.exists(path):
+            spec = importlib.util.spec_from_file_location("_mbfast", path)
+            mod = importlib.util.module_from_spec(spec)
+            spec.loader.exec_module(mod)
+            if mod.desc_size() != ctypes.sizeof(GemmDesc):
+                raise RuntimeError("_mbfast was built against a different mb_gemm_desc; rebuild the package")
+            fn = ctypes.cast(lib.mb_gemm, ctypes.c_void_p).value
+            mod.set_gemm(fn)
+        _fast = mod
+        _fast_tried = True
+        return _fast
+
+
 def last_error() -> str:
     return load().mb_last_error_string().decode(errors="replace")
 

@@ -1,7 +1,8 @@
 """Build the sm_100a shared library in-tree (nvcc, no JIT cache).
 
 The library is one CUDA translation unit (``csrc/mb_abi.cu``) exporting the C ABI
-declared in ``include/metalblas_b200.h``.  It links the CUDA runtime statically
+declared in ``include/metalblas_b200.h``; a small torch C++ extension
+(``csrc/fastpath.cpp``) holds the per-thread descriptor cache of repeated calls.  It links the CUDA runtime statically
 so it does not depend on which libcudart torch happened to load, and reaches the
 driver (for cuTensorMapEncodeTiled) through cudaGetDriverEntryPoint, so it needs
 no libcuda at link time.
@@ -63,12 +64,52 @@ def build(force: bool = False, verbose: bool = False) -> str:
     return LIB
 
 
+FAST_SRC = os.path.join(PKG_DIR, "csrc", "fastpath.cpp")
+
+
+def fast_lib_path() -> str:
+    import sysconfig
+    return os.path.join(PKG_DIR, "_mbfast" + sysconfig.get_config_var("EXT_SUFFIX"))
+
+
+def build_fastpath(force: bool = False, verbose: bool = False) -> str:
+    """Compile the host fast path (csrc/fastpath.cpp, a torch C++ extension) in
+    tree with g++: torch's headers and libraries, no CUDA device code."""
+    import sysconfig
+
+    import torch
+    import torch.utils.cpp_extension as ce
+    out = fast_lib_path()
+    srcs = [FAST_SRC, os.path.join(REPO, "include", "metalblas_b200.h"), __file__]
+    if not force and os.path.exists(out) and all(os.path.getmtime(s) <= os.path.getmtime(out) for s in srcs):
+        return out
+    cuda_home = os.environ.get("CUDA_HOME", "/usr/local/cuda")
+    cmd = ["g++", "-O3", "-std=c++17", "-shared", "-fPIC", "-w",
+           f"-D_GLIBCXX_USE_CXX11_ABI={int(torch._C._GLIBCXX_USE_CXX11_ABI)}",
+           "-DTORCH_EXTENSION_NAME=_mbfast", "-DTORCH_API_INCLUDE_EXTENSION_H",
+           "-I", sysconfig.get_paths()["include"], "-I", os.path.join(cuda_home, "include"),
+           "-I", os.path.join(REPO, "include")]
+    for inc in ce.include_paths():
+        cmd += ["-I", inc]
+    for lib in ce.library_paths():
+        cmd += ["-L", lib, f"-Wl,-rpath,{lib}"]
+    cmd += [FAST_SRC, "-o", out + ".tmp", "-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu", "-ltorch_python"]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError("g++ failed:\n" + " ".join(cmd) + "\n" + res.stdout + res.stderr)
+    if verbose:
+        sys.stderr.write(res.stdout + res.stderr)
+    os.replace(out + ".tmp", out)
+    return out
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--force", action="store_true")
     ap.add_argument("--verbose", action="store_true", help="pass -Xptxas -v (registers, spills)")
     a = ap.parse_args()
     print(build(force=a.force, verbose=a.verbose))
+    print(build_fastpath(force=a.force, verbose=a.verbose))
 
 
 if __name__ == "__main__":

@@ -127,6 +127,9 @@ def reset_caches() -> None:
     _WS.clear()
     _GEN[0] += 1
     _fast_cache().clear()
+    fast = _lib.fast()
+    if fast is not None:
+        fast.clear()
 
 
 try:
@@ -230,7 +233,21 @@ def _launch(A, B, C, M, N, K, batch, a3, b3, c3, *, epilogue=None, backend=_lib.
         if len(cache) >= _FAST_MAX:
             cache.clear()
         cache[key] = (d, ws)
+        _TLS.last = (d, ws)
     return C
+
+
+def _remember(kind, a, b, c):
+    """Hand the descriptor the last _launch cached to the host fast path, keyed
+    on the caller's own tensors (it serves only operands used as they are)."""
+    last = getattr(_TLS, "last", None)
+    if last is None:
+        return
+    _TLS.last = None
+    fast = _lib.fast()
+    if fast is not None:
+        d, ws = last
+        fast.remember(kind, a, b, c, ctypes.addressof(d), ws)
 
 
 def _fill_desc(A, B, C, M, N, K, batch, a3, b3, c3, epilogue, backend, tile_n, split_k):
@@ -314,6 +331,10 @@ def _parse_tile(backend, tile):
     return 0, 0
 
 
+# The host fast path for repeated plain calls (csrc/fastpath.cpp), or None.
+_FAST = _lib.fast()
+
+
 # --------------------------------------------------------------------------- ops
 def _complex_inputs(a, b):
     """Promote the real operand to the complex dtype (metalblas/complex_dispatch.py:25-30)."""
@@ -349,10 +370,14 @@ def _mm2d(a, b, out, epilogue=None, backend=None, tile=None, peers=None):
     be = _BACKENDS[backend]
     if backend in ("mpp", "mpp_tensor") and dtype not in TC_DTYPES:
         be = _lib.MB_BACKEND_SIMT
-    return _launch(A, B, out, M, N, K, 1,
-                   (A.stride(0), A.stride(1), 0), (B.stride(0), B.stride(1), 0),
-                   (out.stride(0), out.stride(1), 0),
-                   epilogue=epilogue, backend=be, tile_n=tile_n, split_k=split_k, peers=peers)
+    _TLS.last = None
+    _launch(A, B, out, M, N, K, 1,
+            (A.stride(0), A.stride(1), 0), (B.stride(0), B.stride(1), 0),
+            (out.stride(0), out.stride(1), 0),
+            epilogue=epilogue, backend=be, tile_n=tile_n, split_k=split_k, peers=peers)
+    if epilogue is None and be == _lib.MB_BACKEND_AUTO and peers is None and A is a and B is b:
+        _remember(0, a, b, out)
+    return out
 
 
 def _flat3(t, size, rows, cols):
@@ -424,6 +449,13 @@ def matmul(a: torch.Tensor, b: torch.Tensor, *, backend: str | None = None,
     (CUDA-core FFMA/IMAD kernel).  swizzle_log is accepted for compatibility;
     rasterisation is done by the persistent tile scheduler.
     """
+    if backend is None and tile is None and _FAST is not None:
+        if out is None:
+            c = _FAST.try_mm_new(a, b)
+            if c is not None:
+                return c
+        elif _FAST.try_mm(a, b, out):
+            return out
     if swizzle_log is not None:
         assert int(swizzle_log) >= 0, "swizzle_log must be >= 0"
     if a.ndim != 2 or b.ndim != 2:
@@ -473,13 +505,24 @@ def _bmm(a, b, out, epilogue=None, peers=None):
         return out
     A = _plain(_matrix_view(a, M, K))
     B = _plain(_matrix_view(b, K, N))
-    return _launch(A, B, out, M, N, K, Bb,
-                   (A.stride(1), A.stride(2), A.stride(0)), (B.stride(1), B.stride(2), B.stride(0)),
-                   (out.stride(1), out.stride(2), out.stride(0)), epilogue=epilogue, peers=peers)
+    _TLS.last = None
+    _launch(A, B, out, M, N, K, Bb,
+            (A.stride(1), A.stride(2), A.stride(0)), (B.stride(1), B.stride(2), B.stride(0)),
+            (out.stride(1), out.stride(2), out.stride(0)), epilogue=epilogue, peers=peers)
+    if epilogue is None and peers is None and A is a and B is b:
+        _remember(1, a, b, out)
+    return out
 
 
 def bmm(a: torch.Tensor, b: torch.Tensor, *, out: torch.Tensor | None = None) -> torch.Tensor:
     """Batched 3-D product; a batch stride of 0 broadcasts (metalblas/dispatch.py:211-225)."""
+    if _FAST is not None:
+        if out is None:
+            c = _FAST.try_bmm_new(a, b)
+            if c is not None:
+                return c
+        elif _FAST.try_bmm(a, b, out):
+            return out
     return _bmm(a, b, out)
 
 

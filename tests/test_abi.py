@@ -69,3 +69,12 @@ def test_status_codes_map_to_reference_exceptions():
     with pytest.raises(RuntimeError):
         _lib.raise_for(_lib.MB_ERR_DEVICE_TIMEOUT)
     _lib.raise_for(_lib.MB_OK)
+
+
+def test_fast_path_extension_matches_the_descriptor_layout(lib):
+    """The host fast path (csrc/fastpath.cpp) is built in tree and was compiled
+    against this header's mb_gemm_desc."""
+    from metalblas_b200 import _lib as L
+    fast = L.fast()
+    assert fast is not None, "the _mbfast extension is not built"
+    assert fast.desc_size() == ctypes.sizeof(L.GemmDesc)
