@@ -429,7 +429,7 @@ void choose_tc_tile_uncached(const Op &o, int sms, int force_bn, int force_split
       // stream-K tail on pairs: whole 256-row tiles for the full waves, the
       // tiles left over cut into equal K-block ranges, one per pair (each CTA
       // of a pair publishes and reduces its own 128 rows)
-      if (have_ws && g_pair_sk && force_sk != 1 && !force_split && !s3 && ptiles % pairs) {
+      if (have_ws && (g_pair_sk || force_sk == 2) && force_sk != 1 && !force_split && !s3 && ptiles % pairs) {
         const int64_t dp = (ptiles / pairs) * pairs;
         const int64_t tail = ptiles - dp;
         const int64_t iters = tail * kb_total;

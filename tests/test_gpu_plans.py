@@ -116,6 +116,24 @@ def test_stream_k_many_parts_and_repeat():
     assert kernels.device_status() == 0
 
 
+def _plan(a, b, **ov):
+    """The plan mb_gemm runs for a @ b on the tensor-core backend with these
+    overrides (forced variants must really run, not fall back to CUDA cores)."""
+    M, K = a.shape
+    N = b.shape[1]
+    d = _lib.new_desc()
+    d.dtype, d.backend = _lib.DTYPE_CODE[a.dtype], _lib.MB_BACKEND_TC
+    d.M, d.N, d.K = M, N, K
+    d.A, d.B, d.C = a.data_ptr(), b.data_ptr(), a.data_ptr()
+    d.a_rs, d.a_cs = a.stride()
+    d.b_rs, d.b_cs = b.stride()
+    d.c_rs, d.c_cs = N, 1
+    for k, v in ov.items():
+        setattr(d, k, v)
+    d.workspace_bytes = -1
+    return _lib.plan_query(d)
+
+
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.int8], ids=NAME.get)
 def test_pair_stream_k(dtype):
     """Stream-K tails on CTA pairs: the BASELINE config-1 shape (64 256-row tiles
@@ -130,6 +148,8 @@ def test_pair_stream_k(dtype):
         a = rand((M, K), dtype, gen, full_range=full)
         b = rand((K, N), dtype, gen, full_range=full)
         ref = orc.product(to_np(a), to_np(b), NAME[dtype])
+        plan = _plan(a, b, tile_n=bn, cta_pair=2, stream_k=2, swap_ab=-1)
+        assert "pair=2 sk=1" in plan, plan
         for _ in range(2):
             c = _run(a, b, bn, 0, -1, pair=2, sk=2)
             assert c is not None
@@ -164,6 +184,8 @@ def test_pair_wide_tile(dtype):
         a = rand((M, K), dtype, gen, full_range=full)
         for b in (rand((K, N), dtype, gen, full_range=full), rand((N, K), dtype, gen, full_range=full).t()):
             ref = orc.product(to_np(a), to_np(b), NAME[dtype])
+            plan = _plan(a, b, tile_n=512, cta_pair=2, split_k=1, swap_ab=-1)
+            assert "bn=512" in plan and "pair=2" in plan, plan
             c = _run(a, b, 512, 1, -1, pair=2)
             assert c is not None
             ok, err = orc.check(to_np(c), ref, NAME[dtype])
