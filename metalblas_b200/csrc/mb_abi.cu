@@ -1821,6 +1821,16 @@ int mb_gemm_peer(const mb_gemm_desc *d, const mb_peer_targets *peers, void *stre
   if (pl.kind != PK_TC)
     return fail(MB_ERR_UNSUPPORTED, "peer replication runs on the tensor-core plan only (bf16/fp16/int8/uint8 "
                                     "operands TMA can address); this product plans as kind %d", pl.kind);
+  if (pl.bn > 256 && d->tile_n == 0) {
+    // The 512-wide tile has one accumulator, so its epilogue (and with it the
+    // peer stores) is exposed at each tile's end; the 256-wide tiles hide the
+    // epilogue and its peer stores behind the next tile's mainloop.
+    mb_gemm_desc q = *d;
+    q.tile_n = 256;
+    pl = Plan{};
+    rc = plan_for(&q, pl, o, sms);
+    if (rc) return rc;
+  }
   if (pl.ws_bytes > 0 && (d->workspace == nullptr || d->workspace_bytes < pl.ws_bytes))
     return fail(MB_ERR_WORKSPACE, "workspace of %lld bytes required", (long long)pl.ws_bytes);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
