@@ -136,6 +136,14 @@ class ClockSampler:
                 "power_w_max": max((num(r[2]) or 0.0) for r in rows)}
 
 
+def _host_cores() -> int:
+    """CPU cores this process may run on (its affinity mask), else os.cpu_count()."""
+    try:
+        return max(1, len(os.sched_getaffinity(0)))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
 def _dist():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -329,7 +337,7 @@ def run_ours(args, w, rank, world, device):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         from oracle import cpu_baseline as cb
-        torch.set_num_threads(os.cpu_count() or 1)
+        torch.set_num_threads(_host_cores())
         rows = cb.calibrate_rows(a_h, b_h, 2.0)
         reps = 5
         sec, rows = cb.time_rows(a_h, b_h, rows, reps)
@@ -566,8 +574,9 @@ def run_reference(args, w, rank, world):
     from oracle import cpu_baseline as cb
     M, N, K, dt = w["M"], w["N"], w["K"], w["dtype"]
     # torch.distributed.run sets OMP_NUM_THREADS=1 for every rank; the
-    # reference's CPU path runs on rank 0 alone, with every host core
-    torch.set_num_threads(os.cpu_count() or 1)
+    # reference's CPU path runs on rank 0 alone, with every core this process
+    # may run on
+    torch.set_num_threads(_host_cores())
     a, b = _inputs(w, 0, 1)
     budget = 90.0  # seconds for the whole run
     per_step = budget / max(1, args.steps + args.warmup)
