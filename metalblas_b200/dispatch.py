@@ -184,6 +184,7 @@ def _launch(A, B, C, M, N, K, batch, a3, b3, c3, *, epilogue=None, backend=_lib.
         if ekey is not None:
             d.bias = pbias or None
         if _lib._lib.mb_gemm(_byref(d), _c_void_p(stream)) == _lib.MB_OK:
+            _TLS.last = hit  # (re-)register with the host fast path
             return C
         cache.pop(key, None)  # rerun through the full path, which raises the error
 
