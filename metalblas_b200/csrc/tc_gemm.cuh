@@ -778,6 +778,49 @@ __device__ __forceinline__ void pack32(const TcParams &p, int b, int m, int n0, 
   for (int j = 0; j < 32 * (int)sizeof(T) / 4; ++j) pk[j] = reinterpret_cast<const uint32_t *>(out)[j];
 }
 
+// Peer copies of two consecutive staged boxes (the previous box `stg_a`, then
+// `stg_b`, CC columns each, adjacent in C): each row is one 128-byte run, so
+// lane l moves chunk l & 7 of rows l / 8, l / 8 + 4, ...: a warp-wide store
+// writes four whole 128-byte lines (the single-box copy writes 64-byte halves,
+// twice the store requests per byte, and remote stores are bound by requests).
+template <class T>
+__device__ __forceinline__ void peer_store_box2(const TcParams &p, uint32_t stg_a, uint32_t stg_b, int lane, int b,
+                                                int row0, int col0) {
+  constexpr int EPC = 16 / (int)sizeof(T);   // elements per 16-byte chunk
+  const int rr = lane >> 3, ch = lane & 7;
+  const int n = col0 + ch * EPC;
+  if (n >= p.N) return;
+  const uint32_t buf = ch < 4 ? stg_a : stg_b;
+  uint4 v[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int r = i * 4 + rr;
+    const uint32_t addr = buf + (uint32_t)(r * STAGING_ROW) + ((uint32_t)((ch & 3) ^ ((r >> 1) & 3)) << 4);
+    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v[i].x), "=r"(v[i].y), "=r"(v[i].z), "=r"(v[i].w)
+                 : "r"(addr));
+  }
+  const bool whole = n + EPC <= p.N;
+#pragma unroll 1
+  for (int pi = 0; pi < p.npeers; ++pi) {
+    T *C = (T *)p.peer_C[pi] + (int64_t)b * p.sC;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int m = row0 + i * 4 + rr;
+      if (m >= p.M) break;
+      T *dst = C + (int64_t)m * p.c_rs + n;
+      if (whole) {
+        *reinterpret_cast<uint4 *>(dst) = v[i];
+      } else {
+        const T *e = reinterpret_cast<const T *>(&v[i]);
+#pragma unroll
+        for (int j = 0; j < EPC; ++j)
+          if (n + j < p.N) dst[j] = e[j];
+      }
+    }
+  }
+}
+
 // Partial-sum slot of piece s of tail tile `tail` for CTA `rank` of its pair:
 // slots are BM x BN 4-byte values, ordered (tail, piece, rank).  A CTA pair
 // shares a 256-row tile, and each CTA publishes and reduces its own 128 rows.
@@ -1204,7 +1247,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
                   tma_store_3d(&p.tmC, stg, n0 - (SUBS - 1) * 32, m0 + q * 32, w.b);
                   bulk_commit();
                 }
-                if constexpr (PEER) peer_store_box<T>(p, stg, lane, w.b, m0 + q * 32, n0 - (SUBS - 1) * 32);
+                if constexpr (PEER) {
+                  // boxes in pairs (adjacent columns in the two staging
+                  // buffers) as 128-byte rows; an unpaired last box alone
+                  const int bx = sc / SUBS, nbox = nsub / SUBS;
+                  const int bcol0 = n0 - (SUBS - 1) * 32;
+                  if (bx & 1)
+                    peer_store_box2<T>(p, stg0 + (uint32_t)((sbuf ^ 1) * STAGING_BUF), stg, lane, w.b, m0 + q * 32,
+                                       bcol0 - CC);
+                  else if (bx == nbox - 1)
+                    peer_store_box<T>(p, stg, lane, w.b, m0 + q * 32, bcol0);
+                }
                 sbuf ^= 1;
               }
             }
