@@ -178,6 +178,11 @@ int mb_gemm_noalloc(const mb_gemm_desc *d, void *stream);
 typedef struct mb_peer_targets {
     int32_t count;                 /* peers that receive the output (0..MB_MAX_PEERS) */
     void *C[MB_MAX_PEERS];         /* each peer's copy of C, same strides as desc->C */
+    void *mc_C;                    /* NULL, or the NVSwitch multicast address of C (every
+                                    * rank's copy, this one included, bound to one multicast
+                                    * object): whole 16-byte chunks are then written once
+                                    * with multimem.st and the switch replicates them;
+                                    * partial chunks still use C[] */
 } mb_peer_targets;
 int mb_gemm_peer(const mb_gemm_desc *d, const mb_peer_targets *peers, void *stream);
 

@@ -71,11 +71,12 @@ class GemmDesc(ctypes.Structure):
 class PeerTargets(ctypes.Structure):
     """Mirror of ``mb_peer_targets``."""
 
-    _fields_ = [("count", ctypes.c_int32), ("C", ctypes.c_void_p * MB_MAX_PEERS)]
+    _fields_ = [("count", ctypes.c_int32), ("C", ctypes.c_void_p * MB_MAX_PEERS), ("mc_C", ctypes.c_void_p)]
 
 
-def peer_targets(addrs) -> PeerTargets:
-    """An mb_peer_targets holding the given device addresses."""
+def peer_targets(addrs, mc=None) -> PeerTargets:
+    """An mb_peer_targets holding the given device addresses (and the
+    multicast address of C, if any)."""
     addrs = list(addrs)
     if len(addrs) > MB_MAX_PEERS:
         raise ValueError(f"at most {MB_MAX_PEERS} peers, got {len(addrs)}")
@@ -83,6 +84,7 @@ def peer_targets(addrs) -> PeerTargets:
     t.count = len(addrs)
     for i, a in enumerate(addrs):
         t.C[i] = int(a)
+    t.mc_C = int(mc) if mc else None
     return t
 
 

@@ -1350,6 +1350,7 @@ int launch_tc_bn(const Op &o, const Plan &pl, const EpiScalars &e, void *ws, int
   if constexpr (PEER) {
     p.npeers = peers->count;
     for (int i = 0; i < peers->count; ++i) p.peer_C[i] = peers->C[i];
+    p.mc_C = peers->mc_C;
   }
   auto kern = tc::tc_gemm_kernel<T, BN, PAIR, TO, PEER>;
   static int attr_done[64] = {0};
@@ -1814,6 +1815,8 @@ int mb_gemm_peer(const mb_gemm_desc *d, const mb_peer_targets *peers, void *stre
     return fail(MB_ERR_INVALID, "peer count %d outside 0..%d", peers->count, MB_MAX_PEERS);
   for (int i = 0; i < peers->count; ++i)
     if (!peers->C[i]) return fail(MB_ERR_INVALID, "null peer output %d", i);
+  if (peers->mc_C && (reinterpret_cast<uintptr_t>(peers->mc_C) & 15) != (reinterpret_cast<uintptr_t>(d->C) & 15))
+    return fail(MB_ERR_INVALID, "multicast address of C must have C's 16-byte alignment");
   Plan pl; Op o; int sms;
   int rc = plan_for(d, pl, o, sms);
   if (rc) return rc;

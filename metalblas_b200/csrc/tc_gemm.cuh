@@ -98,7 +98,19 @@ struct TcParams {
   // this process).  Loads and tensor maps only ever touch this GPU's memory.
   int npeers;
   void *peer_C[kMaxPeers];
+  // NVSwitch multicast address of C (all ranks' copies at once), or null.
+  // When set, whole 16-byte chunks go to every peer with one multimem.st
+  // through it (the switch replicates the write); partial chunks still take
+  // the per-peer stores.
+  void *mc_C;
 };
+
+// One 16-byte store to every GPU bound to the multicast address `mc`.
+__device__ __forceinline__ void multimem_st16(void *mc, const uint4 &v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
+}
 
 template <int BN, int ESZ, int PAIR = 1>
 struct Cfg {
@@ -684,8 +696,16 @@ __device__ __forceinline__ void store_row_chunk(const TcParams &p, int b, int m,
   }
   put_row_chunk<T, NC>(p, (T *)p.C, b, m, n0, out);
   if constexpr (PEER) {
+    constexpr int PER16 = 16 / sizeof(T);
+    if (p.mc_C && NC % PER16 == 0 && p.c_vec && n0 + NC <= p.N) {
+      T *dst = (T *)p.mc_C + (int64_t)b * p.sC + (int64_t)m * p.c_rs + n0;
+#pragma unroll
+      for (int v = 0; v < NC / PER16; ++v)
+        multimem_st16(dst + v * PER16, *reinterpret_cast<const uint4 *>(&out[v * PER16]));
+    } else {
 #pragma unroll 1
-    for (int i = 0; i < p.npeers; ++i) put_row_chunk<T, NC>(p, (T *)p.peer_C[i], b, m, n0, out);
+      for (int i = 0; i < p.npeers; ++i) put_row_chunk<T, NC>(p, (T *)p.peer_C[i], b, m, n0, out);
+    }
   }
 }
 
@@ -710,6 +730,15 @@ __device__ __forceinline__ void peer_store_box(const TcParams &p, uint32_t stg, 
                  : "r"(addr));
   }
   const bool whole = n + EPC <= p.N;
+  if (whole && p.mc_C) {
+    T *C = (T *)p.mc_C + (int64_t)b * p.sC;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int m = row0 + i * 8 + rr;
+      if (m < p.M) multimem_st16(C + (int64_t)m * p.c_rs + n, v[i]);
+    }
+    return;
+  }
 #pragma unroll 1
   for (int pi = 0; pi < p.npeers; ++pi) {
     T *C = (T *)p.peer_C[pi] + (int64_t)b * p.sC;
@@ -801,6 +830,15 @@ __device__ __forceinline__ void peer_store_box2(const TcParams &p, uint32_t stg_
                  : "r"(addr));
   }
   const bool whole = n + EPC <= p.N;
+  if (whole && p.mc_C) {
+    T *C = (T *)p.mc_C + (int64_t)b * p.sC;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int m = row0 + i * 4 + rr;
+      if (m < p.M) multimem_st16(C + (int64_t)m * p.c_rs + n, v[i]);
+    }
+    return;
+  }
 #pragma unroll 1
   for (int pi = 0; pi < p.npeers; ++pi) {
     T *C = (T *)p.peer_C[pi] + (int64_t)b * p.sC;
@@ -1301,8 +1339,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
       if (++abuf == C_::NACC) { abuf = 0; aphase ^= 1u; }
     }
     if (lane == 0) bulk_wait0();  // every TMA store of this warp has completed
-    // peer stores are performed system-wide before the CTA retires
-    if constexpr (PEER) __threadfence_system();
+    // peer and multicast stores are performed system-wide before the CTA
+    // retires (the alias fence orders the multicast-address stores with later
+    // accesses through the unicast addresses of the same memory)
+    if constexpr (PEER) {
+      asm volatile("fence.proxy.alias;" ::: "memory");
+      __threadfence_system();
+    }
     __syncwarp();
   }
 

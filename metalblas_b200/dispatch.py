@@ -150,8 +150,9 @@ def _launch(A, B, C, M, N, K, batch, a3, b3, c3, *, epilogue=None, backend=_lib.
 
     a3/b3/c3 are (row stride, col stride, batch stride) in elements.
     epilogue: (bias, (rs, cs, bs), beta, alpha, beta_nz, alpha_nz) or None.
-    peers: device addresses of other GPUs' copies of C (same strides): the call
-    goes to mb_gemm_peer, which also stores every output element there.
+    peers: (device addresses of other GPUs' copies of C (same strides), the
+    multicast address of C or 0): the call goes to mb_gemm_peer, which also
+    stores every output element there.
     """
     dev = C.device
     if torch.cuda.current_device() != dev.index:
@@ -288,7 +289,8 @@ def _launch_peer(A, B, C, M, N, K, batch, a3, b3, c3, epilogue, backend, tile_n,
     if nbytes > 0:
         ws = _workspace(dev, stream, nbytes)
         d.workspace, d.workspace_bytes = ws.data_ptr(), ws.numel()
-    targets = _lib.peer_targets(peers)
+    addrs, mc = peers
+    targets = _lib.peer_targets(addrs, mc)
     _lib.raise_for(lib.mb_gemm_peer(ctypes.byref(d), ctypes.byref(targets), ctypes.c_void_p(stream)),
                    "mb_gemm_peer")
     return C

@@ -11,9 +11,15 @@ into every other rank's address space with CUDA IPC (``mb_ipc_get_handle`` /
 ``mb_ipc_open``), and a stream-ordered :func:`barrier` after which every rank's
 peer stores of the step have landed.
 
-No NVLink multicast object is created (a rank that dies while its memory is
-bound to one can fault the other ranks' GPUs); the mappings are plain peer
-mappings, closed by :meth:`PeerBuffer.close` or at process exit.
+Where every rank's GPU supports NVSwitch multicast, the buffer is instead
+torch's symmetric memory bound to one multicast object (``multicast_ptr``):
+the kernel then writes each finished tile once through the multicast address
+(``multimem.st``) and the switch replicates it to every GPU, so each GPU sends
+its output once instead of once per peer.  ``METALBLAS_NVLS=0`` keeps the plain
+CUDA-IPC peer mappings.  A rank that dies while its memory is bound to a
+multicast object can fault the other ranks' GPUs, so the owners release the
+buffers (:func:`release_arenas`) before leaving the process group, on error
+paths too.
 
 Reuse rule: a step writes into every rank's buffer, so a step must not start
 writing a slot that a peer may still be reading.  :class:`PeerBuffer` keeps two
@@ -26,6 +32,7 @@ the same buffer.
 from __future__ import annotations
 
 import ctypes
+import os
 
 import torch
 import torch.distributed as dist
@@ -82,6 +89,25 @@ def exchange(payload: torch.Tensor, group, device) -> list[torch.Tensor]:
     return [out[r * _PAYLOAD:(r + 1) * _PAYLOAD] for r in range(world)]
 
 
+def _multicast_wanted() -> bool:
+    return os.environ.get("METALBLAS_NVLS", "1") != "0"
+
+
+def _agree_all(flag: bool, group, device) -> bool:
+    """True when `flag` holds on every rank (one MIN all-reduce)."""
+    t = torch.tensor([1 if flag else 0], dtype=torch.int32, device=_comm_device(group, device))
+    dist.all_reduce(t, op=dist.ReduceOp.MIN, group=group)
+    return bool(int(t.item()))
+
+
+def _multicast_supported(device) -> bool:
+    try:
+        S = torch._C._distributed_c10d._SymmetricMemory
+        return bool(S.has_multicast_support(torch._C._autograd.DeviceType.CUDA, torch.device(device).index))
+    except (AttributeError, RuntimeError, TypeError):
+        return False
+
+
 class PeerBuffer:
     """One device buffer of ``nslots`` slots of ``nbytes`` per rank, with every
     other rank's buffer mapped into this process.
@@ -99,10 +125,18 @@ class PeerBuffer:
         self.device = torch.device(device)
         self.slot = slot_bytes(nbytes)
         self.nslots = int(nslots)
-        self.local = torch.empty(self.slot * self.nslots, dtype=torch.uint8, device=self.device)
         self._turn = 0
         self._bases: list[int] = []
         self._base_addr = [0] * self.world
+        self._symm = None
+        self.mc_base = 0   # multicast address of this buffer's first byte, 0 without one
+        if self.world > 1 and _multicast_wanted() and self.world - 1 <= _lib.MB_MAX_PEERS:
+            # every rank must take the same branch: symmetric memory is collective
+            if _agree_all(_multicast_supported(self.device), group, self.device):
+                self._init_multicast(group)
+        if self._symm is not None:
+            return
+        self.local = torch.empty(self.slot * self.nslots, dtype=torch.uint8, device=self.device)
         self._base_addr[self.rank] = self.local.data_ptr()
         if self.world > 1:
             lib = _lib.load()
@@ -122,6 +156,23 @@ class PeerBuffer:
                     _lib.raise_for(lib.mb_ipc_open(hbuf, ctypes.byref(base)), "mb_ipc_open")
                     self._bases.append(base.value)
                     self._base_addr[r] = base.value + o
+
+    def _init_multicast(self, group) -> None:
+        import torch.distributed._symmetric_memory as symm_mem
+        t = symm_mem.empty(self.slot * self.nslots, dtype=torch.uint8, device=self.device)
+        hdl = symm_mem.rendezvous(t, group if group is not None else dist.group.WORLD)
+        ptrs = list(hdl.buffer_ptrs)
+        off = t.data_ptr() - int(ptrs[self.rank])
+        mc = int(hdl.multicast_ptr)
+        if not _agree_all(mc != 0 and off % 16 == 0, group, self.device):
+            return   # plain IPC mappings instead (every rank agrees)
+        self.local, self._symm = t, hdl
+        self._base_addr = [int(q) + off for q in ptrs]
+        self.mc_base = mc + off
+
+    def mc_addr(self, slot: int, byte_offset: int = 0) -> int:
+        """Multicast address of this rank's slot (+ byte_offset), or 0."""
+        return self.mc_base + slot * self.slot + byte_offset if self.mc_base else 0
 
     def next_slot(self) -> int:
         """The slot the next step should write (alternates)."""
@@ -146,8 +197,15 @@ class PeerBuffer:
         return self.local[slot * self.slot: slot * self.slot + n * esz].view(dtype).view(*shape)
 
     def close(self) -> None:
-        """Unmap the peers' buffers (collective: barrier first so no rank still
-        writes into a buffer whose owner frees it afterwards)."""
+        """Unmap the peers' buffers, or release the multicast-bound symmetric
+        memory (callers barrier first so no rank still writes into a buffer
+        whose owner frees it afterwards)."""
+        if self._symm is not None:
+            torch.cuda.synchronize(self.device)
+            self._symm = None
+            self.local = None
+            self.mc_base = 0
+            return
         if not self._bases:
             return
         lib = _lib.load()

@@ -138,7 +138,8 @@ def sharded_bmm(a: torch.Tensor, b: torch.Tensor, *, group=None, gather: bool = 
             slot = buf.next_slot()
             out = buf.view(slot, a.dtype, (bsz, M, N))
             if e > s:
-                _bmm(a[s:e], bb[s:e], out[s:e], peers=buf.peer_addrs(slot, s * M * N * esz))
+                off = s * M * N * esz
+                _bmm(a[s:e], bb[s:e], out[s:e], peers=(buf.peer_addrs(slot, off), buf.mc_addr(slot, off)))
             _peer.barrier(group, a.device)
             return out
     mm = local_bmm or _default_bmm
@@ -187,7 +188,7 @@ def sharded_matmul_n(a: torch.Tensor, b_block: torch.Tensor, n_total: int, *, gr
             slot = buf.next_slot()
             out = buf.view(slot, a.dtype, (M, n_total))
             if e > s:
-                _mm2d(a, b_block, out[:, s:e], peers=buf.peer_addrs(slot, s * esz))
+                _mm2d(a, b_block, out[:, s:e], peers=(buf.peer_addrs(slot, s * esz), buf.mc_addr(slot, s * esz)))
             _peer.barrier(group, a.device)
             return out
     local = (local_mm or _default_mm)(a, b_block)

@@ -7,8 +7,11 @@ store path of the kernel: whole tiles staged for TMA stores (peer copies of
 the staged boxes), split-K / stream-K finishes and direct stores at a column
 offset that is not 16-byte aligned (peer copies from registers), for bf16,
 fp16 and int8 (bit-exact); two calls in a row exercise both slots of the peer
-buffer.  The NCCL gather (fused=False) and the K-sharded all-reduce are
-checked too.  NVLS is off (no multicast objects)."""
+buffer.  The fused cases run twice: with the NVSwitch multicast buffer
+(multimem.st, where the GPUs support it) and with plain CUDA-IPC peer
+mappings (METALBLAS_NVLS=0).  The NCCL gather (fused=False) and the K-sharded
+all-reduce are checked too.  NCCL's own NVLS is off; the peer buffers are
+released on every exit path before the process group is destroyed."""
 from __future__ import annotations
 
 import os
@@ -40,8 +43,9 @@ def _worker(rank, world, port, results):
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
                             device_id=dev)
     out = {}
+    from metalblas_b200 import peer
     try:
-        from metalblas_b200 import peer, shard
+        from metalblas_b200 import shard
         from oracle import oracle as orc
 
         def host(t):
@@ -72,22 +76,34 @@ def _worker(rank, world, port, results):
                 ok = ok and C.shape == (M, n_total) and check(C, A, B, name)
             return ok
 
-        # whole tiles, TMA-staged epilogue (CTA-pair 256-wide tiles), two calls in a row
-        out["mm_n_bf16_tiles"] = mm_n("bfloat16", 2048, 4096, 2048, torch.bfloat16, calls=2)
-        # split-K finishes; rank 1's block starts at column 500 (1000 bytes: direct stores)
-        out["mm_n_bf16_ragged_split"] = mm_n("bfloat16", 512, 1000, 1024, torch.bfloat16)
-        # stream-K tail on a skinny block
-        out["mm_n_bf16_skinny_sk"] = mm_n("bfloat16", 128, 2048, 16384, torch.bfloat16)
-        out["mm_n_fp16_tiles"] = mm_n("float16", 2048, 4096, 1024, torch.float16)
-        out["mm_n_int8_exact"] = mm_n("int8", 1024, 1024, 2048, torch.int8)
+        def fused_cases(tag):
+            # whole tiles, TMA-staged epilogue (CTA-pair 256-wide tiles), two calls in a row
+            out[f"{tag}mm_n_bf16_tiles"] = mm_n("bfloat16", 2048, 4096, 2048, torch.bfloat16, calls=2)
+            # split-K finishes; rank 1's block starts at column 500 (1000 bytes: direct stores)
+            out[f"{tag}mm_n_bf16_ragged_split"] = mm_n("bfloat16", 512, 1000, 1024, torch.bfloat16)
+            # stream-K tail on a skinny block
+            out[f"{tag}mm_n_bf16_skinny_sk"] = mm_n("bfloat16", 128, 2048, 16384, torch.bfloat16)
+            out[f"{tag}mm_n_fp16_tiles"] = mm_n("float16", 2048, 4096, 1024, torch.float16)
+            out[f"{tag}mm_n_int8_exact"] = mm_n("int8", 1024, 1024, 2048, torch.int8)
+            a = rnd(7, 384, 256)
+            b = rnd(7, 256, 320)
+            c = shard.sharded_bmm(a.to(dev), b.to(dev), gather=True)
+            out[f"{tag}bmm_fused"] = check(c, a, b, "bfloat16")
+
+        fused_cases("")
+        multicast = any(buf.mc_base for buf in peer._ARENAS.values())
+        # the same with plain CUDA-IPC peer mappings
+        torch.cuda.synchronize()
+        peer.release_arenas()
+        os.environ["METALBLAS_NVLS"] = "0"
+        fused_cases("ipc_")
+        os.environ.pop("METALBLAS_NVLS")
         # the unfused NCCL gather
         out["mm_n_bf16_nccl"] = mm_n("bfloat16", 512, 1000, 1024, torch.bfloat16, fused=False)
 
-        # batch-sharded bmm, ragged batch (7 over 2), fused and NCCL
+        # batch-sharded bmm, ragged batch (7 over 2), NCCL
         a = rnd(7, 384, 256)
         b = rnd(7, 256, 320)
-        c = shard.sharded_bmm(a.to(dev), b.to(dev), gather=True)
-        out["bmm_fused"] = check(c, a, b, "bfloat16")
         c = shard.sharded_bmm(a.to(dev), b.to(dev), gather=True, fused=False)
         out["bmm_nccl"] = check(c, a, b, "bfloat16")
         a8, b8 = rnd(8, 384, 256), rnd(8, 256, 320)
@@ -100,9 +116,11 @@ def _worker(rank, world, port, results):
         Ck = shard.sharded_matmul_k(A[:, s:e].contiguous().to(dev), B[s:e].contiguous().to(dev))
         out["mm_k"] = check(Ck, A, B, "bfloat16")
         torch.cuda.synchronize()
-        peer.release_arenas()
         results[rank] = out
+        results[f"multicast{rank}"] = multicast
     finally:
+        torch.cuda.synchronize()
+        peer.release_arenas()
         dist.destroy_process_group()
 
 
@@ -121,6 +139,7 @@ def test_sharded_products_two_gpus():
             p.kill()
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     res = dict(results)
+    print("multicast buffers:", res.pop("multicast0", None), res.pop("multicast1", None))
     assert set(res) == {0, 1}, res
     for r in (0, 1):
         bad = [k for k, v in res[r].items() if not v]
