@@ -273,7 +273,7 @@ def run_ours(args, w, rank, world, device):
         gathered = {"value": flops * world / (gms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": gms,
                     "layout": f"row-major C [{M}, {n_total}] on every rank",
                     "collective": "fused: tcgen05 epilogue stores each tile into every rank's C over NVLink "
-                                  "(mb_gemm_peer), then one barrier", "check": chk}
+                                  "(mb_gemm_peer), then one barrier", "peer_stores": _peer_mode(), "check": chk}
         nms = _timed(lambda i: shard.sharded_matmul_n(As[i % SETS], Bs[i % SETS], n_total, gather=True,
                                                       fused=False), args.steps, world, device)
         gathered_nccl = {"value": flops * world / (nms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": nms,
@@ -404,7 +404,7 @@ def run_bmm_sharded(args, rank, world, device):
         out["gathered"] = {"value": flops / (gms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": gms,
                            "collective": "fused: each rank's bmm epilogue stores its slab into every rank's "
                                          "[256,1024,1024] output over NVLink (mb_gemm_peer), then one barrier",
-                           "check": chk}
+                           "peer_stores": _peer_mode(), "check": chk}
         nms = _timed(lambda i: shard.sharded_bmm(As[i % 2], Bs[i % 2], gather=True, chunks=4, fused=False),
                      steps, world, device)
         out["gathered_nccl"] = {"value": flops / (nms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": nms,
@@ -446,7 +446,7 @@ def run_large_nshard(args, rank, world, device):
                        "layout": "row-major C [16384, 16384] on every rank",
                        "collective": ("fused: tcgen05 epilogue stores each tile into every rank's C over "
                                       "NVLink (mb_gemm_peer), then one barrier") if world > 1 else "none (1 GPU)",
-                       "check": chk}
+                       "peer_stores": _peer_mode(), "check": chk}
     del A, B, C
     return out
 
@@ -494,13 +494,25 @@ def run_skinny(args, rank, world, device):
     out["n_sharded"] = {"value": byts / (ms * 1e-3) / 1e9, "ms_per_step": ms,
                         "tflops": flops / (ms * 1e-3) / 1e12,
                         "collective": "fused gather (mb_gemm_peer) + barrier" if world > 1 else "none (1 GPU)",
-                        "check": cn}
+                        "peer_stores": _peer_mode(), "check": cn}
     out["k_sharded"] = {"value": byts / (kms * 1e-3) / 1e9, "ms_per_step": kms,
                         "tflops": flops / (kms * 1e-3) / 1e12,
                         "collective": "NCCL all_reduce of fp32 partials" if world > 1 else "none (1 GPU)",
                         "check": ck}
     del A, B
     return out
+
+
+def _peer_mode():
+    """How the fused gather's peer stores travelled: through the NVSwitch
+    multicast buffer or plain CUDA-IPC peer mappings ("none" at one rank)."""
+    from metalblas_b200 import peer
+    bufs = list(peer._ARENAS.values())
+    if not bufs:
+        return "none"
+    if any(b.mc_base for b in bufs):
+        return "multicast: one multimem.st per 16 bytes, replicated by NVSwitch"
+    return "CUDA-IPC: one st.global per peer per 16 bytes"
 
 
 def _timed(fn, steps, world, device, warm=3):

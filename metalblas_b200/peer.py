@@ -15,11 +15,12 @@ Where every rank's GPU supports NVSwitch multicast, the buffer is instead
 torch's symmetric memory bound to one multicast object (``multicast_ptr``):
 the kernel then writes each finished tile once through the multicast address
 (``multimem.st``) and the switch replicates it to every GPU, so each GPU sends
-its output once instead of once per peer.  ``METALBLAS_NVLS=0`` keeps the plain
-CUDA-IPC peer mappings.  A rank that dies while its memory is bound to a
-multicast object can fault the other ranks' GPUs, so the owners release the
-buffers (:func:`release_arenas`) before leaving the process group, on error
-paths too.
+its output once instead of once per peer.  That is the default from four
+ranks on (``MULTICAST_MIN_WORLD``); ``METALBLAS_NVLS=1`` forces it at any size
+and ``METALBLAS_NVLS=0`` keeps the plain CUDA-IPC peer mappings.  A rank that
+dies while its memory is bound to a multicast object can fault the other
+ranks' GPUs, so the owners release the buffers (:func:`release_arenas`) before
+leaving the process group, on error paths too.
 
 Reuse rule: a step writes into every rank's buffer, so a step must not start
 writing a slot that a peer may still be reading.  :class:`PeerBuffer` keeps two
@@ -89,8 +90,21 @@ def exchange(payload: torch.Tensor, group, device) -> list[torch.Tensor]:
     return [out[r * _PAYLOAD:(r + 1) * _PAYLOAD] for r in range(world)]
 
 
-def _multicast_wanted() -> bool:
-    return os.environ.get("METALBLAS_NVLS", "1") != "0"
+# Smallest world that takes the multicast buffer by default.  A multimem store
+# reaches every member, the writer's own GPU included, so each GPU receives
+# the whole output (N/N) instead of the peers' share ((N-1)/N): at two GPUs that
+# doubles the inbound bytes for no saving, while from four GPUs on each GPU
+# sends its share once instead of N-1 times.
+MULTICAST_MIN_WORLD = 4
+
+
+def _multicast_wanted(world: int) -> bool:
+    """METALBLAS_NVLS=1 forces the multicast buffer, 0 disables it; unset, it
+    is used from MULTICAST_MIN_WORLD ranks on."""
+    v = os.environ.get("METALBLAS_NVLS", "")
+    if v in ("0", "1"):
+        return v == "1"
+    return world >= MULTICAST_MIN_WORLD
 
 
 def _agree_all(flag: bool, group, device) -> bool:
@@ -130,7 +144,7 @@ class PeerBuffer:
         self._base_addr = [0] * self.world
         self._symm = None
         self.mc_base = 0   # multicast address of this buffer's first byte, 0 without one
-        if self.world > 1 and _multicast_wanted() and self.world - 1 <= _lib.MB_MAX_PEERS:
+        if self.world > 1 and _multicast_wanted(self.world) and self.world - 1 <= _lib.MB_MAX_PEERS:
             # every rank must take the same branch: symmetric memory is collective
             if _agree_all(_multicast_supported(self.device), group, self.device):
                 self._init_multicast(group)

@@ -9,7 +9,7 @@ offset that is not 16-byte aligned (peer copies from registers), for bf16,
 fp16 and int8 (bit-exact); two calls in a row exercise both slots of the peer
 buffer.  The fused cases run twice: with the NVSwitch multicast buffer
 (multimem.st, where the GPUs support it) and with plain CUDA-IPC peer
-mappings (METALBLAS_NVLS=0).  The NCCL gather (fused=False) and the K-sharded
+mappings (METALBLAS_NVLS=0; the default at two ranks).  The NCCL gather (fused=False) and the K-sharded
 all-reduce are checked too.  NCCL's own NVLS is off; the peer buffers are
 released on every exit path before the process group is destroyed."""
 from __future__ import annotations
@@ -90,6 +90,7 @@ def _worker(rank, world, port, results):
             c = shard.sharded_bmm(a.to(dev), b.to(dev), gather=True)
             out[f"{tag}bmm_fused"] = check(c, a, b, "bfloat16")
 
+        os.environ["METALBLAS_NVLS"] = "1"   # multicast buffer, forced at two ranks
         fused_cases("")
         multicast = any(buf.mc_base for buf in peer._ARENAS.values())
         # the same with plain CUDA-IPC peer mappings
