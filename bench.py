@@ -1095,16 +1095,22 @@ ONE_CASES = {
     "gemv_bf16_1x4096x4096": ("gemm", torch.bfloat16, 1, 4096, 4096, None),
     "gemv_bf16_1x4096x4096_wt": ("gemm", torch.bfloat16, 1, 4096, 4096, "wt"),
     "gemv_bf16_16x4096x4096": ("gemm", torch.bfloat16, 16, 4096, 4096, None),
+    # the CUDA-core kernels (backend="simd": FFMA for fp32, IMAD for int32)
+    "simt_fp32_gemm_2048": ("gemm", torch.float32, 2048, 2048, 2048, None, "simd"),
+    "simt_int32_gemm_2048": ("gemm", torch.int32, 2048, 2048, 2048, None, "simd"),
 }
 
 
 def run_one(args):
     import metalblas_b200 as mb
-    kind, dt, M, N, K, lay = ONE_CASES[args.one]
+    kind, dt, M, N, K, lay, backend = (ONE_CASES[args.one] + (None,))[:7]
+    kw = {"backend": backend} if backend else {}
     dev = torch.device("cuda", 0)
     g = torch.Generator(device=dev).manual_seed(0)
 
     def rnd(*shape):
+        if not dt.is_floating_point and not dt.is_complex:
+            return torch.randint(-1000, 1000, shape, generator=g, device=dev, dtype=dt)
         if dt.is_complex:
             return torch.complex(torch.randn(*shape, generator=g, device=dev),
                                  torch.randn(*shape, generator=g, device=dev)).to(dt)
@@ -1115,18 +1121,18 @@ def run_one(args):
     B = [(rnd(N, K).t() if lay == "wt" else rnd(K, N)) for _ in range(sets)]
     C = [torch.empty(M, N, dtype=dt, device=dev) for _ in range(sets)]
     for i in range(max(args.warmup, 3)):
-        mb.matmul(A[i % sets], B[i % sets], out=C[i % sets])
+        mb.matmul(A[i % sets], B[i % sets], out=C[i % sets], **kw)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for i in range(args.steps):
-        mb.matmul(A[i % sets], B[i % sets], out=C[i % sets])
+        mb.matmul(A[i % sets], B[i % sets], out=C[i % sets], **kw)
     e1.record()
     e1.synchronize()
     ms = e0.elapsed_time(e1) / args.steps
     flops = (8.0 if dt.is_complex else 2.0) * M * N * K
     print(json.dumps({"one": args.one, "ms": ms, "tflops": flops / (ms * 1e-3) / 1e12,
-                      "gbs": byts / (ms * 1e-3) / 1e9, "plan": mb.kernels.plan(A[0], B[0]),
+                      "gbs": byts / (ms * 1e-3) / 1e9, "plan": mb.kernels.plan(A[0], B[0], **kw),
                       "l2": f"{sets} rotating input sets"}), flush=True)
 
 
