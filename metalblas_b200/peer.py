@@ -172,16 +172,29 @@ class PeerBuffer:
                     self._base_addr[r] = base.value + o
 
     def _init_multicast(self, group) -> None:
+        """Symmetric memory bound to a multicast object, or nothing (the
+        caller then maps plain IPC buffers).  Each step that can fail on one
+        rank alone is followed by an agreement, so every rank takes the same
+        branch and no rank waits in a collective the others have left."""
         import torch.distributed._symmetric_memory as symm_mem
-        t = symm_mem.empty(self.slot * self.nslots, dtype=torch.uint8, device=self.device)
-        hdl = symm_mem.rendezvous(t, group if group is not None else dist.group.WORLD)
-        ptrs = list(hdl.buffer_ptrs)
-        off = t.data_ptr() - int(ptrs[self.rank])
-        mc = int(hdl.multicast_ptr)
-        if not _agree_all(mc != 0 and off % 16 == 0, group, self.device):
+        try:
+            t = symm_mem.empty(self.slot * self.nslots, dtype=torch.uint8, device=self.device)
+        except (RuntimeError, ValueError):
+            t = None
+        if not _agree_all(t is not None, group, self.device):
+            return
+        try:
+            hdl = symm_mem.rendezvous(t, group if group is not None else dist.group.WORLD)
+            ptrs = [int(q) for q in hdl.buffer_ptrs]
+            off = t.data_ptr() - ptrs[self.rank]
+            mc = int(hdl.multicast_ptr)
+            ok = mc != 0 and off % 16 == 0
+        except (RuntimeError, ValueError):
+            ok = False
+        if not _agree_all(ok, group, self.device):
             return   # plain IPC mappings instead (every rank agrees)
         self.local, self._symm = t, hdl
-        self._base_addr = [int(q) + off for q in ptrs]
+        self._base_addr = [q + off for q in ptrs]
         self.mc_base = mc + off
 
     def mc_addr(self, slot: int, byte_offset: int = 0) -> int:

@@ -125,6 +125,83 @@ def test_peer_exchange_world2_gloo():
     assert dict(results) == {0: (True, True), 1: (True, True)}
 
 
+def _multicast_worker(rank, world, port, results):
+    """peer.PeerBuffer._init_multicast over gloo with torch's symmetric-memory
+    calls replaced by fakes: a failure on one rank alone (allocation, or no
+    multicast address) must send every rank to the IPC fallback, and success
+    must give each rank the same multicast base."""
+    import types
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        import torch.distributed._symmetric_memory as symm_mem
+        from metalblas_b200 import peer
+        mode = {}
+
+        def fake_empty(n, dtype=None, device=None):
+            if mode["fail_alloc_rank"] == rank:
+                raise RuntimeError("no symmetric memory here")
+            return torch.empty(n, dtype=dtype)
+
+        def fake_rendezvous(t, group):
+            ptrs = [0x10000000 * (r + 1) for r in range(world)]
+            ptrs[rank] = t.data_ptr()
+            mc = 0 if mode["no_mc_rank"] == rank else 0x7000000000
+            return types.SimpleNamespace(buffer_ptrs=ptrs, multicast_ptr=mc)
+
+        symm_mem.empty, symm_mem.rendezvous = fake_empty, fake_rendezvous
+
+        def attempt(fail_alloc_rank, no_mc_rank):
+            mode.update(fail_alloc_rank=fail_alloc_rank, no_mc_rank=no_mc_rank)
+            buf = object.__new__(peer.PeerBuffer)
+            buf.slot, buf.nslots, buf.device = 4096, 2, torch.device("cpu")
+            buf.world, buf.rank = world, rank
+            buf._symm, buf.local, buf.mc_base = None, None, 0
+            buf._base_addr = [0] * world
+            buf._init_multicast(None)
+            return buf
+
+        b1 = attempt(fail_alloc_rank=1, no_mc_rank=-1)
+        ok_alloc = b1._symm is None and b1.mc_base == 0 and b1.mc_addr(1) == 0
+        b2 = attempt(fail_alloc_rank=-1, no_mc_rank=0)
+        ok_nomc = b2._symm is None and b2.mc_base == 0
+        b3 = attempt(fail_alloc_rank=-1, no_mc_rank=-1)
+        ok_mc = (b3._symm is not None and b3.mc_base == 0x7000000000 and
+                 b3.mc_addr(1, 32) == 0x7000000000 + 4096 + 32 and
+                 b3.addr(0, rank) == b3.local.data_ptr())
+        results[rank] = (ok_alloc, ok_nomc, ok_mc)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_multicast_setup_falls_back_together_world2_gloo():
+    ctx = mp.get_context("spawn")
+    results = ctx.Manager().dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_multicast_worker, args=(r, 2, port, results)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    assert dict(results) == {0: (True, True, True), 1: (True, True, True)}
+
+
+def test_multicast_policy(monkeypatch):
+    from metalblas_b200 import peer
+    monkeypatch.delenv("METALBLAS_NVLS", raising=False)
+    assert not peer._multicast_wanted(2) and not peer._multicast_wanted(3)
+    assert peer._multicast_wanted(peer.MULTICAST_MIN_WORLD) and peer._multicast_wanted(8)
+    monkeypatch.setenv("METALBLAS_NVLS", "1")
+    assert peer._multicast_wanted(2)
+    monkeypatch.setenv("METALBLAS_NVLS", "0")
+    assert not peer._multicast_wanted(8)
+
+
 def test_peer_payload_and_slots():
     from metalblas_b200 import peer
     h = bytes(range(64))
