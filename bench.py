@@ -273,7 +273,8 @@ def run_ours(args, w, rank, world, device):
         gathered = {"value": flops * world / (gms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": gms,
                     "layout": f"row-major C [{M}, {n_total}] on every rank",
                     "collective": "fused: tcgen05 epilogue stores each tile into every rank's C over NVLink "
-                                  "(mb_gemm_peer), then one barrier", "peer_stores": _peer_mode(), "check": chk}
+                                  "(mb_gemm_peer), then one barrier", "peer_stores": _peer_mode(),
+                    "roofline": _fused_roofline(flops, M * n_total * As[0].element_size(), world, gms), "check": chk}
         nms = _timed(lambda i: shard.sharded_matmul_n(As[i % SETS], Bs[i % SETS], n_total, gather=True,
                                                       fused=False), args.steps, world, device)
         gathered_nccl = {"value": flops * world / (nms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": nms,
@@ -404,7 +405,8 @@ def run_bmm_sharded(args, rank, world, device):
         out["gathered"] = {"value": flops / (gms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": gms,
                            "collective": "fused: each rank's bmm epilogue stores its slab into every rank's "
                                          "[256,1024,1024] output over NVLink (mb_gemm_peer), then one barrier",
-                           "peer_stores": _peer_mode(), "check": chk}
+                           "peer_stores": _peer_mode(),
+                           "roofline": _fused_roofline(flops / world, Bt * M * N * 2, world, gms), "check": chk}
         nms = _timed(lambda i: shard.sharded_bmm(As[i % 2], Bs[i % 2], gather=True, chunks=4, fused=False),
                      steps, world, device)
         out["gathered_nccl"] = {"value": flops / (nms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": nms,
@@ -446,7 +448,8 @@ def run_large_nshard(args, rank, world, device):
                        "layout": "row-major C [16384, 16384] on every rank",
                        "collective": ("fused: tcgen05 epilogue stores each tile into every rank's C over "
                                       "NVLink (mb_gemm_peer), then one barrier") if world > 1 else "none (1 GPU)",
-                       "peer_stores": _peer_mode(), "check": chk}
+                       "peer_stores": _peer_mode(),
+                       "roofline": _fused_roofline(flops / world, Mx * Nx * 2, world, gms), "check": chk}
     del A, B, C
     return out
 
@@ -501,6 +504,24 @@ def run_skinny(args, rank, world, device):
                         "check": ck}
     del A, B
     return out
+
+
+# Measured NVLink peer-copy rate per direction per GPU on this pool (GB/s).
+NVLINK_GBS = 770.0
+
+
+def _fused_roofline(flops_per_rank, out_bytes, world, ms):
+    """Roofline of a product fused with its output gather: the target time is
+    the slower of the rank's math at the dense bf16 peak and the bytes each GPU
+    must receive over NVLink, (N-1)/N of the gathered output, at the measured
+    peer-copy rate; frac = target / measured step time."""
+    peak, _, src = _peaks()
+    t_math = flops_per_rank / (peak * 1e12)
+    t_link = (world - 1) / world * out_bytes / (NVLINK_GBS * 1e9)
+    target = max(t_math, t_link)
+    return {"bound": "tensor" if t_math >= t_link else "nvlink", "target_ms": target * 1e3,
+            "math_ms": t_math * 1e3, "link_ms": t_link * 1e3, "peak_tflops": peak, "peak_source": src,
+            "nvlink_gbs": NVLINK_GBS, "frac": target / (ms * 1e-3)}
 
 
 def _peer_mode():
