@@ -1123,6 +1123,13 @@ EpiScalars make_epi(const mb_gemm_desc *d) {
 // Programmatic dependent launch for the GEMV and tcgen05 kernels (see
 // pdl_trigger / pdl_wait in mb_common.cuh); METALBLAS_PDL=0 launches them
 // with plain stream order.
+// Split-K of thin tiles reduced inside a thread-block cluster (rank 0's shared
+// memory) instead of through the workspace (METALBLAS_CLUSTER_SPLIT=0: off).
+const bool g_csplit = [] {
+  const char *s = getenv("METALBLAS_CLUSTER_SPLIT");
+  return !(s && s[0] == '0');
+}();
+
 const bool g_pdl = [] {
   const char *s = getenv("METALBLAS_PDL");
   return !(s && s[0] == '0');
@@ -1365,7 +1372,39 @@ int launch_tc_bn(const Op &o, const Plan &pl, const EpiScalars &e, void *ws, int
   if constexpr (PAIR == 1) {
     // stream-K ranges are cut for exactly sk_ctas CTAs
     const int grid = pl.sk ? (int)pl.sk_ctas : (int)std::min<int64_t>(units, sms);
-    return launch_pdl(kern, dim3(grid), dim3(tc::NUM_THREADS), C_::SMEM_BYTES, st, 1, "tc_gemm launch", p);
+    int cx = 1;
+    if constexpr (C_::RED_BYTES > 0 && !PEER && std::is_same_v<T, TO>) {
+      // Cluster split-K: one unit per CTA, the `splits` units of a tile in one
+      // cluster (units are numbered tile-major, so CTA u holds split u % splits),
+      // and every cluster resident at once (rank 0 waits for its peers).
+      static int max_clusters[64][C_::CSPLIT_MAX + 1] = {};
+      if (g_csplit && !pl.sk && !pl.tail_half && pl.dp_tiles == 0 && pl.splits >= 2 &&
+          pl.splits <= C_::CSPLIT_MAX && units <= sms && units % pl.splits == 0 && dev >= 0 && dev < 64) {
+        int &slot = max_clusters[dev][pl.splits];
+        if (slot == 0) {
+          cudaLaunchConfig_t cfg = {};
+          cfg.gridDim = dim3(pl.splits);
+          cfg.blockDim = dim3(tc::NUM_THREADS);
+          cfg.dynamicSmemBytes = C_::SMEM_BYTES;
+          cudaLaunchAttribute a[1];
+          a[0].id = cudaLaunchAttributeClusterDimension;
+          a[0].val.clusterDim.x = pl.splits;
+          a[0].val.clusterDim.y = 1;
+          a[0].val.clusterDim.z = 1;
+          cfg.attrs = a;
+          cfg.numAttrs = 1;
+          int n = 0;
+          if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+            (void)cudaGetLastError();
+            n = 0;
+          }
+          slot = n + 1;
+        }
+        if ((int64_t)(slot - 1) >= units / pl.splits) cx = pl.splits;
+      }
+    }
+    p.csplit = cx > 1 ? 1 : 0;
+    return launch_pdl(kern, dim3(grid), dim3(tc::NUM_THREADS), C_::SMEM_BYTES, st, cx, "tc_gemm launch", p);
   } else {
     // one cluster (CTA pair) per unit slot; the pair shares each 256-row tile
     // (stream-K ranges are cut for exactly sk_ctas / 2 pairs)

@@ -92,6 +92,11 @@ struct TcParams {
   int sk;                // tail tiles partitioned stream-K (splits = partial slots per tile)
   long long sk_iters;    // tail tiles * kb_total: the K-block iterations shared out
   unsigned long long timeout_ns;
+  // Cluster split-K: the grid is one unit per CTA, every tile split `splits`
+  // ways along K, and the CTAs of a cluster (cluster rank = split index) share
+  // one tile: ranks 1.. store their partials into rank 0's shared memory
+  // instead of the workspace, and rank 0 sums them in K order.
+  int csplit;
   // Peer replication (kernels instantiated with PEER = true): every output
   // element is also stored, with plain st.global over NVLink, at the same
   // element offset from each peer_C[i] (another GPU's copy of C, mapped into
@@ -135,7 +140,11 @@ struct Cfg {
   static constexpr bool TMA_STORE = ESZ <= 2 && (QUART % CC) == 0;  // fp32 outputs: direct stores
   static constexpr int STAGING_BYTES = TMA_STORE ? NUM_EPI_WARPS * STAGING_PER_WARP : 0;
   static constexpr int BAR_BYTES = 256;
-  static constexpr int STAGES_RAW = (SMEM_LIMIT - 1024 - STAGING_BYTES - BAR_BYTES) / STAGE_BYTES;
+  // Cluster split-K (thin tiles): rank 0 of a cluster receives the raw
+  // partials of ranks 1 .. CSPLIT_MAX-1 here, one BM x BN 4-byte slot each.
+  static constexpr int CSPLIT_MAX = 4;
+  static constexpr int RED_BYTES = (BN <= 32 && PAIR == 1 && ESZ <= 2) ? (CSPLIT_MAX - 1) * BM * BN * 4 : 0;
+  static constexpr int STAGES_RAW = (SMEM_LIMIT - 1024 - STAGING_BYTES - RED_BYTES - BAR_BYTES) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
   // The 512-wide CTA-pair tile issues two N = 256 MMAs per K-step (tile
   // columns [0, 256) and [256, 512)); its accumulator fills all 512 TMEM
@@ -146,14 +155,14 @@ struct Cfg {
   static constexpr int ACC_COLS = BN;           // fp32/s32: one column per N
   static constexpr int TMEM_COLS = (NACC * BN <= 32) ? 32 : (NACC * BN <= 64) ? 64 : (NACC * BN <= 128) ? 128
                                  : (NACC * BN <= 256) ? 256 : 512;
-  static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + STAGING_BYTES + BAR_BYTES;
+  static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + STAGING_BYTES + RED_BYTES + BAR_BYTES;
   // columns per tcgen05.ld on the direct-store and split-K paths (16 for 16- and
   // 32-bit outputs keeps the epilogue within the register budget of 320 threads)
   static constexpr int RCH = QUART < (ESZ >= 2 ? 16 : 32) ? (QUART < 8 ? 8 : QUART) : (ESZ >= 2 ? 16 : 32);
   static_assert(BN % 16 == 0 && BN >= 16 && (BN <= 256 || (BN == 512 && PAIR == 2 && ESZ <= 2)), "UMMA N");
   static_assert(STAGES >= 2, "need a pipeline");
   static_assert(SMEM_BYTES <= SMEM_LIMIT, "shared memory");
-  static_assert(3 * STAGES + 5 <= BAR_BYTES / 8 - 2, "barrier area");
+  static_assert(2 * STAGES + 6 + 1 <= BAR_BYTES / 8, "barrier area");
 };
 
 // ---------------------------------------------------------------------------
@@ -327,6 +336,17 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity,
       }
     }
   }
+}
+// 16-byte store to shared memory of another CTA of the cluster (a mapa address).
+__device__ __forceinline__ void st_cluster_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared::cluster.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d)
+               : "memory");
+}
+__device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr)
+               : "memory");
+  return v;
 }
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
@@ -951,9 +971,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t *ring = smem;
   uint8_t *staging = ring + STAGES * STAGE_BYTES;
-  uint64_t *bars = reinterpret_cast<uint64_t *>(staging + C_::STAGING_BYTES);
-  // bars: full[STAGES], empty[STAGES], tfull[2], tempty[2], drain
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 5);
+  uint8_t *red = staging + C_::STAGING_BYTES;   // cluster split-K partials (rank 0)
+  uint64_t *bars = reinterpret_cast<uint64_t *>(red + C_::RED_BYTES);
+  // bars: full[STAGES], empty[STAGES], tfull[2], tempty[2], drain, red
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 6);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -964,6 +985,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
   auto tfull_bar = [&](int a) { return bar_u32 + 8u * (2 * STAGES + a); };
   auto tempty_bar = [&](int a) { return bar_u32 + 8u * (2 * STAGES + 2 + a); };
   const uint32_t drain_bar = bar_u32 + 8u * (2 * STAGES + 4);
+  const uint32_t red_bar = bar_u32 + 8u * (2 * STAGES + 5);
+  const uint32_t red_u32 = smem_u32(red);
   const uint32_t rank = PAIR == 2 ? cluster_rank() : 0u;
   // the pair leader's full barrier of stage s, as a cluster address
   auto leader_full = [&](int s) { return mapa_shared(full_bar(s), 0); };
@@ -989,6 +1012,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
       mbar_init(tempty_bar(a), NUM_EPI_WARPS * PAIR);
     }
     mbar_init(drain_bar, 1);
+    // cluster split-K: every lane of every epilogue warp of ranks 1.. arrives once
+    if (p.csplit) mbar_init(red_bar, NUM_EPI_WARPS * 32 * (p.splits - 1));
     *abort_flag = 0;
     fence_mbar_init();
     prefetch_tmap(&p.tmA);
@@ -1002,6 +1027,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
   tc_fence_before();
   __syncthreads();
   if constexpr (PAIR == 2) cluster_sync_all();  // peer barriers initialised before any remote arrive
+  if constexpr (PAIR == 1 && C_::RED_BYTES > 0) {
+    if (p.csplit) cluster_sync_all();  // rank 0's reduction barrier initialised before any remote arrive
+  }
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   pdl_wait();
@@ -1314,6 +1342,63 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) tc_gemm_kernel(const __grid_co
         tc_fence_before();
         __syncwarp();
         if (lane == 0) release_tmem(abuf);
+      } else if (C_::RED_BYTES > 0 && p.csplit) {
+        // Cluster split-K: the same lane-interleaved runs as the workspace
+        // partials below, in rank 0's shared memory (slot s - 1 for split s).
+        // Ranks 1.. store theirs and arrive on rank 0's reduction barrier
+        // (release, cluster scope: each lane orders its own stores); rank 0
+        // waits for all of them, adds them to its own accumulator in K order
+        // and stores the tile.
+        const uint32_t slot_bytes = (uint32_t)(BM * BN * 4);
+        const uint32_t off0 = (uint32_t)(ew * 32 * wcols * 4) + (uint32_t)lane * 16u;
+        if (w.s > 0) {
+          const uint32_t rbase = mapa_shared(red_u32 + (uint32_t)(w.s - 1) * slot_bytes + off0, 0);
+#pragma unroll 1
+          for (int c = 0; c < wcols; c += RCHO) {
+            uint32_t r[32];
+            tmem_ld<RCHO>(tbase + c, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < RCHO; j += 4)
+              st_cluster_v4(rbase + (uint32_t)((c + j) >> 2) * 512u, r[j], r[j + 1], r[j + 2], r[j + 3]);
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) release_tmem(abuf);
+          mbar_arrive_cluster(mapa_shared(red_bar, 0));
+        } else {
+          const bool got = mbar_wait_cluster(red_bar, 0, abort_flag, p.timeout_ns);
+          if (got) {
+#pragma unroll 1
+            for (int c = 0; c < wcols; c += RCHO) {
+              uint32_t r[32];
+              tmem_ld<RCHO>(tbase + c, r);
+              tmem_wait_ld();
+#pragma unroll 1
+              for (int s2 = 1; s2 < w.nparts; ++s2) {
+                const uint32_t lb = red_u32 + (uint32_t)(s2 - 1) * slot_bytes + off0 + (uint32_t)(c >> 2) * 512u;
+#pragma unroll
+                for (int j = 0; j < RCHO; j += 4) {
+                  const uint4 v = ld_shared_v4(lb + (uint32_t)(j >> 2) * 512u);
+                  if constexpr (Elem<T>::is_int) {
+                    r[j] += v.x; r[j + 1] += v.y; r[j + 2] += v.z; r[j + 3] += v.w;
+                  } else {
+                    r[j] = __float_as_uint(__uint_as_float(r[j]) + __uint_as_float(v.x));
+                    r[j + 1] = __float_as_uint(__uint_as_float(r[j + 1]) + __uint_as_float(v.y));
+                    r[j + 2] = __float_as_uint(__uint_as_float(r[j + 2]) + __uint_as_float(v.z));
+                    r[j + 3] = __float_as_uint(__uint_as_float(r[j + 3]) + __uint_as_float(v.w));
+                  }
+                }
+              }
+              const int n0 = nbase + c;
+              if (m < p.M && n0 < p.N) store_row_chunk<TO, RCHO, PEER>(p, w.b, m, n0, r);
+            }
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) release_tmem(abuf);
+          if (!got) break;
+        }
       } else {
         // Split-K: publish raw accumulators.  Slot (tail, s) holds BM x BN
         // 4-byte values; warp ew's 32 rows x wcols columns are stored as
