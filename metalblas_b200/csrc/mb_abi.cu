@@ -1375,8 +1375,11 @@ int launch_tc_bn(const Op &o, const Plan &pl, const EpiScalars &e, void *ws, int
     int cx = 1;
     if constexpr (C_::RED_BYTES > 0 && !PEER && std::is_same_v<T, TO>) {
       // Cluster split-K: one unit per CTA, the `splits` units of a tile in one
-      // cluster (units are numbered tile-major, so CTA u holds split u % splits),
-      // and every cluster resident at once (rank 0 waits for its peers).
+      // cluster (units are numbered tile-major, so CTA u holds split u % splits).
+      // The CTAs of a cluster are scheduled together, so rank 0 never waits for
+      // a peer that cannot start; the occupancy check keeps the one-wave
+      // schedule the planner costed (a GPC that cannot hold a whole cluster
+      // would push some clusters into a second wave).
       static int max_clusters[64][C_::CSPLIT_MAX + 1] = {};
       if (g_csplit && !pl.sk && !pl.tail_half && pl.dp_tiles == 0 && pl.splits >= 2 &&
           pl.splits <= C_::CSPLIT_MAX && units <= sms && units % pl.splits == 0 && dev >= 0 && dev < 64) {
