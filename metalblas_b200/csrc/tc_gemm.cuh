@@ -37,7 +37,10 @@
 //    the warp that draws the last ticket.  Every CTA does the same number of
 //    K-blocks, whatever the tile count.
 // Partials are stored lane-interleaved (a warp's 32 rows of 4 columns form one
-// 512-byte run) so both the writes and the reduction are coalesced.
+// 512-byte run) so both the writes and the reduction are coalesced.  Thin tiles
+// (BN <= 32) whose splits all fit in one wave run each tile's splits on the
+// CTAs of one thread-block cluster instead (TcParams::csplit): the partials
+// then travel through rank 0's shared memory, not the workspace.
 //
 // Operand layouts: each operand may be K-major or MN-major in global memory;
 // TMA copies it into the matching canonical SWIZZLE_128B layout and the UMMA
